@@ -1,0 +1,419 @@
+"""Benchmark of the B200 routed-expert MoE layer.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload decode|prefill] [--tokens T]
+
+One step = one MoE layer forward (gate -> route plan -> permute/quant ->
+grouped GEMM1 -> grouped GEMM2 -> combine) over one batch of synthetic tokens,
+inputs resident in HBM.  The default workload is the single-GPU decode layer
+(H=4096, 256 routed experts top-6 + 1 shared, I=2048, FP4 routed / FP8 shared,
+64 tokens, uniform routing).  The L2 cache (126 MB) is flushed between timed
+steps by writing a 256 MB buffer outside the timed events.
+
+Prints one JSON line (rank 0).  ``--impl reference`` times the CPU oracle
+restatement of the reference's layer on the host cores instead (the
+reference's own MoE math is the absent official model; its only native code,
+the packed loader, is not on this layer's compute path).
+
+With torchrun (N > 1) every rank runs the same layer on its own tokens with
+its own copy of the experts (independent replicas, weak scaling); the time is
+the max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "deepseek-v4-flash-dgx-spark_b200"))
+sys.path.insert(0, str(REPO))
+
+METRIC = "moe_layer_tokens_per_s"
+UNIT = "tokens/s"
+
+
+def _parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--workload", default="decode", choices=["decode", "prefill"])
+    p.add_argument("--tokens", type=int, default=None)
+    p.add_argument("--no-sweep", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--seed", type=int, default=0)
+    return p.parse_args()
+
+
+def _dist_init(n):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _peaks():
+    try:
+        return json.loads((REPO / "MEASURED_PEAKS.json").read_text()), "measured"
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def _traffic_record(workload: str):
+    """ncu DRAM traffic per GEMM launch, committed under profiles/ (null if absent)."""
+    try:
+        data = json.loads((REPO / "profiles" / "traffic.json").read_text())
+        return data.get(workload)
+    except (OSError, ValueError):
+        return None
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args, world, rank, local):
+    import torch
+    import torch.distributed as dist
+
+    from spark_b200 import _lib
+    from spark_b200.synthetic import (CONFIGS, algorithmic_decode_bytes, algorithmic_flops, build_moe,
+                                      make_layer)
+
+    dev = torch.device("cuda", local)
+    base = CONFIGS[args.workload]
+    T = args.tokens or (64 if args.workload == "decode" else base.tokens)
+    cfg = base.with_tokens(T)
+    layer = make_layer(cfg, seed=args.seed + 1000 * rank, device=dev)
+    moe = build_moe(layer, device=dev)
+    x = layer["x"]
+    lib = _lib.load()
+    ws = torch.empty(moe.workspace_bytes(T), dtype=torch.uint8, device=dev)
+    y = torch.empty_like(x)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    def step():
+        moe.forward_tokens(x, workspace=ws, out=y)
+
+    # warm-up, then capture the layer in a CUDA graph (launch-bound at decode sizes)
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    _lib.raise_on_device_error()
+    lib.dsv4_profile_enable(1)
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()  # profiling events exist before capture
+    torch.cuda.current_stream().wait_stream(s)
+    with torch.cuda.graph(graph, stream=s):
+        step()
+    graph.replay()
+    torch.cuda.synchronize()
+
+    # touched experts of this batch (for the algorithmic-bytes count)
+    offs = (__import__("ctypes").c_longlong * 17)()
+    d = moe.layer_desc()
+    lib.dsv4_moe_workspace_layout(__import__("ctypes").byref(d), T, offs, 17)
+    counts = ws[offs[3]:offs[3] + (cfg.n_routed + 1) * 4].view(torch.int32)[: cfg.n_routed]
+    touched = int((counts > 0).sum())
+    rows = int(counts.sum()) + T
+
+    # timed region
+    stage = torch.zeros(6, dtype=torch.float64)
+    buf = (__import__("ctypes").c_float * 6)()
+    times = []
+    clocks = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    for _ in range(args.steps):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+        lib.dsv4_profile_read(buf, 6)
+        stage += torch.tensor(list(buf), dtype=torch.float64)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    lib.dsv4_profile_enable(0)
+    _lib.raise_on_device_error()
+    ms = sum(times) / len(times)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    stage_ms = (stage / args.steps).tolist()
+
+    # end to end through the C ABI with host buffers (pinned), copies inside the timed region
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty_like(x_host).pin_memory()
+    x_dev = torch.empty_like(x)
+    e2e = []
+    for i in range(args.warmup + args.steps):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        x_dev.copy_(x_host, non_blocking=True)
+        moe.forward_tokens(x_dev, workspace=ws, out=y)
+        y_host.copy_(y, non_blocking=True)
+        e1.record()
+        e1.synchronize()
+        if i >= args.warmup:
+            e2e.append(e0.elapsed_time(e1))
+    e2e_ms = sum(e2e) / len(e2e)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    peaks, peak_src = _peaks()
+    gemm_ms = stage_ms[3] + stage_ms[4]
+    if args.workload == "decode":
+        alg = algorithmic_decode_bytes(cfg, touched, T)
+        # the expert GEMMs move the touched experts' blocks + the shared expert
+        gemm_bytes = alg - cfg.n_routed * cfg.dim * 2 - cfg.n_routed * 4 - 4 * T * cfg.dim
+        achieved = gemm_bytes / (gemm_ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": _traffic_record("decode"),
+                "kernel": "expert_gemm_kernel (GEMM1 w1|w3 + GEMM2 w2), per layer",
+                "algorithmic_bytes": gemm_bytes, "kernel_ms": round(gemm_ms, 4), "peak_source": peak_src}
+    else:
+        flops = algorithmic_flops(cfg, T) - 2.0 * T * cfg.dim * cfg.n_routed
+        achieved = flops / (gemm_ms * 1e-3) / 1e12
+        fp8_peak = 2 * peaks.get("bf16_tflops", 1590.0)
+        roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": fp8_peak, "unit": "TFLOP/s",
+                "frac": round(achieved / fp8_peak, 4), "traffic": _traffic_record("prefill"),
+                "kernel": "expert_gemm_kernel (GEMM1 + GEMM2), kind::mxf8f6f4 (e4m3 x e2m1, FP8 rate)",
+                "algorithmic_flops": flops, "kernel_ms": round(gemm_ms, 4),
+                "peak_source": f"{peak_src} bf16 x2 (dense FP8 rate)"}
+
+    result = {
+        "metric": METRIC, "value": round(world * T / (ms * 1e-3), 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "e2m1/e4m3 x e4m3 -> f32 (bf16 out)",
+        "data": "synthetic (seeded; random-init weights of the V4-Flash MoE shapes)",
+        "config": {"workload": f"{args.workload}_moe_layer", "tokens_per_gpu": T, "hidden": cfg.dim,
+                   "inter": cfg.inter, "routed_experts": cfg.n_routed, "topk": cfg.topk, "shared_experts": 1,
+                   "routing": "uniform" if cfg.bias == "zero" else "zipf1.2",
+                   "experts_touched": touched, "rows": rows, "l2": "flushed (256 MB write) between steps",
+                   "parallelism": "replicas" if world > 1 else "single",
+                   "cuda_graph": True},
+        "stage_ms": dict(zip(["gate", "plan", "permute", "gemm1", "gemm2", "combine"],
+                             [round(v, 5) for v in stage_ms])),
+        "roofline": roof,
+        "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 2), "unit": UNIT,
+                "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": y.numel() * 2,
+                "ms_per_step": round(e2e_ms, 5), "path": "MoE.forward_tokens -> dsv4_moe_forward (C ABI)"},
+        "clocks": clk,
+        "gpu_launches": 7 * args.steps,
+    }
+    return result, cfg, layer, moe
+
+
+def _sweep(args, local):
+    """Other decode batch sizes and the prefill layer, short runs."""
+    import torch
+
+    from spark_b200.synthetic import CONFIGS, build_moe, make_layer
+
+    out = {}
+    dev = torch.device("cuda", local)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    for wl, T in (("decode", 1), ("decode", 8), ("decode", 32), ("prefill", 8192)):
+        if wl == "decode" and T == (args.tokens or 64) and args.workload == "decode":
+            continue
+        cfg = CONFIGS[wl].with_tokens(T)
+        layer = make_layer(cfg, seed=args.seed + 7, device=dev)
+        moe = build_moe(layer, device=dev)
+        ws = torch.empty(moe.workspace_bytes(T), dtype=torch.uint8, device=dev)
+        y = torch.empty_like(layer["x"])
+        for _ in range(3):
+            moe.forward_tokens(layer["x"], workspace=ws, out=y)
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(10):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            moe.forward_tokens(layer["x"], workspace=ws, out=y)
+            e1.record()
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        ms = statistics.median(ts)
+        out[f"{wl}_T{T}"] = {"ms": round(ms, 4), "tokens_per_s": round(T / (ms * 1e-3), 1)}
+        del moe, layer, ws, y
+        torch.cuda.empty_cache()
+    return out
+
+
+# ---------------------------------------------------------------------------
+# CPU arm: the oracle restatement of the reference's layer on the host cores
+# ---------------------------------------------------------------------------
+def cpu_layer_rate(cfg_name: str, sample_tokens: int, seed: int, threads: int | None = None):
+    """tokens/s of the oracle layer (numpy) on a bounded sample of tokens."""
+    import numpy as np
+    import torch
+
+    from oracle import moe_oracle as O
+    from spark_b200.synthetic import CONFIGS, make_layer
+
+    if threads:
+        torch.set_num_threads(threads)
+    cfg = CONFIGS[cfg_name].with_tokens(sample_tokens)
+    layer = make_layer(cfg, seed=seed, device="cpu")
+    x = layer["x"].float().numpy()
+    gw = layer["gate_w"].float().numpy()
+    blocks = layer["blocks"].numpy()
+    sh = O.shared_from_tensors({k: v.numpy() for k, v in layer["shared"].items()})
+    t0 = time.perf_counter()
+    wts, idx, _ = O.gate_forward(x, gw, layer["gate_bias"].numpy(), cfg.topk, cfg.route_scale)
+    experts = {int(e): O.expert_from_block(blocks[int(e)], cfg.dim, cfg.inter) for e in np.unique(idx)}
+    mw = O.MoEWeights(gate_w=gw, gate_bias=layer["gate_bias"].numpy(), experts=experts, shared=sh,
+                      topk=cfg.topk, route_scale=cfg.route_scale, swiglu_limit=cfg.swiglu_limit)
+    O.moe_forward(x, mw, routing=(wts, idx))
+    dt = time.perf_counter() - t0
+    return sample_tokens / dt, dt
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return None
+    import torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    T = args.tokens or (64 if args.workload == "decode" else 8192)
+    sample = 8 if args.workload == "decode" else 32
+    rates = []
+    for i in range(args.warmup + args.steps):
+        r, _ = cpu_layer_rate(args.workload, sample, args.seed + i, threads)
+        if i >= args.warmup:
+            rates.append(r)
+    v = statistics.median(rates)
+    return {
+        "metric": METRIC, "value": round(v, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(sample / v * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "impl": "reference", "dtype": "f32 (numpy) over e2m1/e4m3 codes",
+        "data": "synthetic", "config": {"workload": f"{args.workload}_moe_layer", "tokens_per_gpu": T,
+                                        "sample_tokens_per_step": sample},
+        "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{sample} tokens of the {args.workload} layer per step (oracle restatement)"},
+        "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = _parse()
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        res = run_reference(args, world, rank)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    world, rank, local = _dist_init(args.gpus)
+    res, cfg, layer, moe = run_ours(args, world, rank, local)
+    del moe, layer
+    if rank == 0 and world == 1:
+        if not args.no_sweep:
+            try:
+                res["sweep"] = _sweep(args, local)
+            except Exception as exc:  # keep the headline line even if a sweep case fails
+                res["sweep"] = {"error": repr(exc)}
+        if not args.no_cpu_baseline:
+            rate, dt = cpu_layer_rate(args.workload, 8 if args.workload == "decode" else 32, args.seed,
+                                      os.cpu_count())
+            res["cpu_baseline"] = {"value": round(rate, 3), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                                   "sample": f"{8 if args.workload == 'decode' else 32} tokens of the "
+                                             f"{args.workload} layer, {dt:.1f} s (oracle restatement)"}
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

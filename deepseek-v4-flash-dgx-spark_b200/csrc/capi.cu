@@ -1,0 +1,492 @@
+// extern "C" entry points of libdsv4moe.so (declared in include/dsv4moe.h).
+#include <stdio.h>
+
+#include "kernels.cuh"
+
+namespace dsv4 {
+
+// The library links the CUDA runtime statically, so it keeps its own notion of
+// the current device: bind it to the device that owns the caller's buffers.
+static void bind_device(const void* dptr) {
+  cudaPointerAttributes a;
+  if (dptr && cudaPointerGetAttributes(&a, dptr) == cudaSuccess &&
+      a.type == cudaMemoryTypeDevice) {
+    int cur = -1;
+    if (cudaGetDevice(&cur) != cudaSuccess || cur != a.device) cudaSetDevice(a.device);
+  }
+  cudaGetLastError();
+}
+
+static int num_sms() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+// ---------------------------------------------------------------------------
+// optional stage timing: library-owned CUDA events recorded between the
+// kernels of dsv4_moe_forward (also inside stream capture, as graph nodes)
+// ---------------------------------------------------------------------------
+constexpr int kStageEvents = 7;  // start, gate, plan, permute, gemm1, gemm2, combine
+static cudaEvent_t g_stage_ev[kStageEvents];
+static bool g_profile = false;
+
+static void stage_mark(int i, cudaStream_t st) {
+  if (!g_profile) return;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(st, &cs);
+  if (cs == cudaStreamCaptureStatusActive)
+    cudaEventRecordWithFlags(g_stage_ev[i], st, cudaEventRecordExternal);
+  else
+    cudaEventRecord(g_stage_ev[i], st);
+}
+
+// ---------------------------------------------------------------------------
+// workspace layout of one layer call
+// ---------------------------------------------------------------------------
+struct Plan {
+  int T, E, k, H, I, S, block_n, max_rows, max_tiles;
+  long long off[15];
+  long long total;
+};
+
+static long long align256(long long v) { return (v + 255) & ~255LL; }
+
+static int choose_block_n(int T, int k, int E) {
+  // rows per routed expert on average; small segments waste less with N = 32
+  const long long avg = (long long)T * k / (E > 0 ? E : 1);
+  if (avg <= 16 && T <= 256) return 32;
+  if (avg <= 48) return 64;
+  return 128;
+}
+
+static int validate(const dsv4_moe_layer* L) {
+  if (!L) return DSV4_ERR_ARG;
+  if (L->hidden <= 0 || L->inter <= 0 || L->hidden % 128 || L->inter % 128) return DSV4_ERR_ARG;
+  if (L->n_routed <= 0 || L->n_routed > 512) return DSV4_ERR_UNSUPPORTED;
+  if (L->topk <= 0 || L->topk > 8 || L->topk > L->n_routed) return DSV4_ERR_UNSUPPORTED;
+  if (L->n_shared != 0 && L->n_shared != 1) return DSV4_ERR_UNSUPPORTED;
+  return DSV4_OK;
+}
+
+static Plan make_plan(const dsv4_moe_layer* L, int T) {
+  Plan p{};
+  p.T = T;
+  p.E = L->n_routed;
+  p.k = L->topk;
+  p.H = L->hidden;
+  p.I = L->inter;
+  p.S = L->n_shared;
+  p.block_n = choose_block_n(T, p.k, p.E);
+  const long long rows = (long long)T * p.k + (long long)T * p.S + 31LL * (p.E + 1);
+  p.max_rows = (int)((rows + 31) / 32 * 32);
+  p.max_tiles = (int)(((long long)T * p.k + (long long)T * p.S) / p.block_n + p.E + 2);
+  const long long atom_groups = p.max_rows / 32 + 4;
+  long long sz[15] = {
+      (long long)T * p.E * 4,                 // logits
+      (long long)T * p.k * 4,                 // weights
+      (long long)T * p.k * 8,                 // indices
+      (long long)(p.E + 1) * 4,               // counts
+      (long long)(p.E + 2) * 4,               // seg_start
+      16,                                     // n_tiles
+      (long long)T * p.k * 4,                 // route_slot
+      (long long)p.max_rows * 4,              // slot_token
+      (long long)p.max_rows * 4,              // slot_weight
+      (long long)p.max_tiles * 16,            // tiles
+      (long long)p.max_rows * p.H,            // xq
+      atom_groups * (p.H / 128) * 512,        // xsf
+      (long long)p.max_rows * p.I,            // hq
+      atom_groups * (p.I / 128) * 512,        // hsf
+      (long long)p.max_rows * p.H * 2,        // O
+  };
+  long long o = 0;
+  for (int i = 0; i < 15; ++i) {
+    p.off[i] = o;
+    o += align256(sz[i]);
+  }
+  p.total = o;
+  return p;
+}
+
+
+// GEMM1 (w1|w3 + SwiGLU + re-quant) then GEMM2 (w2) over a routing plan.
+// out_bf16 receives the expert rows [max_rows, H] (row = plan slot).
+static int run_expert_gemms(const dsv4_moe_layer* L, const int4* tiles, const int* n_tiles,
+                            const float* slot_weight, const uint8_t* xq, const uint8_t* xsf,
+                            uint8_t* hq, uint8_t* hsf, __nv_bfloat16* out_bf16, int out_ld,
+                            int max_rows, int max_tiles, int block_n, const int* expert_slot,
+                            int n_routed, int nsm, cudaStream_t st) {
+  const int H = L->hidden, I = L->inter;
+  const bool has_shared = L->shared_w1 != nullptr;
+  const bool has_routed = L->arena != nullptr;
+  int rc;
+  // arena parameter offsets inside a slot (packed order)
+  const long long sc = (long long)I * H / 32;
+  const long long w1_off = 3 * sc, w2_off = 3 * sc + (long long)I * H / 2,
+                  w3_off = 3 * sc + (long long)I * H;
+  CUtensorMap a0, a1, s0, s1, b;
+  // GEMM1: w1 | w3 over xq
+  if (has_routed) {
+    if ((rc = make_tmap_fp4_arena(&a0, L->arena + w1_off, H, I, L->n_slots, L->slot_stride)))
+      return rc;
+    if ((rc = make_tmap_fp4_arena(&a1, L->arena + w3_off, H, I, L->n_slots, L->slot_stride)))
+      return rc;
+  }
+  if (has_shared) {
+    if ((rc = make_tmap_u8(&s0, L->shared_w1, H, I, 128))) return rc;
+    if ((rc = make_tmap_u8(&s1, L->shared_w3, H, I, 128))) return rc;
+  }
+  if (!has_routed) {
+    a0 = s0;
+    a1 = s1;
+  }
+  if (!has_shared) {
+    s0 = a0;
+    s1 = a1;
+  }
+  if ((rc = make_tmap_u8(&b, xq, H, max_rows, block_n))) return rc;
+  GemmArgs g1{};
+  g1.tiles = tiles;
+  g1.n_tiles = n_tiles;
+  g1.expert_slot = expert_slot;
+  g1.n_routed = n_routed;
+  g1.kt_count = H / 128;
+  g1.nb_count = I / 128;
+  g1.sf_routed = L->arena_sf;
+  g1.sf_slot_stride = L->sf_slot_stride;
+  g1.sf_off0 = 0;
+  g1.sf_off1 = sc;
+  g1.sf_shared0 = L->shared_sf;
+  g1.sf_shared1 = L->shared_sf ? L->shared_sf + sc : nullptr;
+  g1.sfb = xsf;
+  g1.slot_weight = slot_weight;
+  g1.out_q = hq;
+  g1.out_sf = hsf;
+  g1.out_ld = I;
+  g1.swiglu_limit = L->swiglu_limit;
+  const long long work1 = (long long)max_tiles * g1.nb_count;
+  const int grid1 = (int)(work1 < nsm ? work1 : nsm);
+  if ((rc = launch_expert_gemm(true, block_n, a0, a1, s0, s1, b, g1, grid1, st))) return rc;
+  stage_mark(4, st);
+
+  // GEMM2: w2 over hq
+  if (has_routed) {
+    if ((rc = make_tmap_fp4_arena(&a0, L->arena + w2_off, I, H, L->n_slots, L->slot_stride)))
+      return rc;
+  }
+  if (has_shared) {
+    if ((rc = make_tmap_u8(&s0, L->shared_w2, I, H, 128))) return rc;
+  }
+  if (!has_routed) a0 = s0;
+  if (!has_shared) s0 = a0;
+  if ((rc = make_tmap_u8(&b, hq, I, max_rows, block_n))) return rc;
+  GemmArgs g2 = g1;
+  g2.kt_count = I / 128;
+  g2.nb_count = H / 128;
+  g2.sf_off0 = 2 * sc;
+  g2.sf_off1 = 2 * sc;
+  g2.sf_shared0 = L->shared_sf ? L->shared_sf + 2 * sc : nullptr;
+  g2.sf_shared1 = g2.sf_shared0;
+  g2.sfb = hsf;
+  g2.out_q = nullptr;
+  g2.out_sf = nullptr;
+  g2.out_bf16 = out_bf16;
+  g2.out_ld = out_ld;
+  const long long work2 = (long long)max_tiles * g2.nb_count;
+  const int grid2 = (int)(work2 < nsm ? work2 : nsm);
+  rc = launch_expert_gemm(false, block_n, a0, a0, s0, s0, b, g2, grid2, st);
+  stage_mark(5, st);
+  return rc;
+}
+
+// Workspace of one single-expert call: identity plan + activation buffers.
+struct ExpertPlan {
+  int rows_pad, block_n, max_tiles;
+  long long off[8];
+  long long total;
+};
+
+static ExpertPlan make_expert_plan(const dsv4_moe_layer* L, int T) {
+  ExpertPlan p{};
+  p.block_n = T <= 32 ? 32 : (T <= 64 ? 64 : 128);
+  p.rows_pad = (T + 31) / 32 * 32;
+  p.max_tiles = (T + p.block_n - 1) / p.block_n + 1;
+  const long long groups = p.rows_pad / 32 + 4;
+  long long sz[8] = {
+      16,                                        // n_tiles, total_rows
+      (long long)p.rows_pad * 4,                 // slot_token
+      (long long)p.rows_pad * 4,                 // slot_weight
+      (long long)p.max_tiles * 16,               // tiles
+      (long long)p.rows_pad * L->hidden,         // xq
+      groups * (L->hidden / 128) * 512,          // xsf
+      (long long)p.rows_pad * L->inter,          // hq
+      groups * (L->inter / 128) * 512,           // hsf
+  };
+  long long o = 0;
+  for (int i = 0; i < 8; ++i) {
+    p.off[i] = o;
+    o += align256(sz[i]);
+  }
+  p.total = o;
+  return p;
+}
+
+}  // namespace dsv4
+
+using namespace dsv4;
+
+extern "C" {
+
+int dsv4_version(void) { return 1; }
+
+const char* dsv4_status_string(int s) {
+  switch (s) {
+    case DSV4_OK: return "ok";
+    case DSV4_ERR_ARG: return "invalid argument";
+    case DSV4_ERR_CUDA: return "CUDA error";
+    case DSV4_ERR_UNSUPPORTED: return "unsupported shape or option";
+    case DSV4_ERR_IO: return "pread failed";
+    case DSV4_ERR_SHORT_READ: return "short packed expert read";
+    case DSV4_ERR_BOUNDS: return "source slice exceeds storage tensor";
+    case DSV4_ERR_SIZE: return "target size does not match expert copy plan";
+    case DSV4_ERR_WORKSPACE: return "workspace too small";
+    default: return "unknown status";
+  }
+}
+
+int dsv4_device_error(int clear, int* code) {
+  if (!code) return DSV4_ERR_ARG;
+  if (cudaDeviceSynchronize() != cudaSuccess) return DSV4_ERR_CUDA;
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_dsv4_device_error, sizeof(int)) != cudaSuccess)
+    return DSV4_ERR_CUDA;
+  *code = v;
+  if (clear && v) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_dsv4_device_error, &zero, sizeof(int)) != cudaSuccess)
+      return DSV4_ERR_CUDA;
+  }
+  return DSV4_OK;
+}
+
+int dsv4_profile_enable(int enable) {
+  if (enable && !g_profile) {
+    for (int i = 0; i < kStageEvents; ++i)
+      if (cudaEventCreate(&g_stage_ev[i]) != cudaSuccess) return DSV4_ERR_CUDA;
+    g_profile = true;
+  } else if (!enable && g_profile) {
+    for (int i = 0; i < kStageEvents; ++i) cudaEventDestroy(g_stage_ev[i]);
+    g_profile = false;
+  }
+  return DSV4_OK;
+}
+
+int dsv4_profile_read(float* stage_ms, int n) {
+  if (!g_profile || !stage_ms || n < kStageEvents - 1) return DSV4_ERR_ARG;
+  if (cudaEventSynchronize(g_stage_ev[kStageEvents - 1]) != cudaSuccess) return DSV4_ERR_CUDA;
+  for (int i = 0; i + 1 < kStageEvents; ++i) {
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, g_stage_ev[i], g_stage_ev[i + 1]) != cudaSuccess) ms = -1.f;
+    stage_ms[i] = ms;
+  }
+  return DSV4_OK;
+}
+
+long long dsv4_moe_workspace_bytes(const dsv4_moe_layer* L, int T) {
+  if (validate(L) != DSV4_OK || T < 0) return -1;
+  return make_plan(L, T).total;
+}
+
+int dsv4_moe_workspace_layout(const dsv4_moe_layer* L, int T, long long* out, int n_out) {
+  int rc = validate(L);
+  if (rc) return rc;
+  if (!out || n_out < 17 || T < 0) return DSV4_ERR_ARG;
+  const Plan p = make_plan(L, T);
+  for (int i = 0; i < 15; ++i) out[i] = p.off[i];
+  out[15] = p.max_rows;
+  out[16] = p.block_n;
+  return DSV4_OK;
+}
+
+int dsv4_gate_logits(const void* x, const void* w, int w_is_fp32, int T, int H, int E,
+                     float* logits, void* stream) {
+  if (!x || !w || !logits || T < 0 || H <= 0 || H % 8 || E <= 0) return DSV4_ERR_ARG;
+  if (T == 0) return DSV4_OK;
+  if ((size_t)4 * H * sizeof(float) > 200 * 1024) return DSV4_ERR_UNSUPPORTED;
+  bind_device(logits);
+  return launch_gate_logits(x, w, w_is_fp32, T, H, E, logits, static_cast<cudaStream_t>(stream));
+}
+
+int dsv4_gate_topk(const float* logits, const float* bias, int T, int E, int topk,
+                   float route_scale, float* weights, int64_t* indices, void* stream) {
+  if (!logits || !weights || !indices || T < 0 || E <= 0 || topk <= 0) return DSV4_ERR_ARG;
+  if (E > 512 || topk > 8 || topk > E) return DSV4_ERR_UNSUPPORTED;
+  bind_device(weights);
+  return launch_gate_topk(logits, bias, T, E, topk, route_scale, weights, indices,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int dsv4_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* scale, void* stream) {
+  if (!x || !q || !scale || M < 0 || K <= 0 || K % 128) return DSV4_ERR_ARG;
+  bind_device(q);
+  return launch_act_quant(x, M, K, q, scale, num_sms(), static_cast<cudaStream_t>(stream));
+}
+
+int dsv4_moe_forward(const dsv4_moe_layer* L, const void* x, int T, void* y,
+                     const float* routing_weights, const int64_t* routing_indices,
+                     void* workspace, long long workspace_bytes, void* stream) {
+  int rc = validate(L);
+  if (rc) return rc;
+  if (!x || !y || T < 0 || !L->arena || !L->arena_sf || !L->expert_slot) return DSV4_ERR_ARG;
+  if ((routing_weights == nullptr) != (routing_indices == nullptr)) return DSV4_ERR_ARG;
+  if (!routing_weights && !L->gate_w) return DSV4_ERR_ARG;
+  if (L->n_shared && (!L->shared_w1 || !L->shared_w2 || !L->shared_w3 || !L->shared_sf))
+    return DSV4_ERR_ARG;
+  if (L->slot_stride % 32 || L->n_slots <= 0) return DSV4_ERR_ARG;
+  if (T == 0) return DSV4_OK;
+  const Plan p = make_plan(L, T);
+  if (!workspace || workspace_bytes < p.total) return DSV4_ERR_WORKSPACE;
+  bind_device(workspace);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* logits = reinterpret_cast<float*>(ws + p.off[0]);
+  float* weights = reinterpret_cast<float*>(ws + p.off[1]);
+  int64_t* indices = reinterpret_cast<int64_t*>(ws + p.off[2]);
+  int* counts = reinterpret_cast<int*>(ws + p.off[3]);
+  int* seg_start = reinterpret_cast<int*>(ws + p.off[4]);
+  int* n_tiles = reinterpret_cast<int*>(ws + p.off[5]);
+  int* route_slot = reinterpret_cast<int*>(ws + p.off[6]);
+  int* slot_token = reinterpret_cast<int*>(ws + p.off[7]);
+  float* slot_weight = reinterpret_cast<float*>(ws + p.off[8]);
+  int4* tiles = reinterpret_cast<int4*>(ws + p.off[9]);
+  uint8_t* xq = ws + p.off[10];
+  uint8_t* xsf = ws + p.off[11];
+  uint8_t* hq = ws + p.off[12];
+  uint8_t* hsf = ws + p.off[13];
+  __nv_bfloat16* O = reinterpret_cast<__nv_bfloat16*>(ws + p.off[14]);
+  const int nsm = num_sms();
+  const int H = p.H, I = p.I, E = p.E, k = p.k;
+
+  const float* rw = routing_weights;
+  const int64_t* ri = routing_indices;
+  stage_mark(0, st);
+  if (!rw) {
+    if ((rc = launch_gate_logits(x, L->gate_w, L->gate_w_fp32, T, H, E, logits, st))) return rc;
+    if ((rc = launch_gate_topk(logits, L->gate_bias, T, E, k, L->route_scale, weights, indices,
+                               st)))
+      return rc;
+    rw = weights;
+    ri = indices;
+  }
+  stage_mark(1, st);
+  if ((rc = launch_route_plan(ri, rw, T, k, E, p.S, p.block_n, p.max_rows, p.max_tiles, counts,
+                              seg_start, route_slot, slot_token, slot_weight, tiles, n_tiles, st)))
+    return rc;
+  if ((rc = launch_permute_quant(x, H, slot_token, seg_start + E + 1, p.max_rows, xq, xsf, nsm,
+                                 st)))
+    return rc;
+
+  if ((rc = run_expert_gemms(L, tiles, n_tiles, slot_weight, xq, xsf, hq, hsf, O, H, p.max_rows,
+                             p.max_tiles, p.block_n, L->expert_slot, L->n_routed, nsm, st)))
+    return rc;
+  rc = launch_combine(O, H, route_slot, ri, T, k, p.S ? seg_start + E : nullptr, y, st);
+  stage_mark(6, st);
+  return rc;
+}
+
+long long dsv4_expert_workspace_bytes(const dsv4_moe_layer* L, int T) {
+  if (!L || L->hidden % 128 || L->inter % 128 || T < 0) return -1;
+  return make_expert_plan(L, T).total;
+}
+
+int dsv4_expert_forward(const dsv4_moe_layer* L, int expert, const void* x, int T,
+                        const float* row_weights, void* y, void* workspace,
+                        long long workspace_bytes, void* stream) {
+  if (!L || !x || !y || T < 0 || L->hidden % 128 || L->inter % 128) return DSV4_ERR_ARG;
+  if (expert < 0 && (!L->shared_w1 || !L->shared_w2 || !L->shared_w3 || !L->shared_sf))
+    return DSV4_ERR_ARG;
+  if (expert >= 0 && (!L->arena || !L->arena_sf || !L->expert_slot || expert >= L->n_routed ||
+                      L->slot_stride % 32))
+    return DSV4_ERR_ARG;
+  if (T == 0) return DSV4_OK;
+  const ExpertPlan p = make_expert_plan(L, T);
+  if (!workspace || workspace_bytes < p.total) return DSV4_ERR_WORKSPACE;
+  bind_device(workspace);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* n_tiles = reinterpret_cast<int*>(ws + p.off[0]);
+  int* total_rows = n_tiles + 1;
+  int* slot_token = reinterpret_cast<int*>(ws + p.off[1]);
+  float* slot_weight = reinterpret_cast<float*>(ws + p.off[2]);
+  int4* tiles = reinterpret_cast<int4*>(ws + p.off[3]);
+  uint8_t* xq = ws + p.off[4];
+  uint8_t* xsf = ws + p.off[5];
+  uint8_t* hq = ws + p.off[6];
+  uint8_t* hsf = ws + p.off[7];
+  const int nsm = num_sms();
+  // the shared expert is segment n_routed; a routed expert keeps its own id
+  dsv4_moe_layer Lx = *L;
+  int seg = expert;
+  if (expert < 0) {
+    Lx.arena = nullptr;
+    seg = L->n_routed > 0 ? L->n_routed : 0;
+    Lx.n_routed = seg;
+  } else {
+    Lx.shared_w1 = Lx.shared_w2 = Lx.shared_w3 = nullptr;
+    Lx.shared_sf = nullptr;
+  }
+  int rc;
+  if ((rc = launch_single_segment_plan(T, seg, p.block_n, p.rows_pad, row_weights, slot_token,
+                                       slot_weight, tiles, n_tiles, total_rows, st)))
+    return rc;
+  if ((rc = launch_permute_quant(x, L->hidden, slot_token, total_rows, p.rows_pad, xq, xsf, nsm,
+                                 st)))
+    return rc;
+  // rows are tokens and the epilogue stores only rows < T, so GEMM2 writes y
+  return run_expert_gemms(&Lx, tiles, n_tiles, slot_weight, xq, xsf, hq, hsf,
+                          static_cast<__nv_bfloat16*>(y), L->hidden, p.rows_pad, p.max_tiles,
+                          p.block_n, L->expert_slot, Lx.n_routed, nsm, st);
+}
+
+int dsv4_materialize(const uint8_t* slab, const long long* src_off, const int* dst_slot, int n,
+                     int hidden, int inter, uint8_t* arena, long long slot_stride,
+                     uint8_t* arena_sf, long long sf_slot_stride, void* bf16_out,
+                     long long bf16_slot_stride, void* stream) {
+  if (!slab || !src_off || !dst_slot || n < 0 || hidden % 128 || inter % 128) return DSV4_ERR_ARG;
+  const long long block = 3LL * inter * hidden / 32 + 3LL * inter * hidden / 2;
+  if (arena && slot_stride < block) return DSV4_ERR_ARG;
+  if (arena_sf && sf_slot_stride < 3LL * inter * hidden / 32) return DSV4_ERR_ARG;
+  if (arena && slot_stride % 16) return DSV4_ERR_ARG;
+  bind_device(slab);
+  return launch_materialize(slab, src_off, dst_slot, n, block, arena, slot_stride, hidden, inter,
+                            arena_sf, sf_slot_stride, bf16_out, bf16_slot_stride, num_sms(),
+                            static_cast<cudaStream_t>(stream));
+}
+
+int dsv4_build_scale_atoms(const uint8_t* arena, long long slot_stride, const int* slots, int n,
+                           int hidden, int inter, uint8_t* arena_sf, long long sf_slot_stride,
+                           void* stream) {
+  if (!arena || !slots || !arena_sf || n < 0 || hidden % 128 || inter % 128) return DSV4_ERR_ARG;
+  if (sf_slot_stride < 3LL * inter * hidden / 32) return DSV4_ERR_ARG;
+  bind_device(arena);
+  return launch_build_sf_fp4_arena(arena, slot_stride, slots, n, hidden, inter, arena_sf,
+                                   sf_slot_stride, num_sms(), static_cast<cudaStream_t>(stream));
+}
+
+int dsv4_build_shared_scale_atoms(const uint8_t* w1_scale, const uint8_t* w2_scale,
+                                  const uint8_t* w3_scale, int hidden, int inter,
+                                  uint8_t* shared_sf, void* stream) {
+  if (!w1_scale || !w2_scale || !w3_scale || !shared_sf || hidden % 128 || inter % 128)
+    return DSV4_ERR_ARG;
+  bind_device(shared_sf);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const long long sc = (long long)inter * hidden / 32;
+  const int nsm = num_sms();
+  int rc;
+  if ((rc = launch_build_sf_fp8(w1_scale, inter, hidden, shared_sf, nsm, st))) return rc;
+  if ((rc = launch_build_sf_fp8(w3_scale, inter, hidden, shared_sf + sc, nsm, st))) return rc;
+  return launch_build_sf_fp8(w2_scale, hidden, inter, shared_sf + 2 * sc, nsm, st);
+}
+
+}  // extern "C"

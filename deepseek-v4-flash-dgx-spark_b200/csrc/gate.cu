@@ -1,0 +1,206 @@
+// Gate: logits = x . Wg^T (fp32), then sigmoid scores, correction bias, top-k,
+// renormalise, routed scale.  Replaces the official Gate.forward(x, input_ids)
+// that the reference calls at spark_runtime/lazy_official_runtime.py:983.
+#include "kernels.cuh"
+
+namespace dsv4 {
+
+// ---------------------------------------------------------------------------
+// Canonical fp32 sigmoid.  exp() is Cody & Waite range reduction with the
+// two-constant split of ln 2 used by Moshier's Cephes expf (C1 = 355/512,
+// C2 = -2.12194440e-4) and the degree-7 Taylor polynomial of e^r in Horner
+// form.  Every step is a single round-to-nearest fp32 operation (no FMA
+// contraction), so the CPU restatement reproduces it bit for bit.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float exp_canonical(float t) {
+  const float n = rintf(__fmul_rn(t, 1.4426950408889634f));
+  float r = __fsub_rn(t, __fmul_rn(n, 0.693359375f));
+  r = __fsub_rn(r, __fmul_rn(n, -2.12194440e-4f));
+  float p = 1.0f / 5040.0f;
+  p = __fadd_rn(__fmul_rn(p, r), 1.0f / 720.0f);
+  p = __fadd_rn(__fmul_rn(p, r), 1.0f / 120.0f);
+  p = __fadd_rn(__fmul_rn(p, r), 1.0f / 24.0f);
+  p = __fadd_rn(__fmul_rn(p, r), 1.0f / 6.0f);
+  p = __fadd_rn(__fmul_rn(p, r), 0.5f);
+  p = __fadd_rn(__fmul_rn(p, r), 1.0f);
+  p = __fadd_rn(__fmul_rn(p, r), 1.0f);
+  return __fmul_rn(p, exp2i(static_cast<int>(n)));
+}
+
+__device__ __forceinline__ float sigmoid_canonical(float x) {
+  const float t = fminf(fmaxf(-x, -80.0f), 80.0f);
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_canonical(t)));
+}
+
+// ---------------------------------------------------------------------------
+// Logits.  Each CTA owns EPC experts: their gate rows are staged in shared
+// memory as fp32, then each warp walks tokens and accumulates EPC dot
+// products with 16-byte loads of x, reduced across the warp.
+// ---------------------------------------------------------------------------
+constexpr int kGateEPC = 4;
+
+template <bool W_FP32>
+__global__ void __launch_bounds__(256) gate_logits_kernel(const __nv_bfloat16* __restrict__ x,
+                                                          const void* __restrict__ w, int T, int H,
+                                                          int E, float* __restrict__ logits) {
+  extern __shared__ float ws[];  // [kGateEPC][H]
+  const int e0 = blockIdx.x * kGateEPC;
+  const int ne = min(kGateEPC, E - e0);
+  for (int i = threadIdx.x; i < kGateEPC * H; i += blockDim.x) {
+    const int j = i / H, h = i % H;
+    float v = 0.f;
+    if (j < ne) {
+      if (W_FP32)
+        v = static_cast<const float*>(w)[(size_t)(e0 + j) * H + h];
+      else
+        v = __bfloat162float(static_cast<const __nv_bfloat16*>(w)[(size_t)(e0 + j) * H + h]);
+    }
+    ws[i] = v;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  for (int t = warp; t < T; t += nwarps) {
+    float acc[kGateEPC];
+#pragma unroll
+    for (int j = 0; j < kGateEPC; ++j) acc[j] = 0.f;
+    const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)t * H);
+    for (int c = lane; c < H / 8; c += 32) {
+      const uint4 raw = __ldg(xr + c);
+      const __nv_bfloat16* xv = reinterpret_cast<const __nv_bfloat16*>(&raw);
+      float xf[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) xf[i] = __bfloat162float(xv[i]);
+#pragma unroll
+      for (int j = 0; j < kGateEPC; ++j) {
+        const float4* wr = reinterpret_cast<const float4*>(ws + j * H + c * 8);
+        const float4 a = wr[0], b = wr[1];
+        acc[j] = fmaf(xf[0], a.x, acc[j]);
+        acc[j] = fmaf(xf[1], a.y, acc[j]);
+        acc[j] = fmaf(xf[2], a.z, acc[j]);
+        acc[j] = fmaf(xf[3], a.w, acc[j]);
+        acc[j] = fmaf(xf[4], b.x, acc[j]);
+        acc[j] = fmaf(xf[5], b.y, acc[j]);
+        acc[j] = fmaf(xf[6], b.z, acc[j]);
+        acc[j] = fmaf(xf[7], b.w, acc[j]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kGateEPC; ++j) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+    }
+    if (lane == 0) {
+      for (int j = 0; j < ne; ++j) logits[(size_t)t * E + e0 + j] = acc[j];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Top-k.  One warp per token; lane l holds experts l, l+32, ...  k rounds of a
+// warp arg-max on (score + bias), ties to the lower expert id.
+// ---------------------------------------------------------------------------
+constexpr int kMaxExpertsPerLane = 16;  // E <= 512
+constexpr int kMaxTopk = 8;
+
+__global__ void __launch_bounds__(256) gate_topk_kernel(const float* __restrict__ logits,
+                                                        const float* __restrict__ bias, int T,
+                                                        int E, int k, float route_scale,
+                                                        float* __restrict__ weights,
+                                                        int64_t* __restrict__ indices) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  const int t = warp;
+  float score[kMaxExpertsPerLane], sel[kMaxExpertsPerLane];
+  const int per = (E + 31) / 32;
+#pragma unroll
+  for (int i = 0; i < kMaxExpertsPerLane; ++i) {
+    const int e = lane + 32 * i;
+    if (i < per && e < E) {
+      const float s = sigmoid_canonical(logits[(size_t)t * E + e]);
+      score[i] = s;
+      sel[i] = bias ? __fadd_rn(s, bias[e]) : s;
+    } else {
+      score[i] = 0.f;
+      sel[i] = -INFINITY;
+    }
+  }
+  float total = 0.f;
+  float my_w = 0.f;  // lane r keeps the rank-r pick
+  int my_e = 0;
+#pragma unroll
+  for (int r = 0; r < kMaxTopk; ++r) {
+    if (r >= k) break;
+    float best = -INFINITY;
+    int best_e = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < kMaxExpertsPerLane; ++i) {
+      // experts of a lane increase with i, so '>' keeps the lower id on ties
+      if (sel[i] > best) {
+        best = sel[i];
+        best_e = lane + 32 * i;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oe = __shfl_xor_sync(0xffffffffu, best_e, o);
+      if (ob > best || (ob == best && oe < best_e)) {
+        best = ob;
+        best_e = oe;
+      }
+    }
+    // the owning lane retires the winner and broadcasts its raw score
+    float w = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxExpertsPerLane; ++i) {
+      if (lane + 32 * i == best_e) {
+        w = score[i];
+        sel[i] = -INFINITY;
+      }
+    }
+    w = __shfl_sync(0xffffffffu, w, best_e & 31);
+    total = (r == 0) ? w : __fadd_rn(total, w);
+    if (lane == r) {
+      my_w = w;
+      my_e = best_e;
+    }
+  }
+  if (lane < k) {
+    float w = __fdiv_rn(my_w, total);
+    w = __fmul_rn(w, route_scale);
+    weights[(size_t)t * k + lane] = w;
+    indices[(size_t)t * k + lane] = my_e;
+  }
+}
+
+int launch_gate_logits(const void* x, const void* w, int w_is_fp32, int T, int H, int E,
+                       float* logits, cudaStream_t st) {
+  const int grid = (E + kGateEPC - 1) / kGateEPC;
+  const size_t smem = (size_t)kGateEPC * H * sizeof(float);
+  if (w_is_fp32) {
+    cudaFuncSetAttribute(gate_logits_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+    gate_logits_kernel<true><<<grid, 256, smem, st>>>(static_cast<const __nv_bfloat16*>(x), w, T,
+                                                      H, E, logits);
+  } else {
+    cudaFuncSetAttribute(gate_logits_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+    gate_logits_kernel<false><<<grid, 256, smem, st>>>(static_cast<const __nv_bfloat16*>(x), w,
+                                                       T, H, E, logits);
+  }
+  return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
+}
+
+int launch_gate_topk(const float* logits, const float* bias, int T, int E, int k,
+                     float route_scale, float* weights, int64_t* indices, cudaStream_t st) {
+  const int warps_per_cta = 8;
+  const int grid = (T + warps_per_cta - 1) / warps_per_cta;
+  if (grid > 0)
+    gate_topk_kernel<<<grid, warps_per_cta * 32, 0, st>>>(logits, bias, T, E, k, route_scale,
+                                                          weights, indices);
+  return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
+}
+
+}  // namespace dsv4

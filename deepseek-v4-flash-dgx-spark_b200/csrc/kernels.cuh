@@ -1,0 +1,63 @@
+// Internal declarations shared by the dsv4moe translation units.
+#pragma once
+
+#include "common.cuh"
+
+namespace dsv4 {
+
+// Arguments of the grouped expert GEMM kernel (see expert_gemm.cu).
+struct GemmArgs {
+  const int4* tiles;      // [n_tiles] {segment, row0, nrows, 0}
+  const int* n_tiles;     // device scalar written by the route plan
+  const int* expert_slot; // [n_routed] routed expert -> arena slot
+  int n_routed;           // segment id n_routed is the shared expert
+  int kt_count;           // K / 128
+  int nb_count;           // output rows / 128 (per weight)
+  const uint8_t* sf_routed;
+  long long sf_slot_stride;
+  long long sf_off0, sf_off1;  // byte offsets of the A0 / A1 atoms inside a slot
+  const uint8_t* sf_shared0;
+  const uint8_t* sf_shared1;
+  const uint8_t* sfb;          // activation atoms, sliding layout [row/32][kt_count][512]
+  const float* slot_weight;    // GEMM1: routing weight of each segment row
+  uint8_t* out_q;              // GEMM1: H codes [rows][out_ld]
+  uint8_t* out_sf;             // GEMM1: H scale atoms, sliding layout [row/32][out_ld/128][512]
+  __nv_bfloat16* out_bf16;     // GEMM2: O [rows][out_ld]
+  int out_ld;
+  float swiglu_limit;
+};
+
+int launch_gate_logits(const void* x, const void* w, int w_is_fp32, int T, int H, int E,
+                       float* logits, cudaStream_t st);
+int launch_gate_topk(const float* logits, const float* bias, int T, int E, int k,
+                     float route_scale, float* weights, int64_t* indices, cudaStream_t st);
+int launch_route_plan(const int64_t* indices, const float* weights, int T, int k, int E,
+                      int include_shared, int block_n, int max_rows, int max_tiles, int* counts,
+                      int* seg_start, int* route_slot, int* slot_token, float* slot_weight,
+                      int4* tiles, int* n_tiles, cudaStream_t st);
+int launch_permute_quant(const void* x, int H, const int* slot_token, const int* total_rows_ptr,
+                         int max_rows, uint8_t* xq, uint8_t* sfb, int num_sms, cudaStream_t st);
+int launch_single_segment_plan(int T, int seg, int block_n, int rows_pad, const float* w,
+                               int* slot_token, float* slot_weight, int4* tiles, int* n_tiles,
+                               int* total_rows, cudaStream_t st);
+int launch_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* s, int num_sms,
+                     cudaStream_t st);
+int launch_combine(const void* O, int H, const int* route_slot, const int64_t* indices, int T,
+                   int k, const int* shared_base, void* y, cudaStream_t st);
+int launch_materialize(const uint8_t* slab, const long long* src_off, const int* dst_slot, int n,
+                       long long block_bytes, uint8_t* arena, long long slot_stride, int hidden,
+                       int inter, uint8_t* sf, long long sf_slot_stride, void* bf16_out,
+                       long long bf16_slot_stride, int num_sms, cudaStream_t st);
+int launch_build_sf_fp4_arena(const uint8_t* arena, long long slot_stride, const int* slots,
+                              int n, int hidden, int inter, uint8_t* sf, long long sf_slot_stride,
+                              int num_sms, cudaStream_t st);
+int launch_build_sf_fp8(const uint8_t* scale, int rows, int K, uint8_t* atoms, int num_sms,
+                        cudaStream_t st);
+int make_tmap_fp4_arena(CUtensorMap* m, const void* base, int K, int rows, int slots,
+                        long long slot_stride);
+int make_tmap_u8(CUtensorMap* m, const void* base, int K, int rows, int box_rows);
+int launch_expert_gemm(bool gated, int block_n, const CUtensorMap& a0, const CUtensorMap& a1,
+                       const CUtensorMap& s0, const CUtensorMap& s1, const CUtensorMap& b,
+                       const GemmArgs& args, int grid, cudaStream_t st);
+
+}  // namespace dsv4

@@ -1,0 +1,454 @@
+"""B200 MoE layer with the official DeepSeek module interface.
+
+Drop-in for the modules the reference builds its MoE from:
+
+* ``MoE(layer_id, args)`` / ``forward(x, input_ids)`` - the class the reference
+  patches in as ``official_model.MoE`` (``BoundLazyMoE``,
+  spark_runtime/lazy_official_runtime.py:946-1002,1052-1061);
+* ``Gate(layer_id, args)`` / ``forward(x, input_ids) -> (weights, indices)``
+  (official Gate, called at :966,983);
+* ``Expert(dim, inter_dim, dtype=, swiglu_limit=)`` / ``forward(x, weights)``
+  (official Expert, constructed at :769-774 and :976-978);
+* ``ExpertArena(max_slots).acquire(factory) -> (expert, reused)`` /
+  ``release(expert) -> bool`` (:641-667).
+
+Submodule and parameter names follow the official state dict
+(``gate.weight``, ``gate.bias``, ``experts.{i}.w1.weight``, ``.scale``, ...,
+``shared_experts.w1.weight``), so checkpoint names still resolve.  All compute
+goes through libdsv4moe.so; nothing here computes on the CPU.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+from torch import nn
+
+from . import _lib
+from ._lib import MoELayerDesc, check, ptr, stream_ptr
+
+FP4 = torch.float4_e2m1fn_x2
+E8M0 = torch.float8_e8m0fnu
+E4M3 = torch.float8_e4m3fn
+
+
+@dataclass
+class ModelArgs:
+    """The ``ModelArgs`` fields the MoE path reads (lazy_official_runtime.py:959-978,767-774)."""
+
+    dim: int = 4096
+    moe_inter_dim: int = 2048
+    n_routed_experts: int = 256
+    n_activated_experts: int = 6
+    n_shared_experts: int = 1
+    expert_dtype: str = "fp4"
+    swiglu_limit: float = 10.0
+    route_scale: float = 2.5
+    score_func: str = "sigmoid"
+    gate_dtype: torch.dtype = torch.bfloat16
+    gate_bias: bool = True
+
+
+# ---------------------------------------------------------------------------
+# packed expert block (scripts/build_packed_expert_layout.py:76-86)
+# ---------------------------------------------------------------------------
+PACKED_ORDER = ("w1.scale", "w2.scale", "w3.scale", "w1.weight", "w2.weight", "w3.weight")
+
+
+def packed_block_layout(dim: int, inter: int) -> dict[str, tuple[int, int, torch.dtype, tuple[int, int]]]:
+    """name -> (offset, bytes, dtype, shape) of the six routed-expert tensors in
+    one packed block, in the slab's tensor order."""
+    shapes = {
+        "w1.scale": ((inter, dim // 32), E8M0),
+        "w2.scale": ((dim, inter // 32), E8M0),
+        "w3.scale": ((inter, dim // 32), E8M0),
+        "w1.weight": ((inter, dim // 2), FP4),
+        "w2.weight": ((dim, inter // 2), FP4),
+        "w3.weight": ((inter, dim // 2), FP4),
+    }
+    out, off = {}, 0
+    for name in PACKED_ORDER:
+        shape, dtype = shapes[name]
+        n = shape[0] * shape[1]
+        out[name] = (off, n, dtype, shape)
+        off += n
+    return out
+
+
+def packed_block_bytes(dim: int, inter: int) -> int:
+    return 3 * inter * dim // 32 + 3 * inter * dim // 2
+
+
+def scale_atom_bytes(dim: int, inter: int) -> int:
+    return 3 * inter * dim // 32
+
+
+class _QLinear(nn.Module):
+    """Holder of one quantized projection: ``weight`` and ``scale`` parameters."""
+
+    def __init__(self, weight: torch.Tensor, scale: torch.Tensor):
+        super().__init__()
+        self.weight = nn.Parameter(weight, requires_grad=False)
+        self.scale = nn.Parameter(scale, requires_grad=False)
+
+
+# ---------------------------------------------------------------------------
+# Expert
+# ---------------------------------------------------------------------------
+class Expert(nn.Module):
+    """Official ``Expert(dim, inter_dim, dtype=None|float4_e2m1fn_x2, swiglu_limit=)``.
+
+    Routed (fp4): the six tensors are views into one packed block (its own
+    buffer, or an arena slot passed as ``storage``), so a materialized block's
+    bytes are the parameters.  Shared (dtype None): fp8 e4m3 weights with
+    128x128 ue8m0 block scales.  ``scale_atoms`` holds the tensor-memory scale
+    layout the kernels read; call ``refresh_scale_atoms()`` after writing the
+    parameters (``load_state_dict`` does it automatically)."""
+
+    def __init__(self, dim: int, inter_dim: int, dtype=None, swiglu_limit: float = 0.0, *,
+                 storage: torch.Tensor | None = None, scale_atoms: torch.Tensor | None = None,
+                 device=None):
+        super().__init__()
+        self.dim, self.inter_dim = dim, inter_dim
+        self.swiglu_limit = float(swiglu_limit or 0.0)
+        self.fp4 = dtype == FP4
+        device = torch.device(device) if device is not None else (
+            storage.device if storage is not None else torch.device("cuda"))
+        if self.fp4:
+            nbytes = packed_block_bytes(dim, inter_dim)
+            if storage is None:
+                storage = torch.zeros(_round_up(nbytes, 256), dtype=torch.uint8, device=device)
+            if storage.numel() < nbytes or storage.dtype != torch.uint8:
+                raise RuntimeError("expert storage is smaller than one packed block")
+            self.register_buffer("block", storage, persistent=False)
+            lay = packed_block_layout(dim, inter_dim)
+            views = {}
+            for name, (off, n, dt, shape) in lay.items():
+                views[name] = storage[off:off + n].view(dt).view(*shape)
+            self.w1 = _QLinear(views["w1.weight"], views["w1.scale"])
+            self.w2 = _QLinear(views["w2.weight"], views["w2.scale"])
+            self.w3 = _QLinear(views["w3.weight"], views["w3.scale"])
+        else:
+            self.register_buffer("block", None, persistent=False)
+            self.w1 = _QLinear(torch.zeros(inter_dim, dim, dtype=torch.uint8, device=device).view(E4M3),
+                               torch.full((inter_dim // 128, dim // 128), 127, dtype=torch.uint8,
+                                          device=device).view(E8M0))
+            self.w2 = _QLinear(torch.zeros(dim, inter_dim, dtype=torch.uint8, device=device).view(E4M3),
+                               torch.full((dim // 128, inter_dim // 128), 127, dtype=torch.uint8,
+                                          device=device).view(E8M0))
+            self.w3 = _QLinear(torch.zeros(inter_dim, dim, dtype=torch.uint8, device=device).view(E4M3),
+                               torch.full((inter_dim // 128, dim // 128), 127, dtype=torch.uint8,
+                                          device=device).view(E8M0))
+        if scale_atoms is None:
+            scale_atoms = torch.zeros(scale_atom_bytes(dim, inter_dim), dtype=torch.uint8, device=device)
+        self.register_buffer("scale_atoms", scale_atoms, persistent=False)
+        self.register_buffer("_slot0", torch.zeros(1, dtype=torch.int32, device=device), persistent=False)
+        self.register_load_state_dict_post_hook(lambda m, _keys: m.refresh_scale_atoms())
+
+    def refresh_scale_atoms(self, stream=None) -> None:
+        lib = _lib.load()
+        if self.fp4:
+            check(lib.dsv4_build_scale_atoms(ptr(self.block), self.block.numel(), ptr(self._slot0), 1,
+                                             self.dim, self.inter_dim, ptr(self.scale_atoms),
+                                             self.scale_atoms.numel(), stream_ptr(stream)),
+                  "dsv4_build_scale_atoms")
+        else:
+            check(lib.dsv4_build_shared_scale_atoms(ptr(self.w1.scale), ptr(self.w2.scale), ptr(self.w3.scale),
+                                                    self.dim, self.inter_dim, ptr(self.scale_atoms),
+                                                    stream_ptr(stream)),
+                  "dsv4_build_shared_scale_atoms")
+
+    def _desc(self) -> MoELayerDesc:
+        d = MoELayerDesc()
+        d.hidden, d.inter = self.dim, self.inter_dim
+        d.swiglu_limit = self.swiglu_limit
+        d.route_scale = 1.0
+        if self.fp4:
+            d.n_routed, d.topk, d.n_shared = 1, 1, 0
+            d.arena = ptr(self.block)
+            d.slot_stride = _round_up(self.block.numel(), 32) if self.block.numel() % 32 else self.block.numel()
+            d.n_slots = 1
+            d.arena_sf = ptr(self.scale_atoms)
+            d.sf_slot_stride = self.scale_atoms.numel()
+            d.expert_slot = ptr(self._slot0)
+        else:
+            d.n_routed, d.topk, d.n_shared = 0, 1, 1
+            d.shared_w1, d.shared_w2, d.shared_w3 = ptr(self.w1.weight), ptr(self.w2.weight), ptr(self.w3.weight)
+            d.shared_sf = ptr(self.scale_atoms)
+        return d
+
+    def forward(self, x: torch.Tensor, weights: torch.Tensor | None = None) -> torch.Tensor:
+        shape = x.shape
+        x2 = x.reshape(-1, self.dim)
+        if x2.dtype != torch.bfloat16:
+            x2 = x2.to(torch.bfloat16)
+        x2 = x2.contiguous()
+        T = x2.shape[0]
+        y = torch.empty(T, self.dim, dtype=torch.bfloat16, device=x2.device)
+        w = None
+        if weights is not None:
+            w = weights.reshape(-1).to(torch.float32).contiguous()
+            if w.numel() != T:
+                raise RuntimeError("routing weights must have one entry per row")
+        d = self._desc()
+        lib = _lib.load()
+        ws_bytes = lib.dsv4_expert_workspace_bytes(ctypes.byref(d), T)
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x2.device)
+        check(lib.dsv4_expert_forward(ctypes.byref(d), 0 if self.fp4 else -1, ptr(x2), T, ptr(w), ptr(y),
+                                      ptr(ws), ws_bytes, stream_ptr()), "dsv4_expert_forward")
+        return y.view(*shape[:-1], self.dim).to(x.dtype)
+
+
+def _round_up(v: int, m: int) -> int:
+    return (v + m - 1) // m * m
+
+
+# ---------------------------------------------------------------------------
+# ExpertArena: slots of one device buffer
+# ---------------------------------------------------------------------------
+class ExpertArena:
+    """Pool of routed-expert slots in one device buffer.
+
+    Same contract as the reference's ``ExpertArena`` (lazy_official_runtime.py:
+    641-667): ``acquire(factory) -> (expert, reused)`` hands out a slot-backed
+    ``Expert`` (``factory`` is only called when every slot is taken),
+    ``release(expert) -> bool`` returns its slot to the pool.  On B200 the slots
+    are one contiguous allocation, so a layer's resident experts form the
+    arena the grouped GEMM streams (one tensor map over all slots)."""
+
+    def __init__(self, max_slots: int, dim: int = 4096, inter: int = 2048, *, device="cuda",
+                 swiglu_limit: float = 0.0):
+        self.max_slots = max(0, int(max_slots))
+        self.enabled = self.max_slots > 0
+        self.dim, self.inter = dim, inter
+        self.swiglu_limit = swiglu_limit
+        self.block_bytes = packed_block_bytes(dim, inter)
+        self.slot_stride = _round_up(self.block_bytes, 256)
+        self.sf_stride = scale_atom_bytes(dim, inter)
+        self.device = torch.device(device)
+        n = max(self.max_slots, 1)
+        self.buffer = torch.zeros(n * self.slot_stride, dtype=torch.uint8, device=self.device)
+        self.sf = torch.zeros(n * self.sf_stride, dtype=torch.uint8, device=self.device)
+        self._free = list(range(self.max_slots - 1, -1, -1))
+        self._experts: dict[int, Expert] = {}
+        self._released: set[int] = set()
+
+    def slot_storage(self, slot: int) -> tuple[torch.Tensor, torch.Tensor]:
+        s = self.buffer[slot * self.slot_stride:(slot + 1) * self.slot_stride]
+        f = self.sf[slot * self.sf_stride:(slot + 1) * self.sf_stride]
+        return s, f
+
+    def expert_for_slot(self, slot: int) -> Expert:
+        e = self._experts.get(slot)
+        if e is None:
+            s, f = self.slot_storage(slot)
+            e = Expert(self.dim, self.inter, dtype=FP4, swiglu_limit=self.swiglu_limit, storage=s,
+                       scale_atoms=f)
+            e._arena_slot = slot
+            self._experts[slot] = e
+        return e
+
+    def acquire(self, factory=None) -> tuple[nn.Module, bool]:
+        if self.enabled and self._free:
+            slot = self._free.pop()
+            reused = slot in self._released
+            return self.expert_for_slot(slot), reused
+        if factory is None:
+            raise RuntimeError("expert arena is full")
+        return factory(), False
+
+    def release(self, expert: nn.Module) -> bool:
+        slot = getattr(expert, "_arena_slot", None)
+        if not self.enabled or slot is None or slot in self._free:
+            return False
+        self._free.append(slot)
+        self._released.add(slot)
+        return True
+
+    def materialize(self, slab: torch.Tensor, src_offsets: list[int], slots: list[int], *,
+                    bf16_out: torch.Tensor | None = None, stream=None) -> int:
+        """Device-side materializer: packed blocks already in device memory
+        (``slab``, byte offsets ``src_offsets``) -> arena ``slots`` (bit-exact),
+        plus their scale atoms and, optionally, an exact bf16 decode.  Returns the
+        bytes copied (ExpertCopyPlan's copied_bytes)."""
+        n = len(slots)
+        if n == 0:
+            return 0
+        if len(src_offsets) != n:
+            raise RuntimeError("targets and offsets length mismatch")
+        off = torch.tensor(src_offsets, dtype=torch.int64).to(slab.device, non_blocking=True)
+        sl = torch.tensor(slots, dtype=torch.int32).to(slab.device, non_blocking=True)
+        bf16_stride = 0
+        if bf16_out is not None:
+            bf16_stride = bf16_out.shape[-1] if bf16_out.dim() > 1 else bf16_out.numel() // max(self.max_slots, 1)
+        check(_lib.load().dsv4_materialize(ptr(slab), ptr(off), ptr(sl), n, self.dim, self.inter,
+                                           ptr(self.buffer), self.slot_stride, ptr(self.sf), self.sf_stride,
+                                           ptr(bf16_out), bf16_stride, stream_ptr(stream)),
+              "dsv4_materialize")
+        return n * self.block_bytes
+
+
+# ---------------------------------------------------------------------------
+# Gate
+# ---------------------------------------------------------------------------
+class Gate(nn.Module):
+    """Official ``Gate(layer_id, args)``; ``forward(x, input_ids) -> (weights, indices)``.
+
+    Sigmoid scores of ``x . weight^T`` (fp32), selection on score + ``bias``,
+    top-k, weights renormalised to sum 1 and scaled by ``route_scale``
+    (weights fp32 [N,k], indices int64 [N,k])."""
+
+    def __init__(self, layer_id: int, args: ModelArgs, *, device=None):
+        super().__init__()
+        self.layer_id = layer_id
+        self.dim = args.dim
+        self.n_experts = args.n_routed_experts
+        self.topk = args.n_activated_experts
+        self.route_scale = float(args.route_scale)
+        if args.score_func != "sigmoid":
+            raise RuntimeError(f"unsupported score function {args.score_func!r}")
+        device = device or "cuda"
+        self.weight = nn.Parameter(torch.zeros(self.n_experts, self.dim, dtype=args.gate_dtype, device=device),
+                                   requires_grad=False)
+        if args.gate_bias:
+            self.bias = nn.Parameter(torch.zeros(self.n_experts, dtype=torch.float32, device=device),
+                                     requires_grad=False)
+        else:
+            self.register_parameter("bias", None)
+
+    def logits(self, x: torch.Tensor) -> torch.Tensor:
+        x = x.reshape(-1, self.dim).to(torch.bfloat16).contiguous()
+        out = torch.empty(x.shape[0], self.n_experts, dtype=torch.float32, device=x.device)
+        check(_lib.load().dsv4_gate_logits(ptr(x), ptr(self.weight), int(self.weight.dtype == torch.float32),
+                                           x.shape[0], self.dim, self.n_experts, ptr(out), stream_ptr()),
+              "dsv4_gate_logits")
+        return out
+
+    def route(self, logits: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        logits = logits.to(torch.float32).contiguous()
+        T = logits.shape[0]
+        w = torch.empty(T, self.topk, dtype=torch.float32, device=logits.device)
+        idx = torch.empty(T, self.topk, dtype=torch.int64, device=logits.device)
+        check(_lib.load().dsv4_gate_topk(ptr(logits), ptr(self.bias), T, self.n_experts, self.topk,
+                                         self.route_scale, ptr(w), ptr(idx), stream_ptr()),
+              "dsv4_gate_topk")
+        return w, idx
+
+    def forward(self, x: torch.Tensor, input_ids: torch.Tensor | None = None):
+        return self.route(self.logits(x))
+
+
+# ---------------------------------------------------------------------------
+# MoE
+# ---------------------------------------------------------------------------
+class MoE(nn.Module):
+    """``MoE(layer_id, args)``; ``forward(x [B,S,H] bf16, input_ids [B,S]) -> [B,S,H]``.
+
+    Expert ownership follows the reference's expert-parallel split
+    (lazy_official_runtime.py:956-965): rank r of W owns experts
+    [r*E/W, (r+1)*E/W).  With one rank the whole layer is one call of
+    ``dsv4_moe_forward`` (no host synchronisation); with several ranks tokens
+    are dispatched to the owning ranks (see ``spark_b200.ep``)."""
+
+    def __init__(self, layer_id: int, args: ModelArgs, *, device=None, arena: ExpertArena | None = None,
+                 group=None):
+        super().__init__()
+        self.group = group
+        world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        rank = dist.get_rank(group) if dist.is_available() and dist.is_initialized() else 0
+        if args.n_routed_experts % world:
+            raise AssertionError("n_routed_experts must divide evenly across ranks")
+        if args.n_shared_experts != 1:
+            raise AssertionError("exactly one shared expert is supported")
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        device = torch.device(device)
+        self.layer_id = layer_id
+        self.args = args
+        self.dim = args.dim
+        self.world, self.rank = world, rank
+        self.n_routed_experts = args.n_routed_experts
+        self.n_local_experts = args.n_routed_experts // world
+        self.n_activated_experts = args.n_activated_experts
+        self.experts_start_idx = rank * self.n_local_experts
+        self.experts_end_idx = self.experts_start_idx + self.n_local_experts
+        self.gate = Gate(layer_id, args, device=device)
+        self.arena = arena if arena is not None else ExpertArena(
+            self.n_local_experts, args.dim, args.moe_inter_dim, device=device, swiglu_limit=args.swiglu_limit)
+        slots = torch.full((self.n_routed_experts,), 0, dtype=torch.int32)
+        experts = []
+        for i in range(self.n_routed_experts):
+            if self.experts_start_idx <= i < self.experts_end_idx:
+                e, _ = self.arena.acquire()
+                slots[i] = e._arena_slot
+                experts.append(e)
+            else:
+                experts.append(None)
+        self.experts = nn.ModuleList(experts)
+        self.register_buffer("expert_slot", slots.to(device), persistent=False)
+        self.shared_experts = Expert(args.dim, args.moe_inter_dim, swiglu_limit=args.swiglu_limit, device=device)
+        self.register_load_state_dict_post_hook(lambda m, _keys: m.refresh_scale_atoms())
+
+    def refresh_scale_atoms(self) -> None:
+        slots = self.expert_slot[self.experts_start_idx:self.experts_end_idx].contiguous()
+        check(_lib.load().dsv4_build_scale_atoms(ptr(self.arena.buffer), self.arena.slot_stride, ptr(slots),
+                                                 slots.numel(), self.dim, self.args.moe_inter_dim,
+                                                 ptr(self.arena.sf), self.arena.sf_stride, stream_ptr()),
+              "dsv4_build_scale_atoms")
+        self.shared_experts.refresh_scale_atoms()
+
+    def layer_desc(self) -> MoELayerDesc:
+        a = self.args
+        d = MoELayerDesc()
+        d.hidden, d.inter = a.dim, a.moe_inter_dim
+        d.n_routed, d.topk, d.n_shared = a.n_routed_experts, a.n_activated_experts, 1
+        d.route_scale, d.swiglu_limit = float(a.route_scale), float(a.swiglu_limit or 0.0)
+        d.gate_w = ptr(self.gate.weight)
+        d.gate_w_fp32 = int(self.gate.weight.dtype == torch.float32)
+        d.gate_bias = ptr(self.gate.bias)
+        d.arena, d.slot_stride, d.n_slots = ptr(self.arena.buffer), self.arena.slot_stride, max(self.arena.max_slots, 1)
+        d.arena_sf, d.sf_slot_stride = ptr(self.arena.sf), self.arena.sf_stride
+        d.expert_slot = ptr(self.expert_slot)
+        sh = self.shared_experts
+        d.shared_w1, d.shared_w2, d.shared_w3 = ptr(sh.w1.weight), ptr(sh.w2.weight), ptr(sh.w3.weight)
+        d.shared_sf = ptr(sh.scale_atoms)
+        return d
+
+    def workspace_bytes(self, T: int) -> int:
+        d = self.layer_desc()
+        return int(_lib.load().dsv4_moe_workspace_bytes(ctypes.byref(d), T))
+
+    def forward_tokens(self, x: torch.Tensor, *, routing: tuple[torch.Tensor, torch.Tensor] | None = None,
+                       workspace: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Single-rank layer over x [T,H] bf16 -> [T,H] bf16 (no host sync)."""
+        T = x.shape[0]
+        d = self.layer_desc()
+        lib = _lib.load()
+        need = lib.dsv4_moe_workspace_bytes(ctypes.byref(d), T)
+        if workspace is None or workspace.numel() < need:
+            workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device)
+        y = out if out is not None else torch.empty_like(x)
+        rw = ri = None
+        if routing is not None:
+            rw = routing[0].to(torch.float32).contiguous()
+            ri = routing[1].to(torch.int64).contiguous()
+        check(lib.dsv4_moe_forward(ctypes.byref(d), ptr(x), T, ptr(y), ptr(rw), ptr(ri), ptr(workspace),
+                                   workspace.numel(), stream_ptr()), "dsv4_moe_forward")
+        return y
+
+    def forward(self, x: torch.Tensor, input_ids: torch.Tensor | None = None) -> torch.Tensor:
+        shape = x.size()
+        x2 = x.reshape(-1, self.dim)
+        if x2.dtype != torch.bfloat16:
+            x2 = x2.to(torch.bfloat16)
+        x2 = x2.contiguous()
+        if self.world == 1:
+            y = self.forward_tokens(x2)
+        else:
+            from .ep import ep_moe_forward
+
+            y = ep_moe_forward(self, x2)
+        return y.type_as(x).view(shape)

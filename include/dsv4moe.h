@@ -1,0 +1,204 @@
+/*
+ * dsv4moe — B200 (sm_100a) routed-expert MoE hot path of DeepSeek-V4-Flash.
+ *
+ * C ABI of libdsv4moe.so.  Plain pointers and sizes only; every function
+ * returns DSV4_OK (0) or a negative DSV4_ERR_* code and never aborts.  Device
+ * pointers are CUDA global memory of the current device; `stream` is a
+ * cudaStream_t (NULL = legacy default stream).  Kernels are enqueued
+ * asynchronously; errors raised inside a kernel (bounded waits that expired,
+ * out-of-range expert ids) are latched in a device flag read by
+ * dsv4_device_error().
+ *
+ * Reference interfaces replaced (paths inside bigs/deepseek-v4-flash-dgx-spark):
+ *   spark_runtime/lazy_official_runtime.py:946-1002   LazyMoE / official Gate, Expert
+ *   spark_runtime/lazy_official_runtime.py:49-338     PackedExpertStore
+ *   spark_runtime/lazy_official_runtime.py:641-667    ExpertArena
+ *   spark_runtime/native/native_packed_loader.cpp:1-359  read_into, copy plans
+ */
+#ifndef DSV4MOE_H_
+#define DSV4MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DSV4_API __attribute__((visibility("default")))
+#else
+#define DSV4_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define DSV4_OK 0
+#define DSV4_ERR_ARG (-1)         /* invalid argument (TORCH_CHECK failures in the reference) */
+#define DSV4_ERR_CUDA (-2)        /* CUDA runtime / launch error */
+#define DSV4_ERR_UNSUPPORTED (-3) /* shape or option this build does not implement */
+#define DSV4_ERR_IO (-4)          /* pread failed (errno kept in *err_no) */
+#define DSV4_ERR_SHORT_READ (-5)  /* "short packed expert read" */
+#define DSV4_ERR_BOUNDS (-6)      /* "source slice exceeds storage tensor" */
+#define DSV4_ERR_SIZE (-7)        /* "target size does not match expert copy plan" */
+#define DSV4_ERR_WORKSPACE (-8)   /* workspace smaller than dsv4_moe_workspace_bytes() */
+
+/* device-side error codes latched by kernels (read with dsv4_device_error) */
+#define DSV4_DEVERR_TIMEOUT_PRODUCER 101
+#define DSV4_DEVERR_TIMEOUT_MMA 102
+#define DSV4_DEVERR_TIMEOUT_EPILOGUE 103
+#define DSV4_DEVERR_BAD_INDEX 104
+#define DSV4_DEVERR_PLAN_OVERFLOW 105
+
+DSV4_API int dsv4_version(void);
+DSV4_API const char* dsv4_status_string(int status);
+/* Synchronises the device, returns the first device-side error code (0 if
+ * none) in *code, and clears it when clear != 0. */
+DSV4_API int dsv4_device_error(int clear, int* code);
+
+/* ---- MoE layer description ---------------------------------------------
+ * Routed experts live in an expert arena: one device buffer of n_slots slots
+ * of slot_stride bytes; a slot holds one packed expert block, bytes unchanged
+ * from the packed slab (w1.scale, w2.scale, w3.scale, w1.weight, w2.weight,
+ * w3.weight; scripts/build_packed_expert_layout.py:76-86): e2m1x2 weights
+ * [I,H/2], [H,I/2], [I,H/2] and ue8m0 scales per 32 along K.  arena_sf holds
+ * the tensor-memory scale atoms derived from those scales (written by
+ * dsv4_materialize or dsv4_build_scale_atoms), sf_slot_stride = 3*I*H/32.
+ * The shared expert is fp8 e4m3 [I,H], [H,I], [I,H] with 128x128 ue8m0 block
+ * scales; shared_sf holds its atoms (dsv4_build_shared_scale_atoms). */
+typedef struct dsv4_moe_layer {
+  int hidden;          /* H (args.dim) */
+  int inter;           /* I (args.moe_inter_dim) */
+  int n_routed;        /* E (args.n_routed_experts) */
+  int topk;            /* k (args.n_activated_experts) */
+  int n_shared;        /* 0 or 1 (args.n_shared_experts) */
+  float route_scale;   /* routed scaling factor */
+  float swiglu_limit;  /* args.swiglu_limit; <= 0 disables the clamp */
+  const void* gate_w;  /* [E,H] bf16 or fp32 */
+  int gate_w_fp32;     /* 1 if gate_w is fp32 */
+  const float* gate_bias;      /* [E] score-correction bias, or NULL */
+  const uint8_t* arena;        /* routed expert slots */
+  long long slot_stride;       /* bytes per slot (>= packed block bytes, % 32 == 0) */
+  int n_slots;
+  const uint8_t* arena_sf;     /* scale atoms per slot */
+  long long sf_slot_stride;
+  const int* expert_slot;      /* [E] expert id -> slot (device) */
+  const uint8_t* shared_w1;    /* fp8 [I,H] */
+  const uint8_t* shared_w2;    /* fp8 [H,I] */
+  const uint8_t* shared_w3;    /* fp8 [I,H] */
+  const uint8_t* shared_sf;    /* atoms: w1 | w3 | w2, each I*H/32 bytes */
+} dsv4_moe_layer;
+
+/* Bytes of scratch dsv4_moe_forward needs for T tokens (caller allocates). */
+DSV4_API long long dsv4_moe_workspace_bytes(const dsv4_moe_layer* L, int T);
+
+/* Byte offsets inside the workspace of the intermediate buffers, for
+ * inspection: out[0..] = logits, weights, indices, counts, seg_start,
+ * n_tiles, route_slot, slot_token, slot_weight, tiles, xq, xsf, hq, hsf, O.
+ * Also returns max_rows in out[15] and block_n in out[16]. n_out >= 17. */
+DSV4_API int dsv4_moe_workspace_layout(const dsv4_moe_layer* L, int T, long long* out, int n_out);
+
+/* LazyMoE.forward(x, input_ids) (spark_runtime/lazy_official_runtime.py:980-1002)
+ * for one layer on one GPU: gate -> route plan -> permute+act_quant ->
+ * grouped GEMM1 (w1|w3, SwiGLU, x routing weight, fp8 re-quant) -> grouped
+ * GEMM2 (w2) -> ordered combine + shared expert -> bf16 y [T,H].
+ * x: bf16 [T,H].  If routing_weights/routing_indices are non-NULL they
+ * replace the gate (fp32 [T,k], int64 [T,k]).  No host synchronisation. */
+DSV4_API int dsv4_moe_forward(const dsv4_moe_layer* L, const void* x, int T, void* y,
+                     const float* routing_weights, const int64_t* routing_indices,
+                     void* workspace, long long workspace_bytes, void* stream);
+
+/* Official Expert.forward(x, weights) (constructed at
+ * lazy_official_runtime.py:769-774 routed, :976-978 shared; called at :998,
+ * :1001) for one expert over T rows: act_quant -> w1|w3 -> SwiGLU (clamp at
+ * swiglu_limit) -> x row_weights[r] (if non-NULL) -> bf16 -> act_quant -> w2
+ * -> bf16 y [T,H].  expert >= 0 selects routed expert `expert` of the arena
+ * (via expert_slot); expert < 0 selects the fp8 shared expert. */
+DSV4_API long long dsv4_expert_workspace_bytes(const dsv4_moe_layer* L, int T);
+DSV4_API int dsv4_expert_forward(const dsv4_moe_layer* L, int expert, const void* x, int T,
+                                 const float* row_weights, void* y, void* workspace,
+                                 long long workspace_bytes, void* stream);
+
+/* Stage timing of dsv4_moe_forward (no counterpart in the reference; its
+ * telemetry timer is spark_runtime/telemetry.py:98-117): while enabled, every
+ * forward records library-owned CUDA events between its kernels (as graph
+ * nodes when the stream is being captured).  dsv4_profile_read waits for the
+ * last forward and returns 6 durations in ms: gate, plan, permute, GEMM1,
+ * GEMM2, combine. */
+DSV4_API int dsv4_profile_enable(int enable);
+DSV4_API int dsv4_profile_read(float* stage_ms, int n);
+
+/* ---- individual stages (same kernels as dsv4_moe_forward) --------------- */
+
+/* Official Gate logits: logits[T,E] = x[T,H] . Wg[E,H]^T in fp32. */
+DSV4_API int dsv4_gate_logits(const void* x, const void* w, int w_is_fp32, int T, int H, int E,
+                     float* logits, void* stream);
+
+/* Official Gate scoring (lazy_official_runtime.py:966,983): sigmoid scores,
+ * + bias for selection, top-k (ties -> lower id), weights = scores at the
+ * chosen ids renormalised to sum 1, x route_scale.  Bit-exact fp32. */
+DSV4_API int dsv4_gate_topk(const float* logits, const float* bias, int T, int E, int topk,
+                   float route_scale, float* weights, int64_t* indices, void* stream);
+
+/* Official kernel.act_quant(x, 128, "ue8m0") (scripts/smoke_official_kernels.py:
+ * 44-49): bf16 [M,K] -> e4m3 codes [M,K] + ue8m0 scales [M,K/128]. */
+DSV4_API int dsv4_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* scale, void* stream);
+
+/* ---- expert arena / materializer ---------------------------------------
+ * LazyRoutedExpert.materialize + ExpertCopyPlan::read_into_and_copy_cuda
+ * (lazy_official_runtime.py:761-917; native_packed_loader.cpp:122-174,281-316),
+ * device side: blocks already in device memory (slab + src_off[i]) are copied
+ * into arena slots dst_slot[i] (bit-exact), their scale atoms written to
+ * arena_sf, and (if bf16_out != NULL) their weights decoded exactly to bf16
+ * ([I,H], [H,I], [I,H] in packed order w1, w2, w3 per slot).  Any of arena,
+ * arena_sf, bf16_out may be NULL to skip that output.  src_off (int64) and
+ * dst_slot (int32) are device arrays of length n; src_off % 16 == 0. */
+DSV4_API int dsv4_materialize(const uint8_t* slab, const long long* src_off, const int* dst_slot, int n,
+                     int hidden, int inter, uint8_t* arena, long long slot_stride,
+                     uint8_t* arena_sf, long long sf_slot_stride, void* bf16_out,
+                     long long bf16_slot_stride, void* stream);
+
+/* Scale atoms for arena slots whose bytes are already in place
+ * (slots[i] of n, device int32 array). */
+DSV4_API int dsv4_build_scale_atoms(const uint8_t* arena, long long slot_stride, const int* slots, int n,
+                           int hidden, int inter, uint8_t* arena_sf, long long sf_slot_stride,
+                           void* stream);
+
+/* Scale atoms for the fp8 shared expert (128x128 block scales w1/w3 [I/128,H/128],
+ * w2 [H/128,I/128]) into shared_sf (3*I*H/32 bytes: w1 | w3 | w2). */
+DSV4_API int dsv4_build_shared_scale_atoms(const uint8_t* w1_scale, const uint8_t* w2_scale,
+                                  const uint8_t* w3_scale, int hidden, int inter,
+                                  uint8_t* shared_sf, void* stream);
+
+/* ---- packed-slab loader (host) -------------------------------------------
+ * native_packed_loader.cpp:26-68 read_into: EINTR-safe pread loop of up to
+ * `size` bytes at `offset` into dst (host memory).  Returns the byte count
+ * (short at EOF) in *read_bytes.  errno of a failed pread in *err_no. */
+DSV4_API int dsv4_read_into(int fd, void* dst, long long dst_capacity, long long size, long long offset,
+                   long long* read_bytes, int* err_no);
+
+/* native_packed_loader.cpp:70-190 copy_storage_to_tensors[_cuda] and
+ * ExpertCopyPlan::copy_storage_to_tensors[_cuda]: copies slices
+ * storage[offsets[i] : offsets[i]+target_bytes[i]] to targets[i].
+ * expected_sizes (plan sizes) may be NULL.  to_device: 0 = host memcpy,
+ * 1 = cudaMemcpyAsync host->device on `stream`, one per target.
+ * The sum of copied bytes is returned in *copied. */
+DSV4_API int dsv4_copy_slices(const void* storage, long long storage_bytes, void* const* targets,
+                     const long long* target_bytes, const long long* offsets,
+                     const long long* expected_sizes, int n, int to_device, void* stream,
+                     long long* copied);
+
+/* ExpertCopyPlan::read_into_and_copy[_cuda] (native_packed_loader.cpp:232-316):
+ * read `size` bytes at `offset` into staging, fail with DSV4_ERR_SHORT_READ
+ * on a short read, then copy the planned slices.  Timings in seconds. */
+DSV4_API int dsv4_read_into_and_copy(int fd, void* staging, long long staging_capacity, long long size,
+                            long long offset, void* const* targets, const long long* target_bytes,
+                            const long long* offsets, const long long* expected_sizes, int n,
+                            int to_device, void* stream, long long* read_bytes,
+                            long long* copied_bytes, double* read_seconds, double* copy_seconds,
+                            int* err_no);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSV4MOE_H_ */

@@ -1,0 +1,273 @@
+"""GPU parity of every stage of the MoE hot path against the CPU oracle.
+
+Bars: integer / byte / index results bit-exact; floating point within
+max|err| <= 2e-2 * rms(reference) (the bf16-accumulation tolerance of the
+benchmark statement), and the canonical-sigmoid routing bit-exact on identical
+logits.
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-2  # max |err| relative to the reference RMS
+
+
+def _lib():
+    from spark_b200 import _lib
+
+    return _lib
+
+
+def _rel_err(got, ref):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    rms = np.sqrt(np.mean(ref ** 2)) + 1e-30
+    return float(np.max(np.abs(got - ref)) / rms)
+
+
+def _bf16_np(t: torch.Tensor) -> np.ndarray:
+    return t.detach().float().cpu().numpy()
+
+
+def _no_device_error():
+    _lib().raise_on_device_error()
+
+
+# ---------------------------------------------------------------------------
+# act_quant
+# ---------------------------------------------------------------------------
+def test_act_quant_bit_exact(cuda_device):
+    L = _lib()
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(67, 1024, generator=g).to(torch.bfloat16)
+    x[0, :128] = 0
+    x[1, :128] = 0
+    x[1, 3] = 3.5                      # amax = 448 * 2^-7 exactly
+    x[2, 128:256] = -0.0
+    x[3, 256:384] *= 1e-30             # tiny values
+    x[4, 384:512] = 1.75 * 2 ** 10     # exact power-of-two ratio
+    xd = x.to(cuda_device)
+    q = torch.empty(67, 1024, dtype=torch.uint8, device=cuda_device)
+    s = torch.empty(67, 8, dtype=torch.uint8, device=cuda_device)
+    L.check(L.load().dsv4_act_quant(L.ptr(xd), 67, 1024, L.ptr(q), L.ptr(s), L.stream_ptr()))
+    torch.cuda.synchronize()
+    qo, so = O.act_quant(x.float().numpy())
+    assert np.array_equal(s.cpu().numpy(), so)
+    assert np.array_equal(q.cpu().numpy(), qo)
+
+
+# ---------------------------------------------------------------------------
+# gate
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("E,k,T", [(16, 4, 4), (256, 6, 64), (256, 6, 513)])
+def test_gate_topk_bit_exact(cuda_device, E, k, T):
+    L = _lib()
+    g = torch.Generator().manual_seed(E * 1000 + T)
+    logits = torch.randn(T, E, generator=g) * 1.5
+    logits[0, :] = 0.0                        # full tie: lowest ids win
+    logits[1, 5] = logits[1, 9] = 3.0         # pairwise tie
+    bias = (torch.rand(E, generator=g) - 0.5) * 0.2
+    ld, bd = logits.to(cuda_device), bias.to(cuda_device)
+    w = torch.empty(T, k, device=cuda_device)
+    idx = torch.empty(T, k, dtype=torch.int64, device=cuda_device)
+    L.check(L.load().dsv4_gate_topk(L.ptr(ld), L.ptr(bd), T, E, k, 2.5, L.ptr(w), L.ptr(idx), L.stream_ptr()))
+    torch.cuda.synchronize()
+    wo, io = O.route_from_logits(logits.numpy(), bias.numpy(), k, 2.5)
+    assert np.array_equal(idx.cpu().numpy(), io)
+    assert np.array_equal(w.cpu().numpy().view(np.uint32), wo.view(np.uint32))
+
+
+@pytest.mark.parametrize("fp32", [True, False])
+def test_gate_logits(cuda_device, fp32):
+    L = _lib()
+    g = torch.Generator().manual_seed(11)
+    T, H, E = 40, 4096, 256
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    w = torch.randn(E, H, generator=g) * 0.02
+    w = w if fp32 else w.to(torch.bfloat16)
+    out = torch.empty(T, E, device=cuda_device)
+    xd, wd = x.to(cuda_device), w.to(cuda_device)
+    L.check(L.load().dsv4_gate_logits(L.ptr(xd), L.ptr(wd), int(fp32), T, H, E, L.ptr(out), L.stream_ptr()))
+    torch.cuda.synchronize()
+    ref = O.gate_logits(x.float().numpy(), w.float().numpy())
+    err = np.abs(out.cpu().numpy() - ref)
+    scale = np.abs(x.float().numpy()) @ np.abs(w.float().numpy()).T
+    assert np.all(err <= 1e-6 * scale + 1e-7), float((err / scale).max())
+
+
+# ---------------------------------------------------------------------------
+# experts
+# ---------------------------------------------------------------------------
+def _routed_expert(H, I, seed, device):
+    from spark_b200.moe import Expert, FP4, packed_block_bytes
+    from spark_b200.synthetic import routed_blocks
+
+    blk = routed_blocks(1, H, I, seed)[0]
+    e = Expert(H, I, dtype=FP4, swiglu_limit=10.0, device=device)
+    e.block[: packed_block_bytes(H, I)].copy_(blk.to(device))
+    e.refresh_scale_atoms()
+    return e, O.expert_from_block(blk.numpy(), H, I)
+
+
+@pytest.mark.parametrize("H,I,T", [(1024, 512, 4), (1024, 512, 37), (4096, 2048, 1), (4096, 2048, 200)])
+def test_routed_expert_fp4(cuda_device, H, I, T):
+    e, ew = _routed_expert(H, I, 100 + T, cuda_device)
+    g = torch.Generator().manual_seed(T)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    rw = torch.rand(T, generator=g) + 0.25
+    y = e(x.to(cuda_device), rw.to(cuda_device)[:, None])
+    torch.cuda.synchronize()
+    _no_device_error()
+    ref = O.expert_forward(x.float().numpy(), ew, rw.numpy(), 10.0)
+    err = _rel_err(_bf16_np(y), ref)
+    assert err <= TOL, err
+
+
+@pytest.mark.parametrize("H,I,T", [(1024, 512, 4), (4096, 2048, 70)])
+def test_shared_expert_fp8(cuda_device, H, I, T):
+    from spark_b200.moe import Expert
+    from spark_b200.synthetic import shared_expert
+
+    sh = shared_expert(H, I, 5 + T)
+    e = Expert(H, I, swiglu_limit=10.0, device=cuda_device)
+    with torch.no_grad():
+        for n in ("w1", "w2", "w3"):
+            getattr(e, n).weight.view(torch.uint8).copy_(sh[f"{n}.weight"].to(cuda_device))
+            getattr(e, n).scale.view(torch.uint8).copy_(sh[f"{n}.scale"].to(cuda_device))
+    e.refresh_scale_atoms()
+    g = torch.Generator().manual_seed(T)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    y = e(x.to(cuda_device))
+    torch.cuda.synchronize()
+    _no_device_error()
+    ref = O.expert_forward(x.float().numpy(), O.shared_from_tensors({k: v.numpy() for k, v in sh.items()}),
+                           None, 10.0)
+    err = _rel_err(_bf16_np(y), ref)
+    assert err <= TOL, err
+
+
+# ---------------------------------------------------------------------------
+# materializer
+# ---------------------------------------------------------------------------
+def test_materialize_bit_exact(cuda_device):
+    from spark_b200.moe import ExpertArena, packed_block_bytes
+    from spark_b200.synthetic import routed_blocks
+
+    H, I, n = 1024, 512, 6
+    blocks = routed_blocks(n, H, I, 42)
+    arena = ExpertArena(8, H, I, device=cuda_device)
+    slab = blocks.to(cuda_device).reshape(-1)
+    nb = packed_block_bytes(H, I)
+    slots = [7, 0, 3, 5, 1, 2]
+    bf16 = torch.zeros(8, 3 * H * I, dtype=torch.bfloat16, device=cuda_device)
+    copied = arena.materialize(slab, [i * nb for i in range(n)], slots, bf16_out=bf16)
+    torch.cuda.synchronize()
+    assert copied == n * nb
+    buf = arena.buffer.cpu().numpy()
+    sf = arena.sf.cpu().numpy()
+    bfn = bf16.view(torch.int16).cpu().numpy().view(np.uint16)
+    for i, s in enumerate(slots):
+        blk = blocks[i].numpy()
+        assert np.array_equal(buf[s * arena.slot_stride: s * arena.slot_stride + nb], blk)
+        p = O.materialize_block(blk, H, I)
+        ref_sf = np.concatenate([O.sf_atoms(p["w1.scale"].reshape(I, H // 32)),
+                                 O.sf_atoms(p["w3.scale"].reshape(I, H // 32)),
+                                 O.sf_atoms(p["w2.scale"].reshape(H, I // 32))])
+        assert np.array_equal(sf[s * arena.sf_stride:(s + 1) * arena.sf_stride], ref_sf)
+        dec = O.decode_block_bf16(blk, H, I)
+        ref_bf = np.concatenate([dec["w1"].reshape(-1), dec["w2"].reshape(-1), dec["w3"].reshape(-1)])
+        assert np.array_equal(bfn[s], ref_bf)
+
+
+def test_shared_scale_atoms(cuda_device):
+    from spark_b200.moe import Expert
+    from spark_b200.synthetic import shared_expert
+
+    H, I = 1024, 512
+    sh = shared_expert(H, I, 3)
+    e = Expert(H, I, device=cuda_device)
+    with torch.no_grad():
+        for n in ("w1", "w2", "w3"):
+            getattr(e, n).scale.view(torch.uint8).copy_(sh[f"{n}.scale"].to(cuda_device))
+    e.refresh_scale_atoms()
+    ref = np.concatenate([O.sf_atoms_fp8(sh["w1.scale"].numpy(), I, H), O.sf_atoms_fp8(sh["w3.scale"].numpy(), I, H),
+                          O.sf_atoms_fp8(sh["w2.scale"].numpy(), H, I)])
+    assert np.array_equal(e.scale_atoms.cpu().numpy(), ref)
+
+
+# ---------------------------------------------------------------------------
+# full layer
+# ---------------------------------------------------------------------------
+def _layer_ws(moe, T):
+    from spark_b200 import _lib as L
+
+    d = moe.layer_desc()
+    offs = (ctypes.c_longlong * 17)()
+    L.check(L.load().dsv4_moe_workspace_layout(ctypes.byref(d), T, offs, 17))
+    return list(offs)
+
+
+def _oracle_weights(layer, experts):
+    cfg = layer["cfg"]
+    mw = O.MoEWeights(
+        gate_w=layer["gate_w"].float().cpu().numpy(), gate_bias=layer["gate_bias"].cpu().numpy(),
+        experts={e: O.expert_from_block(layer["blocks"][e].cpu().numpy(), cfg.dim, cfg.inter) for e in experts},
+        shared=O.shared_from_tensors({k: v.cpu().numpy() for k, v in layer["shared"].items()}),
+        topk=cfg.topk, route_scale=cfg.route_scale, swiglu_limit=cfg.swiglu_limit)
+    return mw
+
+
+@pytest.mark.parametrize("name,T", [("cpu_ref", 4), ("cpu_ref", 300), ("decode", 1), ("decode", 8)])
+def test_moe_layer(cuda_device, name, T):
+    from spark_b200.synthetic import CONFIGS, build_moe, make_layer
+
+    cfg = CONFIGS[name].with_tokens(T)
+    layer = make_layer(cfg, seed=0, device="cpu")
+    moe = build_moe(layer, device=cuda_device)
+    x = layer["x"].to(cuda_device)
+    ws = torch.empty(moe.workspace_bytes(T), dtype=torch.uint8, device=cuda_device)
+    y = moe.forward_tokens(x, workspace=ws)
+    torch.cuda.synchronize()
+    _no_device_error()
+    offs = _layer_ws(moe, T)
+    k, E = cfg.topk, cfg.n_routed
+    logits = ws[offs[0]:offs[0] + T * E * 4].view(torch.float32).view(T, E).cpu().numpy()
+    w_gpu = ws[offs[1]:offs[1] + T * k * 4].view(torch.float32).view(T, k).cpu().numpy()
+    i_gpu = ws[offs[2]:offs[2] + T * k * 8].view(torch.int64).view(T, k).cpu().numpy()
+    # gate: logits within fp32 accumulation error; routing bit-exact on the device's logits
+    ref_logits = O.gate_logits(layer["x"].float().numpy(), layer["gate_w"].float().numpy())
+    assert np.max(np.abs(logits - ref_logits)) < 1e-4
+    w_ref, i_ref = O.route_from_logits(logits, layer["gate_bias"].numpy(), k, cfg.route_scale)
+    assert np.array_equal(i_gpu, i_ref)
+    assert np.array_equal(w_gpu.view(np.uint32), w_ref.view(np.uint32))
+    # routing plan: per-expert counts are the bincount of the indices
+    counts = ws[offs[3]:offs[3] + (E + 1) * 4].view(torch.int32).cpu().numpy()
+    assert np.array_equal(counts[:E], np.bincount(i_gpu.reshape(-1), minlength=E))
+    assert counts[E] == T
+    # layer output on the device's routing
+    experts = sorted(set(i_gpu.reshape(-1).tolist()))
+    mw = _oracle_weights(layer, experts)
+    y_ref = O.moe_forward(layer["x"].float().numpy(), mw, routing=(w_gpu, i_gpu))[0]
+    err = _rel_err(_bf16_np(y), y_ref)
+    assert err <= TOL, err
+
+
+def test_moe_module_forward_shape_and_dtype(cuda_device):
+    from spark_b200.synthetic import CONFIGS, build_moe, make_layer
+
+    cfg = CONFIGS["cpu_ref"].with_tokens(6)
+    layer = make_layer(cfg, seed=1)
+    moe = build_moe(layer, device=cuda_device)
+    x = layer["x"].view(2, 3, cfg.dim).to(cuda_device)
+    ids = torch.arange(6, device=cuda_device).view(2, 3)
+    y = moe(x, ids)
+    assert y.shape == x.shape and y.dtype == torch.bfloat16
+    w, idx = moe.gate(x.view(-1, cfg.dim), ids.view(-1))
+    assert w.shape == (6, cfg.topk) and idx.dtype == torch.int64
