@@ -23,6 +23,7 @@ the max over ranks.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -51,6 +52,8 @@ def _parse():
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--experts", type=int, default=None,
+                   help="routed experts per layer (default: the workload's 256); profiling runs use fewer")
     return p.parse_args()
 
 
@@ -153,6 +156,10 @@ def run_ours(args, world, rank, local):
 
     dev = torch.device("cuda", local)
     base = CONFIGS[args.workload]
+    if args.experts:
+        from dataclasses import replace as _replace
+
+        base = _replace(base, n_routed=args.experts)
     T = args.tokens or (64 if args.workload == "decode" else base.tokens)
     cfg = base.with_tokens(T)
     layer = make_layer(cfg, seed=args.seed + 1000 * rank, device=dev)
@@ -184,16 +191,16 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize()
 
     # touched experts of this batch (for the algorithmic-bytes count)
-    offs = (__import__("ctypes").c_longlong * 17)()
+    offs = (ctypes.c_longlong * 17)()
     d = moe.layer_desc()
-    lib.dsv4_moe_workspace_layout(__import__("ctypes").byref(d), T, offs, 17)
+    lib.dsv4_moe_workspace_layout(ctypes.byref(d), T, offs, 17)
     counts = ws[offs[3]:offs[3] + (cfg.n_routed + 1) * 4].view(torch.int32)[: cfg.n_routed]
     touched = int((counts > 0).sum())
     rows = int(counts.sum()) + T
 
     # timed region
     stage = torch.zeros(6, dtype=torch.float64)
-    buf = (__import__("ctypes").c_float * 6)()
+    buf = (ctypes.c_float * 6)()
     times = []
     clocks = ClockSampler(local)
     if world > 1:
@@ -247,6 +254,8 @@ def run_ours(args, world, rank, local):
         e2e_ms = float(t.item())
 
     peaks, peak_src = _peaks()
+    if min(stage_ms) < 0:
+        raise RuntimeError(f"stage timing events were not recorded: {stage_ms}")
     gemm_ms = stage_ms[3] + stage_ms[4]
     if args.workload == "decode":
         alg = algorithmic_decode_bytes(cfg, touched, T)
@@ -330,25 +339,31 @@ def _sweep(args, local):
 # CPU arm: the oracle restatement of the reference's layer on the host cores
 # ---------------------------------------------------------------------------
 def cpu_layer_rate(cfg_name: str, sample_tokens: int, seed: int, threads: int | None = None):
-    """tokens/s of the oracle layer (numpy) on a bounded sample of tokens."""
+    """tokens/s of the oracle layer (numpy, fp32/fp64 over the e2m1/e4m3 codes)
+    on a bounded sample of tokens.  Only the experts the sample touches are
+    generated (outside the timed region); the timed region is gate + experts +
+    combine, including the per-step decode of the FP4/FP8 weights."""
     import numpy as np
     import torch
 
     from oracle import moe_oracle as O
-    from spark_b200.synthetic import CONFIGS, make_layer
+    from spark_b200.synthetic import CONFIGS, routed_blocks, shared_expert
 
     if threads:
         torch.set_num_threads(threads)
     cfg = CONFIGS[cfg_name].with_tokens(sample_tokens)
-    layer = make_layer(cfg, seed=seed, device="cpu")
-    x = layer["x"].float().numpy()
-    gw = layer["gate_w"].float().numpy()
-    blocks = layer["blocks"].numpy()
-    sh = O.shared_from_tensors({k: v.numpy() for k, v in layer["shared"].items()})
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(sample_tokens, cfg.dim, generator=g).to(torch.bfloat16).float().numpy()
+    gw = (torch.randn(cfg.n_routed, cfg.dim, generator=g) * cfg.gate_std).to(torch.bfloat16).float().numpy()
+    bias = np.zeros(cfg.n_routed, np.float32)
+    logits = O.gate_logits(x, gw)
+    _, idx0 = O.route_from_logits(logits, bias, cfg.topk, cfg.route_scale)
+    blocks = {int(e): routed_blocks(1, cfg.dim, cfg.inter, seed * 1000 + int(e))[0].numpy() for e in np.unique(idx0)}
+    sh_t = {k: v.numpy() for k, v in shared_expert(cfg.dim, cfg.inter, seed + 31).items()}
     t0 = time.perf_counter()
-    wts, idx, _ = O.gate_forward(x, gw, layer["gate_bias"].numpy(), cfg.topk, cfg.route_scale)
-    experts = {int(e): O.expert_from_block(blocks[int(e)], cfg.dim, cfg.inter) for e in np.unique(idx)}
-    mw = O.MoEWeights(gate_w=gw, gate_bias=layer["gate_bias"].numpy(), experts=experts, shared=sh,
+    wts, idx, _ = O.gate_forward(x, gw, bias, cfg.topk, cfg.route_scale)
+    experts = {e: O.expert_from_block(b, cfg.dim, cfg.inter) for e, b in blocks.items()}
+    mw = O.MoEWeights(gate_w=gw, gate_bias=bias, experts=experts, shared=O.shared_from_tensors(sh_t),
                       topk=cfg.topk, route_scale=cfg.route_scale, swiglu_limit=cfg.swiglu_limit)
     O.moe_forward(x, mw, routing=(wts, idx))
     dt = time.perf_counter() - t0
@@ -363,7 +378,7 @@ def run_reference(args, world, rank):
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     T = args.tokens or (64 if args.workload == "decode" else 8192)
-    sample = 8 if args.workload == "decode" else 32
+    sample = 1 if args.workload == "decode" else 8
     rates = []
     for i in range(args.warmup + args.steps):
         r, _ = cpu_layer_rate(args.workload, sample, args.seed + i, threads)
@@ -401,11 +416,11 @@ def main():
             except Exception as exc:  # keep the headline line even if a sweep case fails
                 res["sweep"] = {"error": repr(exc)}
         if not args.no_cpu_baseline:
-            rate, dt = cpu_layer_rate(args.workload, 8 if args.workload == "decode" else 32, args.seed,
-                                      os.cpu_count())
+            n = 4 if args.workload == "decode" else 8
+            rate, dt = cpu_layer_rate(args.workload, n, args.seed, os.cpu_count())
             res["cpu_baseline"] = {"value": round(rate, 3), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-                                   "sample": f"{8 if args.workload == 'decode' else 32} tokens of the "
-                                             f"{args.workload} layer, {dt:.1f} s (oracle restatement)"}
+                                   "sample": f"{n} tokens of the {args.workload} layer, {dt:.1f} s "
+                                             "(oracle restatement, numpy)"}
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:

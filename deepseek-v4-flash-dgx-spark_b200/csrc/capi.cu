@@ -1,9 +1,22 @@
 // extern "C" entry points of libdsv4moe.so (declared in include/dsv4moe.h).
 #include <stdio.h>
+#include <stdlib.h>
 
 #include "kernels.cuh"
 
 namespace dsv4 {
+
+// Tuning knobs of the grouped GEMM, read once from the environment:
+// DSV4_GEMM_L2PROMO = L2 promotion of the weight tensor maps in bytes (0/64/128/256).
+static int env_int(const char* name, int dflt, int lo, int hi) {
+  const char* e = getenv(name);
+  int v = e ? atoi(e) : dflt;
+  return v < lo ? lo : (v > hi ? hi : v);
+}
+static int gemm_l2promo() {
+  static const int v = env_int("DSV4_GEMM_L2PROMO", 256, 0, 256);
+  return v;
+}
 
 // The library links the CUDA runtime statically, so it keeps its own notion of
 // the current device: bind it to the device that owns the caller's buffers.
@@ -54,6 +67,9 @@ struct Plan {
 static long long align256(long long v) { return (v + 255) & ~255LL; }
 
 static int choose_block_n(int T, int k, int E) {
+  // tuning override: DSV4_BLOCK_N = 32 | 64 | 128
+  static const int forced = env_int("DSV4_BLOCK_N", 0, 0, 128);
+  if (forced == 32 || forced == 64 || forced == 128) return forced;
   // rows per routed expert on average; small segments waste less with N = 32
   const long long avg = (long long)T * k / (E > 0 ? E : 1);
   if (avg <= 16 && T <= 256) return 32;
@@ -63,10 +79,12 @@ static int choose_block_n(int T, int k, int E) {
 
 static int validate(const dsv4_moe_layer* L) {
   if (!L) return DSV4_ERR_ARG;
-  if (L->hidden <= 0 || L->inter <= 0 || L->hidden % 128 || L->inter % 128) return DSV4_ERR_ARG;
+  // the k-packed activation scale atoms cover four 128-wide k tiles
+  if (L->hidden <= 0 || L->inter <= 0 || L->hidden % 512 || L->inter % 512) return DSV4_ERR_ARG;
   if (L->n_routed <= 0 || L->n_routed > 512) return DSV4_ERR_UNSUPPORTED;
   if (L->topk <= 0 || L->topk > 8 || L->topk > L->n_routed) return DSV4_ERR_UNSUPPORTED;
   if (L->n_shared != 0 && L->n_shared != 1) return DSV4_ERR_UNSUPPORTED;
+  if (L->gate_w && L->hidden > 8192) return DSV4_ERR_UNSUPPORTED;
   return DSV4_OK;
 }
 
@@ -95,9 +113,9 @@ static Plan make_plan(const dsv4_moe_layer* L, int T) {
       (long long)p.max_rows * 4,              // slot_weight
       (long long)p.max_tiles * 16,            // tiles
       (long long)p.max_rows * p.H,            // xq
-      atom_groups * (p.H / 128) * 512,        // xsf
+      atom_groups * (p.H / 512) * 512,        // xsf (k-packed: 4 k tiles per atom)
       (long long)p.max_rows * p.I,            // hq
-      atom_groups * (p.I / 128) * 512,        // hsf
+      atom_groups * (p.I / 512) * 512,        // hsf
       (long long)p.max_rows * p.H * 2,        // O
   };
   long long o = 0;
@@ -128,9 +146,9 @@ static int run_expert_gemms(const dsv4_moe_layer* L, const int4* tiles, const in
   CUtensorMap a0, a1, s0, s1, b;
   // GEMM1: w1 | w3 over xq
   if (has_routed) {
-    if ((rc = make_tmap_fp4_arena(&a0, L->arena + w1_off, H, I, L->n_slots, L->slot_stride)))
+    if ((rc = make_tmap_fp4_arena(&a0, L->arena + w1_off, H, I, L->n_slots, L->slot_stride, gemm_l2promo())))
       return rc;
-    if ((rc = make_tmap_fp4_arena(&a1, L->arena + w3_off, H, I, L->n_slots, L->slot_stride)))
+    if ((rc = make_tmap_fp4_arena(&a1, L->arena + w3_off, H, I, L->n_slots, L->slot_stride, gemm_l2promo())))
       return rc;
   }
   if (has_shared) {
@@ -172,7 +190,7 @@ static int run_expert_gemms(const dsv4_moe_layer* L, const int4* tiles, const in
 
   // GEMM2: w2 over hq
   if (has_routed) {
-    if ((rc = make_tmap_fp4_arena(&a0, L->arena + w2_off, I, H, L->n_slots, L->slot_stride)))
+    if ((rc = make_tmap_fp4_arena(&a0, L->arena + w2_off, I, H, L->n_slots, L->slot_stride, gemm_l2promo())))
       return rc;
   }
   if (has_shared) {
@@ -183,7 +201,7 @@ static int run_expert_gemms(const dsv4_moe_layer* L, const int4* tiles, const in
   if ((rc = make_tmap_u8(&b, hq, I, max_rows, block_n))) return rc;
   GemmArgs g2 = g1;
   g2.kt_count = I / 128;
-  g2.nb_count = H / 128;
+  g2.nb_count = H / 256;
   g2.sf_off0 = 2 * sc;
   g2.sf_off1 = 2 * sc;
   g2.sf_shared0 = L->shared_sf ? L->shared_sf + 2 * sc : nullptr;
@@ -219,9 +237,9 @@ static ExpertPlan make_expert_plan(const dsv4_moe_layer* L, int T) {
       (long long)p.rows_pad * 4,                 // slot_weight
       (long long)p.max_tiles * 16,               // tiles
       (long long)p.rows_pad * L->hidden,         // xq
-      groups * (L->hidden / 128) * 512,          // xsf
+      groups * (L->hidden / 512) * 512,          // xsf
       (long long)p.rows_pad * L->inter,          // hq
-      groups * (L->inter / 128) * 512,           // hsf
+      groups * (L->inter / 512) * 512,           // hsf
   };
   long long o = 0;
   for (int i = 0; i < 8; ++i) {
@@ -313,7 +331,7 @@ int dsv4_gate_logits(const void* x, const void* w, int w_is_fp32, int T, int H, 
                      float* logits, void* stream) {
   if (!x || !w || !logits || T < 0 || H <= 0 || H % 8 || E <= 0) return DSV4_ERR_ARG;
   if (T == 0) return DSV4_OK;
-  if ((size_t)4 * H * sizeof(float) > 200 * 1024) return DSV4_ERR_UNSUPPORTED;
+  if (H > 8192) return DSV4_ERR_UNSUPPORTED;  // gate rows are staged in shared memory
   bind_device(logits);
   return launch_gate_logits(x, w, w_is_fp32, T, H, E, logits, static_cast<cudaStream_t>(stream));
 }
@@ -383,9 +401,11 @@ int dsv4_moe_forward(const dsv4_moe_layer* L, const void* x, int T, void* y,
   if ((rc = launch_route_plan(ri, rw, T, k, E, p.S, p.block_n, p.max_rows, p.max_tiles, counts,
                               seg_start, route_slot, slot_token, slot_weight, tiles, n_tiles, st)))
     return rc;
+  stage_mark(2, st);
   if ((rc = launch_permute_quant(x, H, slot_token, seg_start + E + 1, p.max_rows, xq, xsf, nsm,
                                  st)))
     return rc;
+  stage_mark(3, st);
 
   if ((rc = run_expert_gemms(L, tiles, n_tiles, slot_weight, xq, xsf, hq, hsf, O, H, p.max_rows,
                              p.max_tiles, p.block_n, L->expert_slot, L->n_routed, nsm, st)))
@@ -396,14 +416,14 @@ int dsv4_moe_forward(const dsv4_moe_layer* L, const void* x, int T, void* y,
 }
 
 long long dsv4_expert_workspace_bytes(const dsv4_moe_layer* L, int T) {
-  if (!L || L->hidden % 128 || L->inter % 128 || T < 0) return -1;
+  if (!L || L->hidden % 512 || L->inter % 512 || T < 0) return -1;
   return make_expert_plan(L, T).total;
 }
 
 int dsv4_expert_forward(const dsv4_moe_layer* L, int expert, const void* x, int T,
                         const float* row_weights, void* y, void* workspace,
                         long long workspace_bytes, void* stream) {
-  if (!L || !x || !y || T < 0 || L->hidden % 128 || L->inter % 128) return DSV4_ERR_ARG;
+  if (!L || !x || !y || T < 0 || L->hidden % 512 || L->inter % 512) return DSV4_ERR_ARG;
   if (expert < 0 && (!L->shared_w1 || !L->shared_w2 || !L->shared_w3 || !L->shared_sf))
     return DSV4_ERR_ARG;
   if (expert >= 0 && (!L->arena || !L->arena_sf || !L->expert_slot || expert >= L->n_routed ||

@@ -3,30 +3,29 @@
 // Replaces the per-expert official Expert.forward -> act_quant + fp4_gemm /
 // fp8_gemm calls of spark_runtime/lazy_official_runtime.py:995-998,1001
 // (official kernel API: scripts/smoke_official_kernels.py:36-50) with one
-// launch over every (expert segment, 128-row weight block) of the layer.
+// launch over every (expert segment tile, 256-row weight block) of the layer.
 //
-// Orientation ("swap AB"): the weight is the M = 128 operand (A) and the
-// tokens of one expert segment are N (B), so a decode step with one token per
-// expert still fills the 128-row MMA and the kernel streams weights at HBM
-// speed.  D[weight_row, token] lives in TMEM: one lane per weight row, one
-// column per token.
+// Orientation: A = activations of one expert segment tile (M = 128 rows of
+// which the first BM are loaded: 32 for decode, 128 for prefill; rows past BM
+// read the following smem and land in TMEM lanes nobody reads), B = N = 256
+// weight rows (GEMM1: 128 rows of w1 stacked on the same 128 rows of w3;
+// GEMM2: 256 rows of w2).  One block-scaled MMA (kind::mxf8f6f4, K = 32)
+// therefore covers 4 KB of FP4 weights, and the TMEM accumulator holds, per
+// token lane, 256 output columns - so the SwiGLU and the 128-wide fp8
+// re-quantization of the epilogue are per-thread work with contiguous stores.
 //
-// Operands (both K-major, 128-byte swizzle, 128-wide K tiles):
-//   A routed : e2m1 weights straight from the expert arena, TMA'd with the
-//              16U4_ALIGN16B type (16 packed nibbles -> 16 bytes in smem);
-//   A shared : e4m3 weights of the shared expert (the "E-th expert");
-//   B        : e4m3 activations of the permuted segment rows;
-//   scales   : per-32 ue8m0 for A, per-128 (replicated x4) for B, moved
-//              smem -> TMEM with tcgen05.cp; kind::mxf8f6f4.block_scale.
+// Operands (K-major, 128-byte swizzle, 128-wide k tiles):
+//   A            : e4m3 activation rows of the permuted segment (TMA box BM rows);
+//   B routed     : e2m1 weights from the expert arena, TMA type 16U4_ALIGN16B
+//                  (16 packed nibbles -> 16 bytes in smem);
+//   B shared     : e4m3 weights of the shared expert (the E-th segment);
+//   scales       : activations per 128 (k-packed: one 32-bit TMEM word holds
+//                  four k tiles, selected by the MMA's scale-factor id), weights
+//                  per 32 (one word per k tile); both moved smem -> TMEM with
+//                  tcgen05.cp.
 //
-// GEMM1 (GATED): two accumulators (w1 and w3 rows of the same inter block);
-//   epilogue = bf16(g), bf16(u), clamp, silu(g)*u*route_weight, bf16, per-128
-//   act_quant along the inter dim (the 128 TMEM lanes = one scale block) ->
-//   e4m3 H rows + scale atoms that feed GEMM2 directly.
-// GEMM2: w2; epilogue = bf16 expert output rows O[slot, hidden].
-//
-// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner and
-// MMA issuer, warps 2..5 = epilogue (TMEM lane quarter = warp % 4).
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner and MMA
+// issuer, warps 2..5 = epilogue (TMEM lane quarter = warp % 4).
 #include "kernels.cuh"
 
 namespace dsv4 {
@@ -37,60 +36,91 @@ __host__ __device__ constexpr int pow2_at_least(int v) {
   return p;
 }
 
-template <int BN, bool GATED>
+template <int BM, bool GATED>
 struct GemmCfg {
-  static constexpr int A_BYTES = 128 * 128;
-  static constexpr int NA = GATED ? 2 : 1;
-  static constexpr int B_BYTES = BN * 128;
-  static constexpr int TILE_BYTES = NA * A_BYTES + B_BYTES;  // multiple of 1024
-  static constexpr int SFB_OFF = 512 * NA;
-  static constexpr int SF_STAGE = 512 * NA + 512;
+  static constexpr int A_BYTES = BM * 128;       // activation rows of one 128-wide k tile
+  static constexpr int B_HALF = 128 * 128;       // one 128-row weight box in smem
+  static constexpr int B_BYTES = 2 * B_HALF;     // N = 256 weight rows
+  static constexpr int TILE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int SF_STAGE = 1536;          // [act scales 512][weight scales 2 x 512]
   static constexpr int STAGE_BYTES = TILE_BYTES + SF_STAGE;
   static constexpr int SMEM_BUDGET = 200 * 1024;
   static constexpr int STAGES0 = SMEM_BUDGET / STAGE_BYTES;
   static constexpr int STAGES = STAGES0 > 8 ? 8 : STAGES0;
-  static constexpr int ACC_COLS = NA * BN;
-  static constexpr int NACC = (2 * ACC_COLS + 12 <= 512) ? 2 : 1;
-  static constexpr int SF_COL = NACC * ACC_COLS;
-  static constexpr int TMEM_COLS = pow2_at_least(SF_COL + 12);
-  static constexpr uint32_t TX_BYTES = NA * A_BYTES + B_BYTES + 512 * NA + 512;
-  static constexpr uint32_t TX_BYTES_FP4 = NA * (A_BYTES / 2) + B_BYTES + 512 * NA + 512;
-  static constexpr int RED_BYTES = GATED ? 4 * BN * 4 : 0;
+  static constexpr int ACC_COLS = 256;
+  static constexpr int SFA_COL = 256;            // activation scales: 4 columns
+  static constexpr int SFB_COL = 260;            // weight scales: 8 columns (256 rows)
+  static constexpr int TMEM_COLS = 512;
   static constexpr int CTRL_BYTES = 256;
-  static constexpr size_t SMEM_BYTES =
-      1024 + (size_t)STAGES * STAGE_BYTES + CTRL_BYTES + RED_BYTES;
-  static_assert(TILE_BYTES % 1024 == 0, "tiles must keep 1024-byte alignment");
-  static_assert(SF_COL + 12 <= 512, "TMEM overflow");
-  static_assert(BN % 32 == 0 && BN <= 128, "one sliding scale atom covers 128 rows");
+  static constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + CTRL_BYTES;
+  static_assert(A_BYTES % 1024 == 0, "tiles must keep 1024-byte alignment");
+  // the M = 128 MMA reads 128 rows (16 KB) from the A base; they must stay in the stage
+  static_assert(128 * 128 <= TILE_BYTES, "A window leaves the stage");
+  static_assert(BM == 32 || BM == 64 || BM == 128, "activation rows per tile");
   static_assert(STAGES >= 2, "need at least two stages");
 };
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-// Activation scale atoms use a sliding layout: one 512-byte atom per 32-row
-// group g and 128-wide K tile; byte (m0*16 + m1*4 + b) of atom (g, kt) holds
-// the scale of row 32*(g+m1) + m0.  A tile starting at any 32-aligned row then
-// needs exactly one atom and always lands on TMEM scale column 0.
-__device__ __forceinline__ void write_row_scale(uint8_t* atoms, int row, int kt, int KT,
-                                                uint32_t scale_byte) {
-  const uint32_t word = scale_byte * 0x01010101u;
+// Activation scale atoms use a sliding, k-packed layout: one 512-byte atom per
+// 32-row group g and group of four 128-wide k tiles q; byte (m0*16 + m1*4 + b)
+// of atom (g, q) holds the scale of row 32*(g+m1) + m0 for k tile 4q + b.  A
+// tile starting at any 32-aligned row needs one atom per four k tiles, always
+// lands on TMEM scale column 0, and the MMA picks the k tile's byte with its
+// scale-factor id.
+__device__ __forceinline__ void write_row_scale(uint8_t* atoms, int row, int kt, int KT4,
+                                                uint8_t scale_byte) {
   const int g = row >> 5;
 #pragma unroll
   for (int m1 = 0; m1 < 4; ++m1) {
     if (g - m1 >= 0)
-      *reinterpret_cast<uint32_t*>(atoms + ((size_t)(g - m1) * KT + kt) * 512 + (row & 31) * 16 +
-                                   m1 * 4) = word;
+      atoms[((size_t)(g - m1) * KT4 + (kt >> 2)) * 512 + (row & 31) * 16 + m1 * 4 + (kt & 3)] =
+          scale_byte;
   }
 }
 
-template <int BN, bool GATED>
+// Everything the producer needs about one work item (segment tile x 256-row
+// weight block).
+struct ItemInfo {
+  int jb, row0, slot;
+  bool shared;
+  int r0, r1;               // first row of the two 128-row weight boxes
+  const uint8_t* sfb0;      // scale atoms of the two boxes (k tile 0)
+  const uint8_t* sfb1;
+};
+
+template <bool GATED>
+__device__ __forceinline__ ItemInfo decode_item(const GemmArgs& a, int w, int NB, int KT) {
+  ItemInfo it;
+  const int4 tl = a.tiles[w / NB];
+  it.jb = w % NB;
+  it.row0 = tl.y;
+  it.shared = tl.x >= a.n_routed;
+  it.slot = it.shared ? 0 : a.expert_slot[tl.x];
+  const uint8_t* base = it.shared ? nullptr : a.sf_routed + (size_t)it.slot * a.sf_slot_stride;
+  const uint8_t* s0 = it.shared ? a.sf_shared0 : base + a.sf_off0;
+  const uint8_t* s1 = it.shared ? a.sf_shared1 : base + a.sf_off1;
+  if (GATED) {  // w1 rows jb*128.. on top of the same w3 rows
+    it.r0 = it.r1 = it.jb * 128;
+    it.sfb0 = s0 + (size_t)it.jb * KT * 512;
+    it.sfb1 = s1 + (size_t)it.jb * KT * 512;
+  } else {      // 256 consecutive w2 rows
+    it.r0 = it.jb * 256;
+    it.r1 = it.r0 + 128;
+    it.sfb0 = s0 + (size_t)(2 * it.jb) * KT * 512;
+    it.sfb1 = s0 + (size_t)(2 * it.jb + 1) * KT * 512;
+  }
+  return it;
+}
+
+template <int BM, bool GATED>
 __global__ void __launch_bounds__(192, 1)
-    expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA0,
-                       const __grid_constant__ CUtensorMap tmA1,
+    expert_gemm_kernel(const __grid_constant__ CUtensorMap tmW0,
+                       const __grid_constant__ CUtensorMap tmW1,
                        const __grid_constant__ CUtensorMap tmS0,
                        const __grid_constant__ CUtensorMap tmS1,
-                       const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
-  using C = GemmCfg<BN, GATED>;
+                       const __grid_constant__ CUtensorMap tmX, const GemmArgs args) {
+  using C = GemmCfg<BM, GATED>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -100,12 +130,11 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(ctrl);
   uint64_t* empty = full + C::STAGES;
   uint64_t* acc_full = empty + C::STAGES;
-  uint64_t* acc_empty = acc_full + 2;
-  uint64_t* final_bar = acc_empty + 2;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* final_bar = acc_empty + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* epi_abort = abort_flag + 1;
-  float* red = reinterpret_cast<float*>(ctrl + C::CTRL_BYTES);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -113,10 +142,8 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 128);
-    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 128);
     mbar_init(final_bar, 1);
     *abort_flag = 0;
     *epi_abort = 0;
@@ -127,8 +154,8 @@ __global__ void __launch_bounds__(192, 1)
     tmem_relinquish();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmA0);
-    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmW0);
+    tma_prefetch_desc(&tmX);
   }
   tc_fence_before();
   __syncthreads();
@@ -137,24 +164,25 @@ __global__ void __launch_bounds__(192, 1)
 
   const int NB = args.nb_count;
   const int KT = args.kt_count;
+  const int KT4 = KT >> 2;
   const int total = *args.n_tiles * NB;
+  const int step = (int)gridDim.x;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int w = blockIdx.x; w < total && !*abort_flag; w += gridDim.x) {
-        const int4 tl = args.tiles[w / NB];
-        const int jb = w % NB;
-        const bool shared = tl.x >= args.n_routed;
-        const int slot = shared ? 0 : args.expert_slot[tl.x];
-        const uint8_t* sfa0 = shared ? args.sf_shared0
-                                     : args.sf_routed + (size_t)slot * args.sf_slot_stride + args.sf_off0;
-        const uint8_t* sfa1 = shared ? args.sf_shared1
-                                     : args.sf_routed + (size_t)slot * args.sf_slot_stride + args.sf_off1;
-        const int row0 = tl.y;
-        const size_t g0 = (size_t)(row0 >> 5);
+      ItemInfo cur, nxt;
+      if ((int)blockIdx.x < total) cur = decode_item<GATED>(args, blockIdx.x, NB, KT);
+      for (int w = blockIdx.x; w < total && !*abort_flag; w += step) {
+        // the next item's descriptor loads are issued now and used one item
+        // later, so their latency hides behind this item's k loop
+        if (w + step < total) nxt = decode_item<GATED>(args, w + step, NB, KT);
+        const size_t g0 = (size_t)(cur.row0 >> 5);
+        // transaction bytes count what the TMA reads from global memory: an e2m1
+        // box is 8 KB there even though it spreads to 16 KB (16U4_ALIGN16B) in smem
+        const uint32_t tx_base = C::A_BYTES + 2u * (cur.shared ? C::B_HALF : C::B_HALF / 2) + 1024u;
         for (int kt = 0; kt < KT; ++kt) {
           if (!mbar_wait(&empty[stage], phase ^ 1, DSV4_DEVERR_TIMEOUT_PRODUCER)) {
             *abort_flag = 1;
@@ -162,25 +190,28 @@ __global__ void __launch_bounds__(192, 1)
           }
           uint8_t* st = tile_base + (size_t)stage * C::TILE_BYTES;
           uint8_t* sf = sf_base + (size_t)stage * C::SF_STAGE;
-          // transaction bytes count what the TMA reads: an e2m1 tile is 8 KB in
-          // global memory even though it spreads to 16 KB (16U4_ALIGN16B) in smem
-          mbar_arrive_expect_tx(&full[stage], shared ? C::TX_BYTES : C::TX_BYTES_FP4);
-          if (shared) {
-            tma_load_2d(st, &tmS0, &full[stage], kt * 128, jb * 128);
-            if (GATED) tma_load_2d(st + C::A_BYTES, &tmS1, &full[stage], kt * 128, jb * 128);
+          const bool sfa_tile = (kt & 3) == 0;  // one k-packed activation scale atom per 4 tiles
+          mbar_arrive_expect_tx(&full[stage], tx_base + (sfa_tile ? 512u : 0u));
+          tma_load_2d(st, &tmX, &full[stage], kt * 128, cur.row0);
+          uint8_t* b = st + C::A_BYTES;
+          if (cur.shared) {
+            tma_load_2d(b, &tmS0, &full[stage], kt * 128, cur.r0);
+            tma_load_2d(b + C::B_HALF, GATED ? &tmS1 : &tmS0, &full[stage], kt * 128, cur.r1);
           } else {
-            tma_load_3d(st, &tmA0, &full[stage], kt * 128, jb * 128, slot);
-            if (GATED) tma_load_3d(st + C::A_BYTES, &tmA1, &full[stage], kt * 128, jb * 128, slot);
+            tma_load_3d(b, &tmW0, &full[stage], kt * 128, cur.r0, cur.slot);
+            tma_load_3d(b + C::B_HALF, GATED ? &tmW1 : &tmW0, &full[stage], kt * 128, cur.r1,
+                        cur.slot);
           }
-          tma_load_2d(st + C::NA * C::A_BYTES, &tmB, &full[stage], kt * 128, row0);
-          bulk_load(sf, sfa0 + ((size_t)jb * KT + kt) * 512, 512, &full[stage]);
-          if (GATED) bulk_load(sf + 512, sfa1 + ((size_t)jb * KT + kt) * 512, 512, &full[stage]);
-          bulk_load(sf + C::SFB_OFF, args.sfb + (g0 * KT + kt) * 512, 512, &full[stage]);
+          if (sfa_tile)
+            bulk_load(sf, args.sfb + (g0 * KT4 + (kt >> 2)) * 512, 512, &full[stage]);
+          bulk_load(sf + 512, cur.sfb0 + (size_t)kt * 512, 512, &full[stage]);
+          bulk_load(sf + 1024, cur.sfb1 + (size_t)kt * 512, 512, &full[stage]);
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
+        cur = nxt;
       }
       if (*abort_flag) {
         // let copies already in flight land before the CTA can exit
@@ -194,20 +225,20 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      int abuf = 0;
       uint32_t aphase = 0;
-      for (int w = blockIdx.x; w < total && !*abort_flag; w += gridDim.x) {
-        const int4 tl = args.tiles[w / NB];
-        const uint32_t a_fmt = tl.x >= args.n_routed ? 0u : 5u;  // e4m3 shared, e2m1 routed
-        if (!mbar_wait(&acc_empty[abuf], aphase ^ 1, DSV4_DEVERR_TIMEOUT_MMA)) {
+      const uint32_t sfa_t = tmem + C::SFA_COL;
+      const uint32_t sfb_t = tmem + C::SFB_COL;
+      int4 tl_next = make_int4(0, 0, 0, 0);
+      if ((int)blockIdx.x < total) tl_next = args.tiles[blockIdx.x / NB];
+      for (int w = blockIdx.x; w < total && !*abort_flag; w += step) {
+        const int4 tl = tl_next;
+        if (w + step < total) tl_next = args.tiles[(w + step) / NB];
+        const uint32_t b_fmt = tl.x >= args.n_routed ? 0u : 5u;  // e4m3 shared, e2m1 routed
+        if (!mbar_wait(acc_empty, aphase ^ 1, DSV4_DEVERR_TIMEOUT_MMA)) {
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
-        const uint32_t d0 = tmem + abuf * C::ACC_COLS;
-        const uint32_t sfa0_t = tmem + C::SF_COL;
-        const uint32_t sfa1_t = tmem + C::SF_COL + 4;
-        const uint32_t sfb_t = tmem + C::SF_COL + 8;
         bool ok = true;
         for (int kt = 0; kt < KT; ++kt) {
           if (!mbar_wait(&full[stage], phase, DSV4_DEVERR_TIMEOUT_MMA)) {
@@ -217,19 +248,16 @@ __global__ void __launch_bounds__(192, 1)
           tc_fence_after();
           const uint8_t* st = tile_base + (size_t)stage * C::TILE_BYTES;
           const uint8_t* sf = sf_base + (size_t)stage * C::SF_STAGE;
-          tc_cp_sf(sfa0_t, sdesc_sf(smem_u32(sf)));
-          if (GATED) tc_cp_sf(sfa1_t, sdesc_sf(smem_u32(sf + 512)));
-          tc_cp_sf(sfb_t, sdesc_sf(smem_u32(sf + C::SFB_OFF)));
-          const uint64_t a0 = sdesc_k_sw128(smem_u32(st));
-          const uint64_t a1 = sdesc_k_sw128(smem_u32(st + C::A_BYTES));
-          const uint64_t b = sdesc_k_sw128(smem_u32(st + C::NA * C::A_BYTES));
+          if ((kt & 3) == 0) tc_cp_sf(sfa_t, sdesc_sf(smem_u32(sf)));
+          tc_cp_sf(sfb_t, sdesc_sf(smem_u32(sf + 512)));
+          tc_cp_sf(sfb_t + 4, sdesc_sf(smem_u32(sf + 1024)));
+          const uint64_t adesc = sdesc_k_sw128(smem_u32(st));
+          const uint64_t bdesc = sdesc_k_sw128(smem_u32(st + C::A_BYTES));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t idesc = idesc_mxf8f6f4(a_fmt, 0u, BN, kk, kk);
-            const uint32_t acc = (kt > 0 || kk > 0) ? 1u : 0u;
-            tc_mma_mxf8f6f4(d0, a0 + 2 * kk, b + 2 * kk, idesc, sfa0_t, sfb_t, acc);
-            if (GATED)
-              tc_mma_mxf8f6f4(d0 + BN, a1 + 2 * kk, b + 2 * kk, idesc, sfa1_t, sfb_t, acc);
+            const uint32_t idesc = idesc_mxf8f6f4(0u, b_fmt, 256, kt & 3, kk);
+            tc_mma_mxf8f6f4(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, sfa_t, sfb_t,
+                            (kt > 0 || kk > 0) ? 1u : 0u);
           }
           tc_commit(&empty[stage]);
           if (++stage == C::STAGES) {
@@ -241,11 +269,8 @@ __global__ void __launch_bounds__(192, 1)
           *abort_flag = 1;
           break;
         }
-        tc_commit(&acc_full[abuf]);
-        if (++abuf == C::NACC) {
-          abuf = 0;
-          aphase ^= 1;
-        }
+        tc_commit(acc_full);
+        aphase ^= 1;
       }
       // drain every tcgen05 op of this CTA before TMEM is released
       tc_commit(final_bar);
@@ -253,20 +278,22 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // Thread (warp quarter q, lane) owns token row 32q + lane of the tile and
+    // the 256 accumulator columns of that row.  It copies them out of TMEM
+    // (as packed bf16), releases the accumulator to the MMA warp, then does
+    // the arithmetic and the stores while the next item's MMAs run.
     const int q = warp & 3;
-    int abuf = 0;
+    const int r = q * 32 + lane;
     uint32_t aphase = 0;
     const float lim = args.swiglu_limit;
-    for (int w = blockIdx.x; w < total; w += gridDim.x) {
+    const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+    for (int w = blockIdx.x; w < total; w += step) {
       const int4 tl = args.tiles[w / NB];
       const int jb = w % NB;
       const int row0 = tl.y, nrows = tl.z;
-      // The four epilogue warps take every decision together: a warp whose
-      // wait timed out still meets the others at the named barrier, then all
-      // of them leave.  (A named barrier with a missing warp would never end.)
       // epi_abort is written only by epilogue warps and read between two
       // barriers, so all four see the same value.
-      if (!mbar_wait(&acc_full[abuf], aphase, DSV4_DEVERR_TIMEOUT_EPILOGUE)) {
+      if (!mbar_wait(acc_full, aphase, DSV4_DEVERR_TIMEOUT_EPILOGUE)) {
         *epi_abort = 1;
         *abort_flag = 1;
       }
@@ -274,67 +301,81 @@ __global__ void __launch_bounds__(192, 1)
       const bool stop = *epi_abort != 0;
       epi_bar();
       if (stop) break;
+      aphase ^= 1;
       tc_fence_after();
-      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + abuf * C::ACC_COLS;
-      const int col = jb * 128 + q * 32 + lane;  // output feature (weight row)
-      if (GATED) {
-        for (int c = 0; c < BN; c += 16) {
-          float g[16], u[16], h[16];
-          tmem_ld16(taddr + c, g);
-          tmem_ld16(taddr + BN + c, u);
+      const bool warp_rows = q * 32 < nrows;  // TMEM lanes of this quarter hold real rows
+      uint32_t pk[128];                       // packed bf16 pairs out of TMEM
+      if (warp_rows) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int n = c + i;
-            float gb = bf16_round(g[i]);
-            float ub = bf16_round(u[i]);
+        for (int c = 0; c < 8; ++c) {
+          float a[16], b[16];
+          if (GATED) {  // pk[j] = (bf16 g_j, bf16 u_j) for j = 16c .. 16c+15
+            tmem_ld16(taddr + 16 * c, a);
+            tmem_ld16(taddr + 128 + 16 * c, b);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const __nv_bfloat162 v = __floats2bfloat162_rn(a[i], b[i]);
+              pk[16 * c + i] = *reinterpret_cast<const uint32_t*>(&v);
+            }
+          } else {      // pk[j] = bf16 outputs (2j, 2j+1)
+            tmem_ld16(taddr + 32 * c, a);
+            tmem_ld16(taddr + 32 * c + 16, b);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const __nv_bfloat162 v0 = __floats2bfloat162_rn(a[2 * i], a[2 * i + 1]);
+              const __nv_bfloat162 v1 = __floats2bfloat162_rn(b[2 * i], b[2 * i + 1]);
+              pk[16 * c + i] = *reinterpret_cast<const uint32_t*>(&v0);
+              pk[16 * c + 8 + i] = *reinterpret_cast<const uint32_t*>(&v1);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(acc_empty);
+      if (warp_rows && r < nrows) {
+        const int row = row0 + r;
+        if (GATED) {
+          const float wr = args.slot_weight[row];
+          float amax = 0.f;
+#pragma unroll
+          for (int j = 0; j < 128; ++j) {
+            const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(&pk[j]);
+            float gb = __low2float(v), ub = __high2float(v);
             if (lim > 0.f) {
               ub = fminf(fmaxf(ub, -lim), lim);
               gb = fminf(gb, lim);
             }
             const float s = gb / (1.0f + expf(-gb));
-            const float wr = n < nrows ? args.slot_weight[row0 + n] : 0.f;
-            float hv = (s * ub) * wr;
-            hv = bf16_round(hv);
-            h[i] = hv;
-            float m = fabsf(hv);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            if (lane == 0) red[q * BN + n] = m;
+            const float hv = bf16_round((s * ub) * wr);
+            amax = fmaxf(amax, fabsf(hv));
+            pk[j] = __float_as_uint(hv);
           }
-          epi_bar();
+          const int e = act_scale_exp(amax);
+          const float inv = exp2i(-e);
+          uint8_t* dst = args.out_q + (size_t)row * args.out_ld + jb * 128;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int n = c + i;
-            const float amax =
-                fmaxf(fmaxf(red[n], red[BN + n]), fmaxf(red[2 * BN + n], red[3 * BN + n]));
-            const int e = act_scale_exp(amax);
-            const uint8_t code = f32_to_e4m3(h[i] * exp2i(-e));
-            if (n < nrows) {
-              args.out_q[(size_t)(row0 + n) * args.out_ld + col] = code;
-              if (q == 0 && lane == 0)
-                write_row_scale(args.out_sf, row0 + n, jb, args.out_ld >> 7,
-                                static_cast<uint32_t>(e + 127));
+          for (int v = 0; v < 8; ++v) {
+            uint32_t wds[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              uint32_t word = 0;
+#pragma unroll
+              for (int b = 0; b < 4; ++b)
+                word |= static_cast<uint32_t>(
+                            f32_to_e4m3(__uint_as_float(pk[16 * v + 4 * t + b]) * inv))
+                        << (8 * b);
+              wds[t] = word;
             }
+            *reinterpret_cast<uint4*>(dst + 16 * v) = make_uint4(wds[0], wds[1], wds[2], wds[3]);
           }
-          epi_bar();
-        }
-      } else {
-        for (int c = 0; c < BN; c += 16) {
-          float v[16];
-          tmem_ld16(taddr + c, v);
+          write_row_scale(args.out_sf, row, jb, (args.out_ld >> 7) >> 2,
+                          static_cast<uint8_t>(e + 127));
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(args.out_bf16 + (size_t)row * args.out_ld + jb * 256);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int n = c + i;
-            if (n < nrows)
-              args.out_bf16[(size_t)(row0 + n) * args.out_ld + col] = __float2bfloat16_rn(v[i]);
-          }
+          for (int v = 0; v < 32; ++v)
+            dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
         }
-      }
-      tc_fence_before();
-      mbar_arrive(&acc_empty[abuf]);
-      if (++abuf == C::NACC) {
-        abuf = 0;
-        aphase ^= 1;
       }
     }
   }
@@ -370,7 +411,7 @@ static EncodeTiledFn get_encode_fn() {
 
 // FP4 e2m1 weights of every arena slot: dims {K elements, rows, slots}.
 int make_tmap_fp4_arena(CUtensorMap* m, const void* base, int K, int rows, int slots,
-                        long long slot_stride) {
+                        long long slot_stride, int l2_promotion) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return DSV4_ERR_CUDA;
   if ((reinterpret_cast<uintptr_t>(base) & 31) || (slot_stride & 31) || (K % 128) ||
@@ -380,9 +421,14 @@ int make_tmap_fp4_arena(CUtensorMap* m, const void* base, int K, int rows, int s
   cuuint64_t strides[2] = {(cuuint64_t)(K / 2), (cuuint64_t)slot_stride};
   cuuint32_t box[3] = {128, 128, 1};
   cuuint32_t es[3] = {1, 1, 1};
+  const CUtensorMapL2promotion promo =
+      l2_promotion >= 256 ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B
+      : l2_promotion >= 128 ? CU_TENSOR_MAP_L2_PROMOTION_L2_128B
+      : l2_promotion >= 64  ? CU_TENSOR_MAP_L2_PROMOTION_L2_64B
+                            : CU_TENSOR_MAP_L2_PROMOTION_NONE;
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, const_cast<void*>(base), dims,
                    strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                   promo, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? DSV4_OK : DSV4_ERR_CUDA;
 }
 
@@ -401,20 +447,20 @@ int make_tmap_u8(CUtensorMap* m, const void* base, int K, int rows, int box_rows
   return r == CUDA_SUCCESS ? DSV4_OK : DSV4_ERR_CUDA;
 }
 
-template <int BN, bool GATED>
+template <int BM, bool GATED>
 static int launch_one(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& s0,
                       const CUtensorMap& s1, const CUtensorMap& b, const GemmArgs& args, int grid,
                       cudaStream_t st) {
-  using C = GemmCfg<BN, GATED>;
+  using C = GemmCfg<BM, GATED>;
   static bool attr_set = false;
   if (!attr_set) {
-    if (cudaFuncSetAttribute(expert_gemm_kernel<BN, GATED>,
+    if (cudaFuncSetAttribute(expert_gemm_kernel<BM, GATED>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)C::SMEM_BYTES) != cudaSuccess)
       return DSV4_ERR_CUDA;
     attr_set = true;
   }
-  expert_gemm_kernel<BN, GATED><<<grid, 192, C::SMEM_BYTES, st>>>(a0, a1, s0, s1, b, args);
+  expert_gemm_kernel<BM, GATED><<<grid, 192, C::SMEM_BYTES, st>>>(a0, a1, s0, s1, b, args);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
 

@@ -37,34 +37,59 @@ __device__ __forceinline__ float sigmoid_canonical(float x) {
 // memory as fp32, then each warp walks tokens and accumulates EPC dot
 // products with 16-byte loads of x, reduced across the warp.
 // ---------------------------------------------------------------------------
-constexpr int kGateEPC = 4;
+constexpr int kGateEPC = 2;
+constexpr int kGateThreads = 256;
 
 template <bool W_FP32>
-__global__ void __launch_bounds__(256) gate_logits_kernel(const __nv_bfloat16* __restrict__ x,
-                                                          const void* __restrict__ w, int T, int H,
-                                                          int E, float* __restrict__ logits) {
-  extern __shared__ float ws[];  // [kGateEPC][H]
+__global__ void __launch_bounds__(kGateThreads) gate_logits_kernel(
+    const __nv_bfloat16* __restrict__ x, const void* __restrict__ w, int T, int H, int E,
+    float* __restrict__ logits) {
+  extern __shared__ float ws[];  // [kGateEPC][H] fp32
   const int e0 = blockIdx.x * kGateEPC;
   const int ne = min(kGateEPC, E - e0);
-  for (int i = threadIdx.x; i < kGateEPC * H; i += blockDim.x) {
-    const int j = i / H, h = i % H;
-    float v = 0.f;
-    if (j < ne) {
-      if (W_FP32)
-        v = static_cast<const float*>(w)[(size_t)(e0 + j) * H + h];
-      else
-        v = __bfloat162float(static_cast<const __nv_bfloat16*>(w)[(size_t)(e0 + j) * H + h]);
+  // Stage the gate rows with 16-byte loads, every load of a thread issued
+  // before any is used (the rows come from DRAM: latency, not bandwidth).
+  const int vec = W_FP32 ? 4 : 8;  // elements per 16-byte load
+  const int nvec = kGateEPC * H / vec;
+  constexpr int kMaxPerThread = 16;
+  uint4 buf[kMaxPerThread];
+#pragma unroll
+  for (int u = 0; u < kMaxPerThread; ++u) {
+    const int v = threadIdx.x + u * kGateThreads;
+    buf[u] = make_uint4(0, 0, 0, 0);
+    if (v < nvec && (v * vec) / H < ne) {
+      const char* base = static_cast<const char*>(w) + (size_t)e0 * H * (W_FP32 ? 4 : 2);
+      buf[u] = __ldg(reinterpret_cast<const uint4*>(base) + v);
     }
-    ws[i] = v;
+  }
+#pragma unroll
+  for (int u = 0; u < kMaxPerThread; ++u) {
+    const int v = threadIdx.x + u * kGateThreads;
+    if (v < nvec) {
+      float* dst = ws + v * vec;
+      if (W_FP32) {
+        *reinterpret_cast<uint4*>(dst) = buf[u];
+      } else {
+        const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&buf[u]);
+        float4 lo, hi;
+        lo.x = __bfloat162float(b[0]); lo.y = __bfloat162float(b[1]);
+        lo.z = __bfloat162float(b[2]); lo.w = __bfloat162float(b[3]);
+        hi.x = __bfloat162float(b[4]); hi.y = __bfloat162float(b[5]);
+        hi.z = __bfloat162float(b[6]); hi.w = __bfloat162float(b[7]);
+        reinterpret_cast<float4*>(dst)[0] = lo;
+        reinterpret_cast<float4*>(dst)[1] = hi;
+      }
+    }
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nwarps = blockDim.x >> 5;
+  const int nwarps = kGateThreads >> 5;
   for (int t = warp; t < T; t += nwarps) {
     float acc[kGateEPC];
 #pragma unroll
     for (int j = 0; j < kGateEPC; ++j) acc[j] = 0.f;
     const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)t * H);
+#pragma unroll 4
     for (int c = lane; c < H / 8; c += 32) {
       const uint4 raw = __ldg(xr + c);
       const __nv_bfloat16* xv = reinterpret_cast<const __nv_bfloat16*>(&raw);
@@ -182,12 +207,12 @@ int launch_gate_logits(const void* x, const void* w, int w_is_fp32, int T, int H
   if (w_is_fp32) {
     cudaFuncSetAttribute(gate_logits_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
-    gate_logits_kernel<true><<<grid, 256, smem, st>>>(static_cast<const __nv_bfloat16*>(x), w, T,
+    gate_logits_kernel<true><<<grid, kGateThreads, smem, st>>>(static_cast<const __nv_bfloat16*>(x), w, T,
                                                       H, E, logits);
   } else {
     cudaFuncSetAttribute(gate_logits_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
-    gate_logits_kernel<false><<<grid, 256, smem, st>>>(static_cast<const __nv_bfloat16*>(x), w,
+    gate_logits_kernel<false><<<grid, kGateThreads, smem, st>>>(static_cast<const __nv_bfloat16*>(x), w,
                                                        T, H, E, logits);
   }
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;

@@ -12,16 +12,16 @@ struct GemmArgs {
   const int* expert_slot; // [n_routed] routed expert -> arena slot
   int n_routed;           // segment id n_routed is the shared expert
   int kt_count;           // K / 128
-  int nb_count;           // output rows / 128 (per weight)
+  int nb_count;           // weight blocks per tile: GEMM1 inter/128 (w1|w3 pairs), GEMM2 hidden/256
   const uint8_t* sf_routed;
   long long sf_slot_stride;
   long long sf_off0, sf_off1;  // byte offsets of the A0 / A1 atoms inside a slot
   const uint8_t* sf_shared0;
   const uint8_t* sf_shared1;
-  const uint8_t* sfb;          // activation atoms, sliding layout [row/32][kt_count][512]
+  const uint8_t* sfb;          // activation atoms, sliding k-packed layout [row/32][kt_count/4][512]
   const float* slot_weight;    // GEMM1: routing weight of each segment row
   uint8_t* out_q;              // GEMM1: H codes [rows][out_ld]
-  uint8_t* out_sf;             // GEMM1: H scale atoms, sliding layout [row/32][out_ld/128][512]
+  uint8_t* out_sf;             // GEMM1: H scale atoms, same layout [row/32][out_ld/512][512]
   __nv_bfloat16* out_bf16;     // GEMM2: O [rows][out_ld]
   int out_ld;
   float swiglu_limit;
@@ -54,7 +54,7 @@ int launch_build_sf_fp4_arena(const uint8_t* arena, long long slot_stride, const
 int launch_build_sf_fp8(const uint8_t* scale, int rows, int K, uint8_t* atoms, int num_sms,
                         cudaStream_t st);
 int make_tmap_fp4_arena(CUtensorMap* m, const void* base, int K, int rows, int slots,
-                        long long slot_stride);
+                        long long slot_stride, int l2_promotion);
 int make_tmap_u8(CUtensorMap* m, const void* base, int K, int rows, int box_rows);
 int launch_expert_gemm(bool gated, int block_n, const CUtensorMap& a0, const CUtensorMap& a1,
                        const CUtensorMap& s0, const CUtensorMap& s1, const CUtensorMap& b,

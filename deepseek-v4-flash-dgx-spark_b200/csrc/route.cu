@@ -141,32 +141,49 @@ __global__ void __launch_bounds__(kPlanThreads) route_plan_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// Per-128 act_quant of one row, one warp: lane l owns elements 4l..4l+3 of each
-// 128-wide block.  Writes e4m3 codes and returns (in every lane) the ue8m0 byte.
+// Per-128 act_quant of one row by one warp: lane l owns elements 4l..4l+3 of
+// each 128-wide block.  Blocks are processed 8 at a time with all 8 loads in
+// flight before any is used (the rows come from L2/DRAM: latency-bound).
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t quant_block_128(const __nv_bfloat16* src, int lane,
-                                                    uint8_t* dst, bool valid) {
-  float v[4] = {0.f, 0.f, 0.f, 0.f};
-  if (valid) {
-    const uint2 raw = *reinterpret_cast<const uint2*>(src + lane * 4);
-    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
+constexpr int kQuantGroup = 8;
+
+template <typename ScaleSink>
+__device__ __forceinline__ void quant_row(const __nv_bfloat16* __restrict__ src, bool valid,
+                                          uint8_t* __restrict__ dst, int KT, int lane,
+                                          ScaleSink sink) {
+  for (int k0 = 0; k0 < KT; k0 += kQuantGroup) {
+    uint2 raw[kQuantGroup];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(b[i]);
+    for (int g = 0; g < kQuantGroup; ++g) {
+      raw[g] = make_uint2(0, 0);
+      if (valid && k0 + g < KT)
+        raw[g] = *reinterpret_cast<const uint2*>(src + (size_t)(k0 + g) * 128 + lane * 4);
+    }
+#pragma unroll
+    for (int g = 0; g < kQuantGroup; ++g) {
+      if (k0 + g >= KT) break;
+      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw[g]);
+      float v[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(b[i]);
+      float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const int e = act_scale_exp(amax);
+      const float inv = exp2i(-e);
+      uint32_t packed = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        packed |= static_cast<uint32_t>(f32_to_e4m3(v[i] * inv)) << (8 * i);
+      *reinterpret_cast<uint32_t*>(dst + (size_t)(k0 + g) * 128 + lane * 4) = packed;
+      sink(k0 + g, static_cast<uint32_t>(e + 127));
+    }
   }
-  float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  const int e = act_scale_exp(amax);
-  const float inv = exp2i(-e);
-  uint32_t packed = 0;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) packed |= static_cast<uint32_t>(f32_to_e4m3(v[i] * inv)) << (8 * i);
-  *reinterpret_cast<uint32_t*>(dst + lane * 4) = packed;
-  return static_cast<uint32_t>(e + 127);
 }
 
-// Activation scales go to the sliding atoms: atom (g, kt) holds rows 32g ..
-// 32g+127, row r at byte (r%32)*16 + ((r/32)-g)*4, its byte replicated x4.
+// Activation scales go to the sliding k-packed atoms: atom (g, q) holds rows
+// 32g .. 32g+127 for k tiles 4q .. 4q+3, row r / tile kt at byte
+// (r%32)*16 + ((r/32)-g)*4 + kt%4.
 __global__ void __launch_bounds__(256) permute_quant_kernel(
     const __nv_bfloat16* __restrict__ x, int H, const int* __restrict__ slot_token,
     const int* __restrict__ total_rows_ptr, uint8_t* __restrict__ xq, uint8_t* __restrict__ sfb) {
@@ -176,18 +193,16 @@ __global__ void __launch_bounds__(256) permute_quant_kernel(
   const int nwarps = (gridDim.x * blockDim.x) >> 5;
   for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < total; row += nwarps) {
     const int t = slot_token[row];
-    const __nv_bfloat16* src = x + (size_t)(t < 0 ? 0 : t) * H;
-    uint8_t* dst = xq + (size_t)row * H;
-    for (int kt = 0; kt < KT; ++kt) {
-      const uint32_t s = quant_block_128(src + kt * 128, lane, dst + kt * 128, t >= 0);
-      if (lane < 4) {
-        const int m1 = lane;
-        const int g = (row >> 5) - m1;
-        if (g >= 0)
-          *reinterpret_cast<uint32_t*>(sfb + ((size_t)g * KT + kt) * 512 + (row & 31) * 16 +
-                                       m1 * 4) = s * 0x01010101u;
-      }
-    }
+    quant_row(x + (size_t)(t < 0 ? 0 : t) * H, t >= 0, xq + (size_t)row * H, KT, lane,
+              [&](int kt, uint32_t s) {
+                if (lane < 4) {
+                  const int m1 = lane;
+                  const int g = (row >> 5) - m1;
+                  if (g >= 0)
+                    sfb[((size_t)g * (KT >> 2) + (kt >> 2)) * 512 + (row & 31) * 16 + m1 * 4 +
+                        (kt & 3)] = static_cast<uint8_t>(s);
+                }
+              });
   }
 }
 
@@ -198,23 +213,21 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const __nv_bfloat16* __r
   const int KT = K / 128;
   const int nwarps = (gridDim.x * blockDim.x) >> 5;
   for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < M; row += nwarps) {
-    for (int kt = 0; kt < KT; ++kt) {
-      const uint32_t sc =
-          quant_block_128(x + (size_t)row * K + kt * 128, lane, q + (size_t)row * K + kt * 128, true);
+    quant_row(x + (size_t)row * K, true, q + (size_t)row * K, KT, lane, [&](int kt, uint32_t sc) {
       if (lane == 0) s[(size_t)row * KT + kt] = static_cast<uint8_t>(sc);
-    }
+    });
   }
 }
 
 // ---------------------------------------------------------------------------
 // Combine: y[t] = bf16( sum over t's routes in ascending expert id of O[slot]
 // (fp32) + O[shared slot] ).  Routing weights were applied inside the expert
-// (before w2), so this is a plain ordered sum.  One CTA of 128 threads per
-// token, 8 bf16 per 16-byte load.
+// (before w2), so this is a plain ordered sum.  One CTA per token, one thread
+// per 8-element chunk: a thread's k+1 row loads are all in flight at once.
 // ---------------------------------------------------------------------------
 constexpr int kMaxK = 8;
 
-__global__ void __launch_bounds__(128) combine_kernel(const __nv_bfloat16* __restrict__ O, int H,
+__global__ void __launch_bounds__(512) combine_kernel(const __nv_bfloat16* __restrict__ O, int H,
                                                       const int* __restrict__ route_slot,
                                                       const int64_t* __restrict__ indices, int T,
                                                       int k, const int* __restrict__ shared_base,
@@ -345,7 +358,7 @@ int launch_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* s, int nu
 int launch_combine(const void* O, int H, const int* route_slot, const int64_t* indices, int T,
                    int k, const int* shared_base, void* y, cudaStream_t st) {
   if (T <= 0) return DSV4_OK;
-  combine_kernel<<<T, 128, 0, st>>>(static_cast<const __nv_bfloat16*>(O), H, route_slot, indices,
+  combine_kernel<<<T, H / 8 < 512 ? H / 8 : 512, 0, st>>>(static_cast<const __nv_bfloat16*>(O), H, route_slot, indices,
                                     T, k, shared_base, static_cast<__nv_bfloat16*>(y));
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
