@@ -6,3 +6,4 @@
 #include "expert_gemm.cu"
 #include "materialize.cu"
 #include "capi.cu"
+#include "no_alloc.cu"

@@ -80,6 +80,8 @@ _SIGNATURES = {
     "dsv4_moe_forward": (c_int, [ctypes.POINTER(MoELayerDesc), c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_ll, c_vp]),
     "dsv4_expert_workspace_bytes": (c_ll, [ctypes.POINTER(MoELayerDesc), c_int]),
     "dsv4_expert_forward": (c_int, [ctypes.POINTER(MoELayerDesc), c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_ll, c_vp]),
+    "dsv4_expert_static_scratch_bytes": (c_ll, []),
+    "dsv4_expert_forward_static": (c_int, [ctypes.POINTER(MoELayerDesc), c_int, c_vp, c_int, c_vp, c_vp, c_vp]),
     "dsv4_profile_enable": (c_int, [c_int]),
     "dsv4_profile_read": (c_int, [ctypes.POINTER(c_float), c_int]),
     "dsv4_gate_logits": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp]),

@@ -127,6 +127,23 @@ DSV4_API int dsv4_expert_forward(const dsv4_moe_layer* L, int expert, const void
 DSV4_API int dsv4_profile_enable(int enable);
 DSV4_API int dsv4_profile_read(float* stage_ms, int n);
 
+/* Allocation-free dsv4_expert_forward (no counterpart in the reference).
+ * For callers that may not allocate device memory and cannot pass a
+ * workspace: a host runtime that owns every allocation and passes only the
+ * input and output buffers, or a serving loop that must not touch the
+ * allocator while it runs.  Same arguments and results as
+ * dsv4_expert_forward minus the workspace; the scratch is a fixed
+ * dsv4_expert_static_scratch_bytes() (4 MiB) array of device memory that the
+ * library holds on every GPU it runs on until the process exits.  Calls whose
+ * dsv4_expert_workspace_bytes(L, T) exceeds it return DSV4_ERR_WORKSPACE
+ * (up to 640 tokens at H=4096, I=2048).  The first call on a device looks up
+ * the array's device address; make it before any stream capture.  All calls
+ * share the array: calls that may overlap on the GPU race and must not be
+ * issued.  Nothing is allocated, freed or cleared. */
+DSV4_API long long dsv4_expert_static_scratch_bytes(void);
+DSV4_API int dsv4_expert_forward_static(const dsv4_moe_layer* L, int expert, const void* x, int T,
+                                        const float* row_weights, void* y, void* stream);
+
 /* ---- individual stages (same kernels as dsv4_moe_forward) --------------- */
 
 /* Official Gate logits: logits[T,E] = x[T,H] . Wg[E,H]^T in fp32. */
