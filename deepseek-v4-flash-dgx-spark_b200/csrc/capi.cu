@@ -55,12 +55,52 @@ static void stage_mark(int i, cudaStream_t st) {
     cudaEventRecord(g_stage_ev[i], st);
 }
 
+// Official Gate.forward.  bf16 gate weights over 256 experts run on the
+// tensor core: batches of kFusedGateTokens or more with the routing fused
+// into the GEMM epilogue, smaller ones as split GEMM partials (when `partials`
+// has room for them) summed in a fixed order by the top-k kernel.  Other gates
+// use the SIMT logits kernel.  Every path routes bit-exactly on the logits it
+// produced.
+constexpr int kFusedGateTokens = 2048;
+
+static bool tc_gate_ok(const void* x, const void* w, int w_fp32, int H, int E) {
+  return !w_fp32 && E == 256 && H % 64 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+         (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+}
+
+static long long gate_partials_bytes(int T, int H, int E, int nsm, bool tc) {
+  if (!tc || T >= kFusedGateTokens || T <= 0) return 0;
+  int bm, ks;
+  gate_gemm_split_shape(T, H, E, nsm, &bm, &ks);
+  return (long long)ks * T * E * 4;
+}
+
+static int gate_route(const void* x, const void* w, int w_fp32, const float* bias, int T, int H,
+                      int E, int k, float route_scale, float* logits, float* weights,
+                      int64_t* indices, float* partials, long long partials_bytes, int nsm,
+                      cudaStream_t st) {
+  if (tc_gate_ok(x, w, w_fp32, H, E)) {
+    const long long need = gate_partials_bytes(T, H, E, nsm, true);
+    if (need > 0 && partials && partials_bytes >= need) {
+      int bm, ks;
+      gate_gemm_split_shape(T, H, E, nsm, &bm, &ks);
+      int rc = launch_gate_gemm_partials(x, w, T, H, E, partials, nsm, st);
+      if (rc) return rc;
+      return launch_gate_topk(partials, bias, T, E, k, route_scale, weights, indices, st, ks, logits);
+    }
+    return launch_gate_gemm_topk(x, w, T, H, bias, k, route_scale, logits, weights, indices, nsm, st);
+  }
+  int rc = launch_gate_logits(x, w, w_fp32, T, H, E, logits, st);
+  if (rc) return rc;
+  return launch_gate_topk(logits, bias, T, E, k, route_scale, weights, indices, st);
+}
+
 // ---------------------------------------------------------------------------
 // workspace layout of one layer call
 // ---------------------------------------------------------------------------
 struct Plan {
   int T, E, k, H, I, S, block_n, max_rows, max_tiles;
-  long long off[15];
+  long long off[16];
   long long total;
 };
 
@@ -101,7 +141,7 @@ static Plan make_plan(const dsv4_moe_layer* L, int T) {
   p.max_rows = (int)((rows + 31) / 32 * 32);
   p.max_tiles = (int)(((long long)T * p.k + (long long)T * p.S) / p.block_n + p.E + 2);
   const long long atom_groups = p.max_rows / 32 + 4;
-  long long sz[15] = {
+  long long sz[16] = {
       (long long)T * p.E * 4,                 // logits
       (long long)T * p.k * 4,                 // weights
       (long long)T * p.k * 8,                 // indices
@@ -117,9 +157,11 @@ static Plan make_plan(const dsv4_moe_layer* L, int T) {
       (long long)p.max_rows * p.I,            // hq
       atom_groups * (p.I / 512) * 512,        // hsf
       (long long)p.max_rows * p.H * 2,        // O
+      gate_partials_bytes(T, p.H, p.E, num_sms(),
+                          L->gate_w && !L->gate_w_fp32 && p.E == 256),  // gate partial logits
   };
   long long o = 0;
-  for (int i = 0; i < 15; ++i) {
+  for (int i = 0; i < 16; ++i) {
     p.off[i] = o;
     o += align256(sz[i]);
   }
@@ -324,6 +366,7 @@ int dsv4_moe_workspace_layout(const dsv4_moe_layer* L, int T, long long* out, in
   for (int i = 0; i < 15; ++i) out[i] = p.off[i];
   out[15] = p.max_rows;
   out[16] = p.block_n;
+  if (n_out > 17) out[17] = p.off[15];
   return DSV4_OK;
 }
 
@@ -343,6 +386,25 @@ int dsv4_gate_topk(const float* logits, const float* bias, int T, int E, int top
   bind_device(weights);
   return launch_gate_topk(logits, bias, T, E, topk, route_scale, weights, indices,
                           static_cast<cudaStream_t>(stream));
+}
+
+long long dsv4_gate_workspace_bytes(const void* w, int w_is_fp32, int T, int H, int E) {
+  if (T < 0 || H <= 0 || E <= 0) return -1;
+  return gate_partials_bytes(T, H, E, num_sms(), !w_is_fp32 && E == 256 && H % 64 == 0 && w);
+}
+
+int dsv4_gate_route(const void* x, const void* w, int w_is_fp32, const float* bias, int T, int H,
+                    int E, int topk, float route_scale, float* logits, float* weights,
+                    int64_t* indices, void* workspace, long long workspace_bytes, void* stream) {
+  if (!x || !w || !logits || !weights || !indices || T < 0 || H <= 0 || H % 8 || E <= 0 ||
+      topk <= 0)
+    return DSV4_ERR_ARG;
+  if (E > 512 || topk > 8 || topk > E || H > 8192) return DSV4_ERR_UNSUPPORTED;
+  if (T == 0) return DSV4_OK;
+  bind_device(logits);
+  return gate_route(x, w, w_is_fp32, bias, T, H, E, topk, route_scale, logits, weights, indices,
+                    static_cast<float*>(workspace), workspace ? workspace_bytes : 0, num_sms(),
+                    static_cast<cudaStream_t>(stream));
 }
 
 int dsv4_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* scale, void* stream) {
@@ -390,9 +452,9 @@ int dsv4_moe_forward(const dsv4_moe_layer* L, const void* x, int T, void* y,
   const int64_t* ri = routing_indices;
   stage_mark(0, st);
   if (!rw) {
-    if ((rc = launch_gate_logits(x, L->gate_w, L->gate_w_fp32, T, H, E, logits, st))) return rc;
-    if ((rc = launch_gate_topk(logits, L->gate_bias, T, E, k, L->route_scale, weights, indices,
-                               st)))
+    if ((rc = gate_route(x, L->gate_w, L->gate_w_fp32, L->gate_bias, T, H, E, k, L->route_scale,
+                         logits, weights, indices, reinterpret_cast<float*>(ws + p.off[15]),
+                         p.total - p.off[15], nsm, st)))
       return rc;
     rw = weights;
     ri = indices;

@@ -447,6 +447,21 @@ int make_tmap_u8(CUtensorMap* m, const void* base, int K, int rows, int box_rows
   return r == CUDA_SUCCESS ? DSV4_OK : DSV4_ERR_CUDA;
 }
 
+// bf16 row-major matrix [rows][K], box {64 elements = 128 bytes, box_rows}.
+int make_tmap_bf16(CUtensorMap* m, const void* base, int K, int rows, int box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return DSV4_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (K % 64)) return DSV4_ERR_ARG;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                   box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? DSV4_OK : DSV4_ERR_CUDA;
+}
+
 template <int BM, bool GATED>
 static int launch_one(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& s0,
                       const CUtensorMap& s1, const CUtensorMap& b, const GemmArgs& args, int grid,

@@ -128,7 +128,10 @@ __global__ void __launch_bounds__(kGateThreads) gate_logits_kernel(
 constexpr int kMaxExpertsPerLane = 16;  // E <= 512
 constexpr int kMaxTopk = 8;
 
+// With nsplit > 1, `logits` holds nsplit partial slices [nsplit][T][E] that are
+// summed in slice order (fp32) and the sums are written to logits_out.
 __global__ void __launch_bounds__(256) gate_topk_kernel(const float* __restrict__ logits,
+                                                        int nsplit, float* __restrict__ logits_out,
                                                         const float* __restrict__ bias, int T,
                                                         int E, int k, float route_scale,
                                                         float* __restrict__ weights,
@@ -143,7 +146,10 @@ __global__ void __launch_bounds__(256) gate_topk_kernel(const float* __restrict_
   for (int i = 0; i < kMaxExpertsPerLane; ++i) {
     const int e = lane + 32 * i;
     if (i < per && e < E) {
-      const float s = sigmoid_canonical(logits[(size_t)t * E + e]);
+      float lg = logits[(size_t)t * E + e];
+      for (int sl = 1; sl < nsplit; ++sl) lg = __fadd_rn(lg, logits[((size_t)sl * T + t) * E + e]);
+      if (logits_out) logits_out[(size_t)t * E + e] = lg;
+      const float s = sigmoid_canonical(lg);
       score[i] = s;
       sel[i] = bias ? __fadd_rn(s, bias[e]) : s;
     } else {
@@ -219,12 +225,13 @@ int launch_gate_logits(const void* x, const void* w, int w_is_fp32, int T, int H
 }
 
 int launch_gate_topk(const float* logits, const float* bias, int T, int E, int k,
-                     float route_scale, float* weights, int64_t* indices, cudaStream_t st) {
+                     float route_scale, float* weights, int64_t* indices, cudaStream_t st,
+                     int nsplit, float* logits_out) {
   const int warps_per_cta = 8;
   const int grid = (T + warps_per_cta - 1) / warps_per_cta;
   if (grid > 0)
-    gate_topk_kernel<<<grid, warps_per_cta * 32, 0, st>>>(logits, bias, T, E, k, route_scale,
-                                                          weights, indices);
+    gate_topk_kernel<<<grid, warps_per_cta * 32, 0, st>>>(logits, nsplit, logits_out, bias, T, E,
+                                                          k, route_scale, weights, indices);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
 

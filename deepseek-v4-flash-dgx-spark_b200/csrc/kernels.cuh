@@ -30,7 +30,14 @@ struct GemmArgs {
 int launch_gate_logits(const void* x, const void* w, int w_is_fp32, int T, int H, int E,
                        float* logits, cudaStream_t st);
 int launch_gate_topk(const float* logits, const float* bias, int T, int E, int k,
-                     float route_scale, float* weights, int64_t* indices, cudaStream_t st);
+                     float route_scale, float* weights, int64_t* indices, cudaStream_t st,
+                     int nsplit = 1, float* logits_out = nullptr);
+int launch_gate_gemm_partials(const void* x, const void* w, int T, int H, int E, float* partials,
+                              int num_sms, cudaStream_t st);
+void gate_gemm_split_shape(int T, int H, int E, int num_sms, int* bm, int* ksplit);
+int launch_gate_gemm_topk(const void* x, const void* w, int T, int H, const float* bias, int k,
+                          float route_scale, float* logits, float* weights, int64_t* indices,
+                          int num_sms, cudaStream_t st);
 int launch_route_plan(const int64_t* indices, const float* weights, int T, int k, int E,
                       int include_shared, int block_n, int max_rows, int max_tiles, int* counts,
                       int* seg_start, int* route_slot, int* slot_token, float* slot_weight,

@@ -85,6 +85,9 @@ _SIGNATURES = {
     "dsv4_profile_enable": (c_int, [c_int]),
     "dsv4_profile_read": (c_int, [ctypes.POINTER(c_float), c_int]),
     "dsv4_gate_logits": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp]),
+    "dsv4_gate_workspace_bytes": (c_ll, [c_vp, c_int, c_int, c_int, c_int]),
+    "dsv4_gate_route": (c_int, [c_vp, c_vp, c_int, c_vp, c_int, c_int, c_int, c_int, c_float, c_vp, c_vp, c_vp,
+                                c_vp, c_ll, c_vp]),
     "dsv4_gate_topk": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_float, c_vp, c_vp, c_vp]),
     "dsv4_act_quant": (c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_vp]),
     "dsv4_materialize": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_ll, c_vp, c_ll, c_vp, c_ll, c_vp]),

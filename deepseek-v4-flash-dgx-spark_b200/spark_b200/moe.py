@@ -338,7 +338,20 @@ class Gate(nn.Module):
         return w, idx
 
     def forward(self, x: torch.Tensor, input_ids: torch.Tensor | None = None):
-        return self.route(self.logits(x))
+        x = x.reshape(-1, self.dim).to(torch.bfloat16).contiguous()
+        T = x.shape[0]
+        logits = torch.empty(T, self.n_experts, dtype=torch.float32, device=x.device)
+        w = torch.empty(T, self.topk, dtype=torch.float32, device=x.device)
+        idx = torch.empty(T, self.topk, dtype=torch.int64, device=x.device)
+        lib = _lib.load()
+        fp32 = int(self.weight.dtype == torch.float32)
+        need = lib.dsv4_gate_workspace_bytes(ptr(self.weight), fp32, T, self.dim, self.n_experts)
+        ws = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device) if need > 0 else None
+        check(lib.dsv4_gate_route(ptr(x), ptr(self.weight), fp32, ptr(self.bias), T, self.dim, self.n_experts,
+                                  self.topk, self.route_scale, ptr(logits), ptr(w), ptr(idx), ptr(ws),
+                                  max(need, 0), stream_ptr()), "dsv4_gate_route")
+        self.last_logits = logits
+        return w, idx
 
 
 # ---------------------------------------------------------------------------

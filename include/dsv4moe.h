@@ -156,6 +156,19 @@ DSV4_API int dsv4_gate_logits(const void* x, const void* w, int w_is_fp32, int T
 DSV4_API int dsv4_gate_topk(const float* logits, const float* bias, int T, int E, int topk,
                    float route_scale, float* weights, int64_t* indices, void* stream);
 
+/* Official Gate.forward(x, input_ids) -> (weights, indices) (called at
+ * lazy_official_runtime.py:983) in one call.  bf16 gate weights over 256
+ * experts run on the tensor core: large batches with the routing fused into
+ * the GEMM epilogue, small ones as split GEMM partials in `workspace`
+ * (dsv4_gate_workspace_bytes() bytes; with less, the fused form is used).
+ * Other gates run dsv4_gate_logits + dsv4_gate_topk.  Writes the fp32 logits
+ * [T,E] too; routing is bit-exact on those logits on every path. */
+DSV4_API long long dsv4_gate_workspace_bytes(const void* w, int w_is_fp32, int T, int H, int E);
+DSV4_API int dsv4_gate_route(const void* x, const void* w, int w_is_fp32, const float* bias, int T,
+                             int H, int E, int topk, float route_scale, float* logits,
+                             float* weights, int64_t* indices, void* workspace,
+                             long long workspace_bytes, void* stream);
+
 /* Official kernel.act_quant(x, 128, "ue8m0") (scripts/smoke_official_kernels.py:
  * 44-49): bf16 [M,K] -> e4m3 codes [M,K] + ue8m0 scales [M,K/128]. */
 DSV4_API int dsv4_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* scale, void* stream);

@@ -271,3 +271,72 @@ def test_moe_module_forward_shape_and_dtype(cuda_device):
     assert y.shape == x.shape and y.dtype == torch.bfloat16
     w, idx = moe.gate(x.view(-1, cfg.dim), ids.view(-1))
     assert w.shape == (6, cfg.topk) and idx.dtype == torch.int64
+
+
+def test_prefill_layer_full_size_routing_and_sampled_rows(cuda_device):
+    """T=8192 with the Zipf(1.2)-tilted gate: routing checked on every token
+    (bit-exact on the device's logits, counts = bincount), outputs checked on a
+    sample of tokens against the oracle (tokens are independent, so the sample
+    needs only the experts it touches)."""
+    from spark_b200.synthetic import CONFIGS, build_moe, make_layer
+
+    cfg = CONFIGS["prefill"]
+    T = cfg.tokens
+    layer = make_layer(cfg, seed=5, device=cuda_device)
+    moe = build_moe(layer, device=cuda_device)
+    x = layer["x"]
+    ws = torch.empty(moe.workspace_bytes(T), dtype=torch.uint8, device=cuda_device)
+    y = moe.forward_tokens(x, workspace=ws)
+    torch.cuda.synchronize()
+    _no_device_error()
+    offs = _layer_ws(moe, T)
+    k, E = cfg.topk, cfg.n_routed
+    logits = ws[offs[0]:offs[0] + T * E * 4].view(torch.float32).view(T, E).cpu().numpy()
+    w_gpu = ws[offs[1]:offs[1] + T * k * 4].view(torch.float32).view(T, k).cpu().numpy()
+    i_gpu = ws[offs[2]:offs[2] + T * k * 8].view(torch.int64).view(T, k).cpu().numpy()
+    w_ref, i_ref = O.route_from_logits(logits, layer["gate_bias"].cpu().numpy(), k, cfg.route_scale)
+    assert np.array_equal(i_gpu, i_ref)
+    assert np.array_equal(w_gpu.view(np.uint32), w_ref.view(np.uint32))
+    counts = ws[offs[3]:offs[3] + (E + 1) * 4].view(torch.int32).cpu().numpy()
+    assert np.array_equal(counts[:E], np.bincount(i_gpu.reshape(-1), minlength=E))
+    top8 = np.sort(counts[:E])[::-1][:8].sum() / (T * k)
+    assert 0.2 < top8 < 0.45, top8   # Zipf tilt: ~30% of token-slots on 8 experts
+    sample = np.random.default_rng(0).choice(T, 8, replace=False)
+    experts = sorted(set(i_gpu[sample].reshape(-1).tolist()))
+    cpu_layer = {**layer, "blocks": layer["blocks"].cpu(), "gate_w": layer["gate_w"].cpu(),
+                 "gate_bias": layer["gate_bias"].cpu(), "shared": {a: b.cpu() for a, b in layer["shared"].items()}}
+    mw = _oracle_weights(cpu_layer, experts)
+    y_ref = O.moe_forward(x[sample].float().cpu().numpy(), mw, routing=(w_gpu[sample], i_gpu[sample]))[0]
+    err = _rel_err(_bf16_np(y)[sample], y_ref)
+    assert err <= TOL, err
+
+
+@pytest.mark.parametrize("T", [1, 37, 513, 2047, 9000])
+def test_gate_route_tensor_core_path(cuda_device, T):
+    """bf16 gate over 256 experts: tcgen05 logits with routing fused in the
+    epilogue.  Logits within fp32-accumulation error of the oracle, routing
+    bit-exact on the device's own logits (ragged last tile included)."""
+    L = _lib()
+    g = torch.Generator().manual_seed(T)
+    H, E, k = 4096, 256, 6
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    w = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16)
+    bias = (torch.rand(E, generator=g) - 0.5) * 0.2
+    xd, wd, bd = x.to(cuda_device), w.to(cuda_device), bias.to(cuda_device)
+    logits = torch.empty(T, E, device=cuda_device)
+    wt = torch.empty(T, k, device=cuda_device)
+    idx = torch.empty(T, k, dtype=torch.int64, device=cuda_device)
+    need = L.load().dsv4_gate_workspace_bytes(L.ptr(wd), 0, T, H, E)
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=cuda_device)
+    L.check(L.load().dsv4_gate_route(L.ptr(xd), L.ptr(wd), 0, L.ptr(bd), T, H, E, k, 2.5, L.ptr(logits),
+                                     L.ptr(wt), L.ptr(idx), L.ptr(ws), need, L.stream_ptr()))
+    torch.cuda.synchronize()
+    _no_device_error()
+    lg = logits.cpu().numpy()
+    sel = slice(0, min(T, 600))
+    ref = O.gate_logits(x[sel].float().numpy(), w.float().numpy())
+    scale = np.abs(x[sel].float().numpy()) @ np.abs(w.float().numpy()).T
+    assert np.all(np.abs(lg[sel] - ref) <= 1e-6 * scale + 1e-7)
+    wo, io = O.route_from_logits(lg, bias.numpy(), k, 2.5)
+    assert np.array_equal(idx.cpu().numpy(), io)
+    assert np.array_equal(wt.cpu().numpy().view(np.uint32), wo.view(np.uint32))
