@@ -185,8 +185,10 @@ def run_ours(args, world, rank, local):
     with torch.cuda.stream(s):
         step()  # profiling events exist before capture
     torch.cuda.current_stream().wait_stream(s)
+    n_launch0 = lib.dsv4_kernel_launches()
     with torch.cuda.graph(graph, stream=s):
         step()
+    launches_per_step = lib.dsv4_kernel_launches() - n_launch0  # kernels in the captured layer
     graph.replay()
     torch.cuda.synchronize()
 
@@ -294,7 +296,7 @@ def run_ours(args, world, rank, local):
                 "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": y.numel() * 2,
                 "ms_per_step": round(e2e_ms, 5), "path": "MoE.forward_tokens -> dsv4_moe_forward (C ABI)"},
         "clocks": clk,
-        "gpu_launches": 7 * args.steps,
+        "gpu_launches": launches_per_step * args.steps,
     }
     return result, cfg, layer, moe
 

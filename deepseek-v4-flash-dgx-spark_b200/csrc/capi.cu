@@ -100,7 +100,7 @@ static int gate_route(const void* x, const void* w, int w_fp32, const float* bia
 // ---------------------------------------------------------------------------
 struct Plan {
   int T, E, k, H, I, S, block_n, max_rows, max_tiles;
-  long long off[16];
+  long long off[19];
   long long total;
 };
 
@@ -141,7 +141,8 @@ static Plan make_plan(const dsv4_moe_layer* L, int T) {
   p.max_rows = (int)((rows + 31) / 32 * 32);
   p.max_tiles = (int)(((long long)T * p.k + (long long)T * p.S) / p.block_n + p.E + 2);
   const long long atom_groups = p.max_rows / 32 + 4;
-  long long sz[16] = {
+  const long long nchunks = T > 0 ? (T + route_chunk_tokens(T) - 1) / route_chunk_tokens(T) : 0;
+  long long sz[19] = {
       (long long)T * p.E * 4,                 // logits
       (long long)T * p.k * 4,                 // weights
       (long long)T * p.k * 8,                 // indices
@@ -159,9 +160,12 @@ static Plan make_plan(const dsv4_moe_layer* L, int T) {
       (long long)p.max_rows * p.H * 2,        // O
       gate_partials_bytes(T, p.H, p.E, num_sms(),
                           L->gate_w && !L->gate_w_fp32 && p.E == 256),  // gate partial logits
+      (long long)p.E * nchunks * 4,           // per-chunk expert counts
+      (long long)p.E * nchunks * 4,           // per-chunk segment offsets
+      16,                                     // plan control words
   };
   long long o = 0;
-  for (int i = 0; i < 16; ++i) {
+  for (int i = 0; i < 19; ++i) {
     p.off[i] = o;
     o += align256(sz[i]);
   }
@@ -299,6 +303,8 @@ using namespace dsv4;
 extern "C" {
 
 int dsv4_version(void) { return 1; }
+
+long long dsv4_kernel_launches(void) { return g_kernel_launches.load(std::memory_order_relaxed); }
 
 const char* dsv4_status_string(int s) {
   switch (s) {
@@ -454,18 +460,23 @@ int dsv4_moe_forward(const dsv4_moe_layer* L, const void* x, int T, void* y,
   if (!rw) {
     if ((rc = gate_route(x, L->gate_w, L->gate_w_fp32, L->gate_bias, T, H, E, k, L->route_scale,
                          logits, weights, indices, reinterpret_cast<float*>(ws + p.off[15]),
-                         p.total - p.off[15], nsm, st)))
+                         p.off[16] - p.off[15], nsm, st)))
       return rc;
     rw = weights;
     ri = indices;
   }
   stage_mark(1, st);
-  if ((rc = launch_route_plan(ri, rw, T, k, E, p.S, p.block_n, p.max_rows, p.max_tiles, counts,
-                              seg_start, route_slot, slot_token, slot_weight, tiles, n_tiles, st)))
+  int* chunk_cnt = reinterpret_cast<int*>(ws + p.off[16]);
+  int* chunk_base = reinterpret_cast<int*>(ws + p.off[17]);
+  int* ctrl = reinterpret_cast<int*>(ws + p.off[18]);
+  if ((rc = launch_route_plan(ri, T, k, E, 0, p.S ? T : 0, p.block_n, p.max_rows, p.max_tiles,
+                              chunk_cnt, chunk_base, ctrl, counts, seg_start, tiles, n_tiles,
+                              slot_token, slot_weight, st)))
     return rc;
   stage_mark(2, st);
-  if ((rc = launch_permute_quant(x, H, slot_token, seg_start + E + 1, p.max_rows, xq, xsf, nsm,
-                                 st)))
+  if ((rc = launch_route_scatter(x, T, nullptr, 0, ri, rw, T, k, E, H, p.S ? T : 0, seg_start,
+                                 chunk_base, ctrl, route_slot, slot_token, slot_weight, xq, xsf,
+                                 nsm, st)))
     return rc;
   stage_mark(3, st);
 

@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "dsv4moe.h"
 
 namespace dsv4 {
@@ -22,6 +24,11 @@ namespace dsv4 {
 __device__ int g_dsv4_device_error = 0;
 
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s
+
+// Kernels enqueued by the library (host side; a captured graph counts each of
+// its kernels once), read by dsv4_kernel_launches().
+inline std::atomic<long long> g_kernel_launches{0};
+inline void count_launch() { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
 
 __device__ __forceinline__ void record_error(int code) {
   atomicCAS(&g_dsv4_device_error, 0, code);

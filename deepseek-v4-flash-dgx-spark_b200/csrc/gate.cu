@@ -122,36 +122,55 @@ __global__ void __launch_bounds__(kGateThreads) gate_logits_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// Top-k.  One warp per token; lane l holds experts l, l+32, ...  k rounds of a
-// warp arg-max on (score + bias), ties to the lower expert id.
+// Top-k.  One CTA per token.  The selecting warp's lane l holds experts l,
+// l+32, ...; k rounds of a warp arg-max on (score + bias), ties to the lower
+// expert id.
 // ---------------------------------------------------------------------------
 constexpr int kMaxExpertsPerLane = 16;  // E <= 512
 constexpr int kMaxTopk = 8;
+constexpr int kSliceBatch = 8;  // split-K slices loaded together
 
 // With nsplit > 1, `logits` holds nsplit partial slices [nsplit][T][E] that are
 // summed in slice order (fp32) and the sums are written to logits_out.
-__global__ void __launch_bounds__(256) gate_topk_kernel(const float* __restrict__ logits,
+__global__ void __launch_bounds__(512) gate_topk_kernel(const float* __restrict__ logits,
                                                         int nsplit, float* __restrict__ logits_out,
                                                         const float* __restrict__ bias, int T,
                                                         int E, int k, float route_scale,
                                                         float* __restrict__ weights,
                                                         int64_t* __restrict__ indices) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  // One CTA per token, one thread per expert: each thread sums its expert's
+  // split-K slices in slice order (loads issued kSliceBatch at a time so they
+  // are in flight together), then warp 0 selects the top k from shared memory.
+  __shared__ float s_score[kMaxExpertsPerLane * 32], s_sel[kMaxExpertsPerLane * 32];
+  const int t = blockIdx.x;
   const int lane = threadIdx.x & 31;
-  if (warp >= T) return;
-  const int t = warp;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const float* src = logits + (size_t)t * E + e;
+    const size_t slice = (size_t)T * E;
+    float lg = src[0];
+    for (int sl0 = 1; sl0 < nsplit; sl0 += kSliceBatch) {
+      float v[kSliceBatch];
+#pragma unroll
+      for (int j = 0; j < kSliceBatch; ++j) v[j] = sl0 + j < nsplit ? src[(size_t)(sl0 + j) * slice] : 0.f;
+#pragma unroll
+      for (int j = 0; j < kSliceBatch; ++j)
+        if (sl0 + j < nsplit) lg = __fadd_rn(lg, v[j]);
+    }
+    if (logits_out) logits_out[(size_t)t * E + e] = lg;
+    const float s = sigmoid_canonical(lg);
+    s_score[e] = s;
+    s_sel[e] = bias ? __fadd_rn(s, bias[e]) : s;
+  }
+  __syncthreads();
+  if (threadIdx.x >= 32) return;
   float score[kMaxExpertsPerLane], sel[kMaxExpertsPerLane];
   const int per = (E + 31) / 32;
 #pragma unroll
   for (int i = 0; i < kMaxExpertsPerLane; ++i) {
     const int e = lane + 32 * i;
     if (i < per && e < E) {
-      float lg = logits[(size_t)t * E + e];
-      for (int sl = 1; sl < nsplit; ++sl) lg = __fadd_rn(lg, logits[((size_t)sl * T + t) * E + e]);
-      if (logits_out) logits_out[(size_t)t * E + e] = lg;
-      const float s = sigmoid_canonical(lg);
-      score[i] = s;
-      sel[i] = bias ? __fadd_rn(s, bias[e]) : s;
+      score[i] = s_score[e];
+      sel[i] = s_sel[e];
     } else {
       score[i] = 0.f;
       sel[i] = -INFINITY;
@@ -213,11 +232,13 @@ int launch_gate_logits(const void* x, const void* w, int w_is_fp32, int T, int H
   if (w_is_fp32) {
     cudaFuncSetAttribute(gate_logits_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
+    count_launch();
     gate_logits_kernel<true><<<grid, kGateThreads, smem, st>>>(static_cast<const __nv_bfloat16*>(x), w, T,
                                                       H, E, logits);
   } else {
     cudaFuncSetAttribute(gate_logits_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
+    count_launch();
     gate_logits_kernel<false><<<grid, kGateThreads, smem, st>>>(static_cast<const __nv_bfloat16*>(x), w,
                                                        T, H, E, logits);
   }
@@ -227,11 +248,12 @@ int launch_gate_logits(const void* x, const void* w, int w_is_fp32, int T, int H
 int launch_gate_topk(const float* logits, const float* bias, int T, int E, int k,
                      float route_scale, float* weights, int64_t* indices, cudaStream_t st,
                      int nsplit, float* logits_out) {
-  const int warps_per_cta = 8;
-  const int grid = (T + warps_per_cta - 1) / warps_per_cta;
-  if (grid > 0)
-    gate_topk_kernel<<<grid, warps_per_cta * 32, 0, st>>>(logits, nsplit, logits_out, bias, T, E,
-                                                          k, route_scale, weights, indices);
+  const int threads = std::min(kMaxExpertsPerLane * 32, (E + 31) / 32 * 32);
+  if (T > 0) {
+    count_launch();
+    gate_topk_kernel<<<T, threads, 0, st>>>(logits, nsplit, logits_out, bias, T, E, k, route_scale,
+                                            weights, indices);
+  }
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
 

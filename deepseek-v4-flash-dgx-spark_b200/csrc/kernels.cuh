@@ -38,10 +38,17 @@ void gate_gemm_split_shape(int T, int H, int E, int num_sms, int* bm, int* kspli
 int launch_gate_gemm_topk(const void* x, const void* w, int T, int H, const float* bias, int k,
                           float route_scale, float* logits, float* weights, int64_t* indices,
                           int num_sms, cudaStream_t st);
-int launch_route_plan(const int64_t* indices, const float* weights, int T, int k, int E,
-                      int include_shared, int block_n, int max_rows, int max_tiles, int* counts,
-                      int* seg_start, int* route_slot, int* slot_token, float* slot_weight,
-                      int4* tiles, int* n_tiles, cudaStream_t st);
+int route_chunk_tokens(int T);
+int launch_route_plan(const int64_t* indices, int T, int k, int E, int allow_skip,
+                      int shared_rows, int block_n, int max_rows, int max_tiles, int* chunk_cnt,
+                      int* chunk_base, int* ctrl, int* counts, int* seg_start, int4* tiles,
+                      int* n_tiles, int* slot_token, float* slot_weight, cudaStream_t st);
+int launch_route_scatter(const void* x, int n_x_rows, const uint8_t* rows_in,
+                         long long rows_in_stride, const int64_t* indices, const float* weights,
+                         int T, int k, int E, int H, int shared_rows, const int* seg_start,
+                         const int* chunk_base, const int* ctrl, int* route_slot, int* slot_token,
+                         float* slot_weight, uint8_t* xq, uint8_t* sfb, int num_sms,
+                         cudaStream_t st);
 int launch_permute_quant(const void* x, int H, const int* slot_token, const int* total_rows_ptr,
                          int max_rows, uint8_t* xq, uint8_t* sfb, int num_sms, cudaStream_t st);
 int launch_single_segment_plan(int T, int seg, int block_n, int rows_pad, const float* w,

@@ -142,17 +142,20 @@ int launch_materialize(const uint8_t* slab, const long long* src_off, const int*
                        long long bf16_slot_stride, int num_sms, cudaStream_t st) {
   if (n <= 0) return DSV4_OK;
   if (arena) {
+    count_launch();
     materialize_copy_kernel<<<grid_for((block_bytes >> 4) * n, num_sms), 256, 0, st>>>(
         slab, src_off, dst_slot, n, block_bytes, arena, slot_stride);
   }
   if (sf) {
     const long long rows = 3LL * inter * hidden / 32 / 16 * n;
+    count_launch();
     build_sf_fp4_kernel<<<grid_for(rows, num_sms), 256, 0, st>>>(slab, src_off, 0, dst_slot, n,
                                                                  hidden, inter, sf,
                                                                  sf_slot_stride);
   }
   if (bf16_out) {
     const long long groups = 3LL * inter * hidden / 8 * n;
+    count_launch();
     decode_bf16_kernel<<<grid_for(groups, num_sms), 256, 0, st>>>(
         slab, src_off, dst_slot, n, hidden, inter, static_cast<__nv_bfloat16*>(bf16_out),
         bf16_slot_stride);
@@ -165,6 +168,7 @@ int launch_build_sf_fp4_arena(const uint8_t* arena, long long slot_stride, const
                               int num_sms, cudaStream_t st) {
   if (n <= 0) return DSV4_OK;
   const long long rows = 3LL * inter * hidden / 32 / 16 * n;
+  count_launch();
   build_sf_fp4_kernel<<<grid_for(rows, num_sms), 256, 0, st>>>(arena, nullptr, slot_stride, slots,
                                                                n, hidden, inter, sf,
                                                                sf_slot_stride);
@@ -174,6 +178,7 @@ int launch_build_sf_fp4_arena(const uint8_t* arena, long long slot_stride, const
 int launch_build_sf_fp8(const uint8_t* scale, int rows, int K, uint8_t* atoms, int num_sms,
                         cudaStream_t st) {
   const long long work = (long long)(rows / 128) * (K / 128) * 32;
+  count_launch();
   build_sf_fp8_kernel<<<grid_for(work, num_sms), 256, 0, st>>>(scale, rows, K, atoms);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }

@@ -11,73 +11,92 @@
 namespace dsv4 {
 
 // ---------------------------------------------------------------------------
-// Route plan (one CTA).  Stable counting sort of the T*k (token, rank) routes
-// into per-expert segments: inside a segment rows follow token order, which is
-// the order torch.where gives.  Segment sizes are padded to 32 rows so every
-// GEMM tile starts on a 32-row boundary of the activation scale atoms.  The
-// shared expert is segment E and holds every token.
+// Route plan: a stable counting sort of the T*k (token, rank) routes into
+// per-expert segments, in three launches that use the whole GPU:
+//   route_count    per chunk of `chunk` tokens, a histogram over experts
+//   route_scan     per expert, exclusive scan of its chunk counts (token
+//                  order); the last CTA to finish lays out the segments
+//   route_scatter  per chunk, each route's rank among earlier routes of the
+//                  chunk with the same expert gives its slot; the chunk's token
+//                  rows are quantized once and written to all their slots
+// Inside a segment rows follow token order, which is the order torch.where
+// gives.  Segment sizes are padded to 32 rows so every GEMM tile starts on a
+// 32-row boundary of the activation scale atoms.  The shared expert is
+// segment E and holds the first `shared_rows` tokens.
+//
+// ctrl[0] counts finished route_scan CTAs, ctrl[1] flags an invalid index,
+// ctrl[2] flags a failed plan; the caller zeroes ctrl before route_count.
 // ---------------------------------------------------------------------------
-constexpr int kPlanThreads = 1024;
-constexpr int kPlanWarps = kPlanThreads / 32;
 constexpr int kSegAlign = 32;
+constexpr int kMaxK = 8;
+constexpr int kMaxChunk = 32;  // tokens per chunk (chunk * k <= 256 threads)
+constexpr int kScanThreads = 256;
+constexpr int kMaxSegments = 513;
 
-__global__ void __launch_bounds__(kPlanThreads) route_plan_kernel(
-    const int64_t* __restrict__ indices, const float* __restrict__ weights, int T, int k, int E,
-    int include_shared, int block_n, int max_rows, int max_tiles, int* __restrict__ counts,
-    int* __restrict__ seg_start, int* __restrict__ route_slot, int* __restrict__ slot_token,
-    float* __restrict__ slot_weight, int4* __restrict__ tiles, int* __restrict__ n_tiles) {
-  extern __shared__ int sm[];
-  const int NS = E + 1;                  // segments: E routed + shared
-  int* cnt = sm;                         // [NS]
-  int* tbase = cnt + NS;                 // [NS + 1] tile base per segment
-  int* warp_cnt = tbase + NS + 1;        // [kPlanWarps][NS]
-  __shared__ int s_total_rows, s_total_tiles, s_bad;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int i = tid; i < NS; i += kPlanThreads) cnt[i] = 0;
-  for (int i = tid; i < kPlanWarps * NS; i += kPlanThreads) warp_cnt[i] = 0;
-  if (tid == 0) s_bad = 0;
+__global__ void __launch_bounds__(256) route_count_kernel(const int64_t* __restrict__ indices,
+                                                          int T, int k, int E, int allow_skip,
+                                                          int chunk, int nchunks,
+                                                          int* __restrict__ chunk_cnt,
+                                                          int* __restrict__ ctrl) {
+  __shared__ int hist[kMaxSegments];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
   __syncthreads();
-
-  const int n_routes = T * k;
-  for (int base = 0; base < n_routes; base += kPlanThreads) {
-    const int i = base + tid;
-    int e = -1;
-    if (i < n_routes) {
-      const int64_t v = indices[i];
-      if (v >= 0 && v < E) e = static_cast<int>(v);
-      else s_bad = 1;
-    }
-    const unsigned mask = __match_any_sync(0xffffffffu, e);
-    const int rank_w = __popc(mask & ((1u << lane) - 1u));
-    const bool leader = (__ffs(mask) - 1) == lane;
-    if (leader && e >= 0) warp_cnt[warp * NS + e] = __popc(mask);
-    __syncthreads();
-    for (int s = tid; s < E; s += kPlanThreads) {
-      int run = cnt[s];
-      for (int w = 0; w < kPlanWarps; ++w) {
-        const int c = warp_cnt[w * NS + s];
-        if (c) {
-          warp_cnt[w * NS + s] = run;
-          run += c;
-        }
-      }
-      cnt[s] = run;
-    }
-    __syncthreads();
-    if (e >= 0) route_slot[i] = warp_cnt[warp * NS + e] + rank_w;  // rank inside segment
-    __syncthreads();
-    if (leader && e >= 0) warp_cnt[warp * NS + e] = 0;
-    __syncthreads();
+  const int c = blockIdx.x;
+  const int r1 = min(T, (c + 1) * chunk) * k;
+  for (int i = c * chunk * k + threadIdx.x; i < r1; i += blockDim.x) {
+    const int64_t v = indices[i];
+    if (v >= 0 && v < E) atomicAdd(&hist[v], 1);
+    else if (!(allow_skip && v == -1)) atomicOr(&ctrl[1], 1);
   }
-  if (tid == 0) cnt[E] = include_shared ? T : 0;
   __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) chunk_cnt[(size_t)e * nchunks + c] = hist[e];
+}
 
-  // exclusive scans of padded row counts and of tile counts (warp 0)
+__global__ void __launch_bounds__(kScanThreads) route_scan_kernel(
+    const int* __restrict__ chunk_cnt, int nchunks, int E, int shared_rows, int block_n,
+    int max_rows, int max_tiles, int* __restrict__ chunk_base, int* __restrict__ counts,
+    int* __restrict__ seg_start, int4* __restrict__ tiles, int* __restrict__ n_tiles,
+    int* __restrict__ slot_token, float* __restrict__ slot_weight, int* __restrict__ ctrl) {
+  __shared__ int s_cnt[kMaxSegments], s_start[kMaxSegments + 1], s_tbase[kMaxSegments + 1];
+  __shared__ int s_last, s_fail;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // one warp per expert: exclusive scan of its chunk counts in chunk (token) order
+  const int e = blockIdx.x * (kScanThreads / 32) + warp;
+  if (e < E) {
+    const int* src = chunk_cnt + (size_t)e * nchunks;
+    int* dst = chunk_base + (size_t)e * nchunks;
+    int run = 0;
+    for (int c0 = 0; c0 < nchunks; c0 += 32) {
+      const int c = c0 + lane;
+      const int v = c < nchunks ? src[c] : 0;
+      int inc = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int a = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += a;
+      }
+      if (c < nchunks) dst[c] = run + inc - v;
+      run += __shfl_sync(0xffffffffu, inc, 31);
+    }
+    if (lane == 0) counts[e] = run;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(&ctrl[0], 1) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+
+  // the last CTA: padded segment offsets, tiles, padding rows
+  const int NS = E + 1;
+  for (int s = tid; s < NS; s += kScanThreads)
+    s_cnt[s] = s < E ? __ldcg(counts + s) : shared_rows;
+  __syncthreads();
   if (warp == 0) {
     int row_run = 0, tile_run = 0;
     for (int s0 = 0; s0 < NS; s0 += 32) {
       const int s = s0 + lane;
-      const int c = s < NS ? cnt[s] : 0;
+      const int c = s < NS ? s_cnt[s] : 0;
       const int rows = (c + kSegAlign - 1) / kSegAlign * kSegAlign;
       const int nt = (c + block_n - 1) / block_n;
       int r_inc = rows, t_inc = nt;
@@ -91,61 +110,195 @@ __global__ void __launch_bounds__(kPlanThreads) route_plan_kernel(
         }
       }
       if (s < NS) {
-        seg_start[s] = row_run + r_inc - rows;
-        tbase[s] = tile_run + t_inc - nt;
+        s_start[s] = row_run + r_inc - rows;
+        s_tbase[s] = tile_run + t_inc - nt;
       }
       row_run += __shfl_sync(0xffffffffu, r_inc, 31);
       tile_run += __shfl_sync(0xffffffffu, t_inc, 31);
     }
     if (lane == 0) {
-      seg_start[NS] = row_run;
-      tbase[NS] = tile_run;
-      s_total_rows = row_run;
-      s_total_tiles = tile_run;
+      s_start[NS] = row_run;
+      s_tbase[NS] = tile_run;
+      const int bad = __ldcg(ctrl + 1);
+      s_fail = bad || row_run > max_rows || tile_run > max_tiles;
+      if (s_fail) {
+        record_error(bad ? DSV4_DEVERR_BAD_INDEX : DSV4_DEVERR_PLAN_OVERFLOW);
+        ctrl[2] = 1;
+      }
     }
   }
   __syncthreads();
-  if (s_total_rows > max_rows || s_total_tiles > max_tiles || s_bad) {
-    if (tid == 0) {
-      record_error(s_bad ? DSV4_DEVERR_BAD_INDEX : DSV4_DEVERR_PLAN_OVERFLOW);
-      *n_tiles = 0;
-    }
+  if (s_fail) {
+    if (tid == 0) *n_tiles = 0;
     return;
   }
-
-  for (int i = tid; i < n_routes; i += kPlanThreads) {
-    const int e = static_cast<int>(indices[i]);
-    const int slot = seg_start[e] + route_slot[i];
-    route_slot[i] = slot;
-    slot_token[slot] = i / k;
-    slot_weight[slot] = weights[i];
+  for (int s = tid; s <= NS; s += kScanThreads) {
+    seg_start[s] = s_start[s];
+    if (s < NS) counts[s] = s_cnt[s];
   }
-  if (include_shared) {
-    for (int t = tid; t < T; t += kPlanThreads) {
-      slot_token[seg_start[E] + t] = t;
-      slot_weight[seg_start[E] + t] = 1.0f;
-    }
-  }
-  for (int s = tid; s < NS; s += kPlanThreads) {
-    const int c = cnt[s];
-    counts[s] = c;
-    for (int r = seg_start[s] + c; r < seg_start[s + 1]; ++r) {
+  for (int s = warp; s < NS; s += kScanThreads / 32) {
+    const int c = s_cnt[s], base = s_start[s], nt = s_tbase[s + 1] - s_tbase[s];
+    for (int m = lane; m < nt; m += 32)
+      tiles[s_tbase[s] + m] = make_int4(s, base + m * block_n, min(block_n, c - m * block_n), 0);
+    for (int r = base + c + lane; r < s_start[s + 1]; r += 32) {
       slot_token[r] = -1;
       slot_weight[r] = 0.f;
     }
-    const int nt = tbase[s + 1] - tbase[s];
-    for (int m = 0; m < nt; ++m)
-      tiles[tbase[s] + m] = make_int4(s, seg_start[s] + m * block_n, min(block_n, c - m * block_n), 0);
   }
-  if (tid == 0) *n_tiles = s_total_tiles;
+  if (tid == 0) *n_tiles = s_tbase[NS];
+}
+
+// Per-128 act_quant of one token row by one warp, the codes and scales written
+// to every slot in `slots` (smem, -1 = none).  The row is walked in quads of
+// four 128-wide k tiles: lane l owns elements 16l..16l+15 of a quad (k tile
+// 4q + l/8), so the 8 lanes of a k tile reduce its amax in 3 shuffles, codes
+// leave as one 16-byte store per lane and slot, and the quad's four scales as
+// one 32-bit word.  Scales go to the sliding k-packed atoms: atom (g, q) holds
+// rows 32g .. 32g+127 for k tiles 4q .. 4q+3, row r / tile kt at byte
+// (r%32)*16 + ((r/32)-g)*4 + kt%4, so one quad of one row is 4 consecutive
+// bytes in each of the (up to) four atoms that contain the row.
+constexpr int kQuadsInFlight = 2;
+constexpr int kQuantGroup = 8;  // k tiles of loads in flight in quant_row; the least a scatter CTA takes
+
+__device__ __forceinline__ void scatter_row(const __nv_bfloat16* __restrict__ xrow,
+                                            const uint8_t* __restrict__ qrow, int q0, int q1,
+                                            int KT, int H, const int* slots, int nslots, int lane,
+                                            uint8_t* __restrict__ xq, uint8_t* __restrict__ sfb) {
+  for (int qa = q0; qa < q1; qa += kQuadsInFlight) {
+    uint4 raw[kQuadsInFlight][2];
+    uint4 code[kQuadsInFlight];
+    uint32_t sc[kQuadsInFlight];
+#pragma unroll
+    for (int g = 0; g < kQuadsInFlight; ++g) {
+      raw[g][0] = raw[g][1] = code[g] = make_uint4(0, 0, 0, 0);
+      sc[g] = 0;
+      if (qa + g < q1) {
+        const size_t e0 = (size_t)(qa + g) * 512 + lane * 16;
+        if (xrow) {
+          raw[g][0] = *reinterpret_cast<const uint4*>(xrow + e0);
+          raw[g][1] = *reinterpret_cast<const uint4*>(xrow + e0 + 8);
+        } else {
+          code[g] = *reinterpret_cast<const uint4*>(qrow + e0);
+          sc[g] = qrow[H + (qa + g) * 4 + (lane >> 3)];
+        }
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < kQuadsInFlight; ++g) {
+      if (qa + g >= q1) break;
+      if (xrow) {
+        float v[16];
+        const __nv_bfloat16* b0 = reinterpret_cast<const __nv_bfloat16*>(&raw[g][0]);
+        const __nv_bfloat16* b1 = reinterpret_cast<const __nv_bfloat16*>(&raw[g][1]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          v[i] = __bfloat162float(b0[i]);
+          v[8 + i] = __bfloat162float(b1[i]);
+        }
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const int e = act_scale_exp(amax);
+        const float inv = exp2i(-e);
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          w[j] = 0;
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            w[j] |= static_cast<uint32_t>(f32_to_e4m3(v[4 * j + i] * inv)) << (8 * i);
+        }
+        code[g] = make_uint4(w[0], w[1], w[2], w[3]);
+        sc[g] = static_cast<uint32_t>(e + 127);
+      }
+      // the quad's four scales, k tile j held by lane 8j
+      const uint32_t s4 = __shfl_sync(0xffffffffu, sc[g], 0) | (__shfl_sync(0xffffffffu, sc[g], 8) << 8) |
+                          (__shfl_sync(0xffffffffu, sc[g], 16) << 16) |
+                          (__shfl_sync(0xffffffffu, sc[g], 24) << 24);
+      for (int d = 0; d < nslots; ++d) {
+        const int slot = slots[d];
+        if (slot < 0) continue;
+        *reinterpret_cast<uint4*>(xq + (size_t)slot * H + (size_t)(qa + g) * 512 + lane * 16) = code[g];
+        if (lane < 4) {
+          const int ga = (slot >> 5) - lane;
+          if (ga >= 0)
+            *reinterpret_cast<uint32_t*>(sfb + ((size_t)ga * (KT >> 2) + (qa + g)) * 512 + (slot & 31) * 16 +
+                                         lane * 4) = s4;
+        }
+      }
+    }
+  }
+}
+
+// grid (nchunks, ksplit): CTA (c, y) places chunk c's routes and writes quads
+// [y*KQ/ksplit, (y+1)*KQ/ksplit) (KQ = H/512) of its token rows.  Tokens t < n_x_rows are
+// quantized from x (bf16); later tokens are fp8 rows of `rows_in` (codes, then
+// H/128 scale bytes) copied as they are.
+__global__ void __launch_bounds__(256) route_scatter_kernel(
+    const __nv_bfloat16* __restrict__ x, int n_x_rows, const uint8_t* __restrict__ rows_in,
+    long long rows_in_stride, const int64_t* __restrict__ indices, const float* __restrict__ weights,
+    int T, int k, int E, int H, int shared_rows, int chunk, int nchunks,
+    const int* __restrict__ seg_start, const int* __restrict__ chunk_base, const int* __restrict__ ctrl,
+    int* __restrict__ route_slot, int* __restrict__ slot_token, float* __restrict__ slot_weight,
+    uint8_t* __restrict__ xq, uint8_t* __restrict__ sfb) {
+  __shared__ int s_e[kMaxChunk * kMaxK];
+  __shared__ int s_slot[kMaxChunk][kMaxK + 1];
+  if (__ldcg(ctrl + 2)) return;
+  const int c = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int t0 = c * chunk;
+  const int nt = min(chunk, T - t0);
+  const int nr = nt * k, i0 = t0 * k;
+  const bool owner = blockIdx.y == 0;
+  if (tid < nr) {
+    const int64_t v = indices[i0 + tid];
+    s_e[tid] = (v >= 0 && v < E) ? static_cast<int>(v) : -1;
+  }
+  __syncthreads();
+  if (tid < nr) {
+    const int e = s_e[tid];
+    int slot = -1;
+    if (e >= 0) {
+      int rank = 0;
+      for (int j = 0; j < tid; ++j) rank += s_e[j] == e;
+      slot = seg_start[e] + chunk_base[(size_t)e * nchunks + c] + rank;
+      if (owner) {
+        slot_token[slot] = t0 + tid / k;
+        slot_weight[slot] = weights[i0 + tid];
+      }
+    }
+    if (owner) route_slot[i0 + tid] = slot;
+    s_slot[tid / k][tid % k] = slot;
+  }
+  if (tid < nt) {
+    const int t = t0 + tid;
+    int slot = -1;
+    if (t < shared_rows) {
+      slot = seg_start[E] + t;
+      if (owner) {
+        slot_token[slot] = t;
+        slot_weight[slot] = 1.0f;
+      }
+    }
+    s_slot[tid][k] = slot;
+  }
+  __syncthreads();
+  const int KT = H / 128, KQ = KT / 4;
+  const int per = (KQ + gridDim.y - 1) / gridDim.y;
+  const int q0 = blockIdx.y * per, q1 = min(KQ, q0 + per);
+  for (int lt = warp; lt < nt; lt += blockDim.x / 32) {
+    const int t = t0 + lt;
+    const __nv_bfloat16* xrow = t < n_x_rows ? x + (size_t)t * H : nullptr;
+    const uint8_t* qrow = t < n_x_rows ? nullptr : rows_in + (size_t)(t - n_x_rows) * rows_in_stride;
+    scatter_row(xrow, qrow, q0, q1, KT, H, s_slot[lt], k + 1, lane, xq, sfb);
+  }
 }
 
 // ---------------------------------------------------------------------------
-// Per-128 act_quant of one row by one warp: lane l owns elements 4l..4l+3 of
-// each 128-wide block.  Blocks are processed 8 at a time with all 8 loads in
-// flight before any is used (the rows come from L2/DRAM: latency-bound).
+// Per-128 act_quant of one row by one warp into a single destination row (the
+// expert forward's identity plan and the plain act_quant entry point).
 // ---------------------------------------------------------------------------
-constexpr int kQuantGroup = 8;
 
 template <typename ScaleSink>
 __device__ __forceinline__ void quant_row(const __nv_bfloat16* __restrict__ src, bool valid,
@@ -225,8 +378,6 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const __nv_bfloat16* __r
 // (before w2), so this is a plain ordered sum.  One CTA per token, one thread
 // per 8-element chunk: a thread's k+1 row loads are all in flight at once.
 // ---------------------------------------------------------------------------
-constexpr int kMaxK = 8;
-
 __global__ void __launch_bounds__(512) combine_kernel(const __nv_bfloat16* __restrict__ O, int H,
                                                       const int* __restrict__ route_slot,
                                                       const int64_t* __restrict__ indices, int T,
@@ -309,19 +460,44 @@ __global__ void single_segment_plan_kernel(int T, int seg, int block_n, int rows
 // ---------------------------------------------------------------------------
 // host launchers
 // ---------------------------------------------------------------------------
-int launch_route_plan(const int64_t* indices, const float* weights, int T, int k, int E,
-                      int include_shared, int block_n, int max_rows, int max_tiles, int* counts,
-                      int* seg_start, int* route_slot, int* slot_token, float* slot_weight,
-                      int4* tiles, int* n_tiles, cudaStream_t st) {
-  const int NS = E + 1;
-  const size_t smem = (size_t)(NS + NS + 1 + kPlanWarps * NS) * sizeof(int);
-  if (cudaFuncSetAttribute(route_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem) != cudaSuccess)
-    return DSV4_ERR_CUDA;
-  route_plan_kernel<<<1, kPlanThreads, smem, st>>>(indices, weights, T, k, E, include_shared,
-                                                   block_n, max_rows, max_tiles, counts, seg_start,
-                                                   route_slot, slot_token, slot_weight, tiles,
-                                                   n_tiles);
+int route_chunk_tokens(int T) { return T <= 1024 ? 8 : kMaxChunk; }
+
+int launch_route_plan(const int64_t* indices, int T, int k, int E, int allow_skip,
+                      int shared_rows, int block_n, int max_rows, int max_tiles, int* chunk_cnt,
+                      int* chunk_base, int* ctrl, int* counts, int* seg_start, int4* tiles,
+                      int* n_tiles, int* slot_token, float* slot_weight, cudaStream_t st) {
+  if (T <= 0 || k > kMaxK || E + 1 > kMaxSegments) return DSV4_ERR_ARG;
+  const int chunk = route_chunk_tokens(T);
+  const int nchunks = (T + chunk - 1) / chunk;
+  if (cudaMemsetAsync(ctrl, 0, 4 * sizeof(int), st) != cudaSuccess) return DSV4_ERR_CUDA;
+  count_launch();
+  route_count_kernel<<<nchunks, 256, 0, st>>>(indices, T, k, E, allow_skip, chunk, nchunks,
+                                              chunk_cnt, ctrl);
+  count_launch();
+  route_scan_kernel<<<(E + kScanThreads / 32 - 1) / (kScanThreads / 32), kScanThreads, 0, st>>>(chunk_cnt, nchunks, E, shared_rows, block_n,
+                                                max_rows, max_tiles, chunk_base, counts, seg_start,
+                                                tiles, n_tiles, slot_token, slot_weight, ctrl);
+  return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
+}
+
+int launch_route_scatter(const void* x, int n_x_rows, const uint8_t* rows_in,
+                         long long rows_in_stride, const int64_t* indices, const float* weights,
+                         int T, int k, int E, int H, int shared_rows, const int* seg_start,
+                         const int* chunk_base, const int* ctrl, int* route_slot, int* slot_token,
+                         float* slot_weight, uint8_t* xq, uint8_t* sfb, int num_sms,
+                         cudaStream_t st) {
+  if (T <= 0) return DSV4_OK;
+  const int chunk = route_chunk_tokens(T);
+  const int nchunks = (T + chunk - 1) / chunk;
+  const int KT = H / 128;
+  int ksplit = (4 * num_sms) / nchunks;
+  ksplit = ksplit < 1 ? 1 : (ksplit > KT / kQuantGroup ? KT / kQuantGroup : ksplit);
+  if (ksplit < 1) ksplit = 1;
+  count_launch();
+  route_scatter_kernel<<<dim3(nchunks, ksplit), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(x), n_x_rows, rows_in, rows_in_stride, indices, weights, T,
+      k, E, H, shared_rows, chunk, nchunks, seg_start, chunk_base, ctrl, route_slot, slot_token,
+      slot_weight, xq, sfb);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
 
@@ -331,6 +507,7 @@ int launch_permute_quant(const void* x, int H, const int* slot_token, const int*
   int grid = (max_rows + warps - 1) / warps;
   grid = grid < num_sms * 8 ? grid : num_sms * 8;
   if (grid < 1) grid = 1;
+  count_launch();
   permute_quant_kernel<<<grid, warps * 32, 0, st>>>(static_cast<const __nv_bfloat16*>(x), H,
                                                     slot_token, total_rows_ptr, xq, sfb);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
@@ -340,6 +517,7 @@ int launch_single_segment_plan(int T, int seg, int block_n, int rows_pad, const 
                                int* slot_token, float* slot_weight, int4* tiles, int* n_tiles,
                                int* total_rows, cudaStream_t st) {
   const int grid = (rows_pad + 255) / 256;
+  count_launch();
   single_segment_plan_kernel<<<grid > 0 ? grid : 1, 256, 0, st>>>(
       T, seg, block_n, rows_pad, w, slot_token, slot_weight, tiles, n_tiles, total_rows);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
@@ -351,6 +529,7 @@ int launch_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* s, int nu
   int grid = (M + warps - 1) / warps;
   grid = grid < num_sms * 8 ? grid : num_sms * 8;
   if (grid < 1) return DSV4_OK;
+  count_launch();
   act_quant_kernel<<<grid, warps * 32, 0, st>>>(static_cast<const __nv_bfloat16*>(x), M, K, q, s);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
@@ -358,6 +537,7 @@ int launch_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* s, int nu
 int launch_combine(const void* O, int H, const int* route_slot, const int64_t* indices, int T,
                    int k, const int* shared_base, void* y, cudaStream_t st) {
   if (T <= 0) return DSV4_OK;
+  count_launch();
   combine_kernel<<<T, H / 8 < 512 ? H / 8 : 512, 0, st>>>(static_cast<const __nv_bfloat16*>(O), H, route_slot, indices,
                                     T, k, shared_base, static_cast<__nv_bfloat16*>(y));
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;

@@ -73,6 +73,7 @@ class MoELayerDesc(ctypes.Structure):
 
 _SIGNATURES = {
     "dsv4_version": (c_int, []),
+    "dsv4_kernel_launches": (c_ll, []),
     "dsv4_status_string": (ctypes.c_char_p, [c_int]),
     "dsv4_device_error": (c_int, [c_int, c_ip]),
     "dsv4_moe_workspace_bytes": (c_ll, [ctypes.POINTER(MoELayerDesc), c_int]),

@@ -50,6 +50,11 @@ extern "C" {
 #define DSV4_DEVERR_PLAN_OVERFLOW 105
 
 DSV4_API int dsv4_version(void);
+/* Number of kernels the library has enqueued in this process (every launch
+ * counts once, including launches captured into a CUDA graph; graph replays
+ * do not pass through the library and are not counted).  No counterpart in
+ * the reference: it backs the launch count a benchmark reports. */
+DSV4_API long long dsv4_kernel_launches(void);
 DSV4_API const char* dsv4_status_string(int status);
 /* Synchronises the device, returns the first device-side error code (0 if
  * none) in *code, and clears it when clear != 0. */

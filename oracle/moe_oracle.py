@@ -368,6 +368,44 @@ def moe_forward(x_bf16: np.ndarray, mw: MoEWeights, routing=None, dense_cache=No
     return y, wts, idx, outs
 
 
+def route_plan(indices: np.ndarray, n_experts: int, block_n: int, shared_rows: int, align: int = 32):
+    """Segment layout of the routes (the dispatch of lazy_official_runtime.py:985,996-998).
+
+    Expert e's rows are the tokens ``torch.where(indices == e)`` returns, in that
+    (token) order; segments are the experts in ascending id followed by the
+    shared expert (the first ``shared_rows`` tokens), each padded to ``align``
+    rows.  Returns dict(counts [E+1], seg_start [E+2], route_slot [T*k] (-1 for
+    a skipped route), slot_token [rows] (-1 on padding), tiles [(segment,
+    row0, rows)]).  Indices of -1 are skipped routes."""
+    idx = np.asarray(indices).reshape(indices.shape[0], -1)
+    T, k = idx.shape
+    flat = idx.reshape(-1)
+    counts = np.zeros(n_experts + 1, dtype=np.int64)
+    seg_start = np.zeros(n_experts + 2, dtype=np.int64)
+    route_slot = np.full(T * k, -1, dtype=np.int64)
+    members = []
+    for e in range(n_experts):
+        rows, top = np.nonzero(idx == e)
+        members.append(rows * k + top)
+        counts[e] = rows.size
+    counts[n_experts] = shared_rows
+    run = 0
+    for s in range(n_experts + 1):
+        seg_start[s] = run
+        run += -(-int(counts[s]) // align) * align
+    seg_start[n_experts + 1] = run
+    slot_token = np.full(run, -1, dtype=np.int64)
+    for e in range(n_experts):
+        slots = seg_start[e] + np.arange(counts[e])
+        route_slot[members[e]] = slots
+        slot_token[slots] = members[e] // k
+    slot_token[seg_start[n_experts]:seg_start[n_experts] + shared_rows] = np.arange(shared_rows)
+    tiles = [(s, int(seg_start[s]) + m, min(block_n, int(counts[s]) - m))
+             for s in range(n_experts + 1) for m in range(0, int(counts[s]), block_n)]
+    return {"counts": counts, "seg_start": seg_start, "route_slot": route_slot, "slot_token": slot_token,
+            "tiles": tiles}
+
+
 def moe_forward_ep(x_bf16_per_rank: list, mw: MoEWeights, world: int, routing_per_rank=None):
     """Expert-parallel layer: every rank routes its own tokens; rank r owns
     experts [r*E/W, (r+1)*E/W) (lazy_official_runtime.py:956-965).  Each token's

@@ -340,3 +340,57 @@ def test_gate_route_tensor_core_path(cuda_device, T):
     wo, io = O.route_from_logits(lg, bias.numpy(), k, 2.5)
     assert np.array_equal(idx.cpu().numpy(), io)
     assert np.array_equal(wt.cpu().numpy().view(np.uint32), wo.view(np.uint32))
+
+
+# ---------------------------------------------------------------------------
+# routing plan: bit-exact permutation against the oracle
+# ---------------------------------------------------------------------------
+def _plan_from_ws(ws, offs, T, k, E):
+    i32 = lambda o, n: ws[o:o + 4 * n].view(torch.int32).cpu().numpy().astype(np.int64)
+    seg = i32(offs[4], E + 2)
+    rows = int(seg[E + 1])
+    n_tiles = int(i32(offs[5], 1)[0])
+    tiles = i32(offs[9], 4 * n_tiles).reshape(-1, 4)
+    return {"counts": i32(offs[3], E + 1), "seg_start": seg, "route_slot": i32(offs[6], T * k),
+            "slot_token": i32(offs[7], rows), "tiles": [tuple(int(v) for v in t[:3]) for t in tiles]}
+
+
+@pytest.mark.parametrize("name,T,pattern", [("cpu_ref", 1, "random"), ("cpu_ref", 37, "random"),
+                                            ("cpu_ref", 300, "one_hot"), ("cpu_ref", 1500, "random"),
+                                            ("decode", 64, "random"), ("decode", 1100, "skewed")])
+def test_route_plan_matches_oracle(cuda_device, name, T, pattern):
+    """counts, padded segment starts, every route's slot, every slot's token
+    (-1 on padding) and the tile list equal the oracle's stable counting sort;
+    covers one chunk, ragged chunks, both chunk sizes and a segment holding
+    every token."""
+    from spark_b200.synthetic import CONFIGS, build_moe, make_layer
+
+    cfg = CONFIGS[name].with_tokens(T)
+    layer = make_layer(cfg, seed=1, device="cpu")
+    moe = build_moe(layer, device=cuda_device)
+    E, k = cfg.n_routed, cfg.topk
+    g = torch.Generator().manual_seed(T)
+    if pattern == "one_hot":  # every token routes to experts 0..k-1
+        idx = torch.arange(k).repeat(T, 1)
+    elif pattern == "skewed":  # half of all routes land on 8 experts
+        hot = torch.randperm(E, generator=g)[:8]
+        rows = []
+        for _ in range(T):
+            a = hot[torch.randperm(8, generator=g)[:k // 2]].tolist()
+            rest = [e for e in torch.randperm(E, generator=g).tolist() if e not in a][:k - len(a)]
+            rows.append(a + rest)
+        idx = torch.tensor(rows)
+    else:
+        idx = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)])
+    w = torch.rand(T, k, generator=g)
+    x = layer["x"].to(cuda_device)
+    ws = torch.empty(moe.workspace_bytes(T), dtype=torch.uint8, device=cuda_device)
+    moe.forward_tokens(x, workspace=ws, routing=(w.to(cuda_device), idx.to(cuda_device)))
+    torch.cuda.synchronize()
+    _no_device_error()
+    offs = _layer_ws(moe, T)
+    got = _plan_from_ws(ws, offs, T, k, E)
+    ref = O.route_plan(idx.numpy(), E, int(offs[16]), T)
+    for key in ("counts", "seg_start", "route_slot", "slot_token"):
+        assert np.array_equal(got[key], ref[key]), key
+    assert got["tiles"] == ref["tiles"]

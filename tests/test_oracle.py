@@ -126,3 +126,22 @@ def test_expert_forward_linear_in_route_weight(limit):
     y1 = O.expert_forward(x, ew, np.ones(3, np.float32), limit)
     y0 = O.expert_forward(x, ew, None, limit)
     assert np.array_equal(y0, y1)
+
+
+def test_route_plan_follows_torch_where_order():
+    """Segment e lists torch.where(indices == e)'s tokens in order; padding to
+    32 rows; the shared segment is the identity; tiles cover each segment."""
+    g = torch.Generator().manual_seed(5)
+    T, k, E, bn = 77, 4, 16, 32
+    idx = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)])
+    p = O.route_plan(idx.numpy(), E, bn, T)
+    for e in range(E):
+        rows, top = torch.where(idx == e)
+        s0, c = int(p["seg_start"][e]), int(p["counts"][e])
+        assert np.array_equal(p["slot_token"][s0:s0 + c], rows.numpy())
+        assert np.array_equal(p["route_slot"][(rows * k + top).numpy()], np.arange(s0, s0 + c))
+        assert (p["slot_token"][s0 + c:int(p["seg_start"][e + 1])] == -1).all()
+        assert int(p["seg_start"][e + 1]) - s0 == -(-c // 32) * 32
+    s0 = int(p["seg_start"][E])
+    assert np.array_equal(p["slot_token"][s0:s0 + T], np.arange(T))
+    assert sum(t[2] for t in p["tiles"]) == T * k + T
