@@ -15,9 +15,11 @@ restatement of the reference's layer on the host cores instead (the
 reference's own MoE math is the absent official model; its only native code,
 the packed loader, is not on this layer's compute path).
 
-With torchrun (N > 1) every rank runs the same layer on its own tokens with
-its own copy of the experts (independent replicas, weak scaling); the time is
-the max over ranks.
+With torchrun (N > 1) the layer is expert-parallel: rank r owns experts
+[r*E/N, (r+1)*E/N), routes its own tokens (64 per GPU for decode, 4096 for
+prefill) and exchanges FP8 rows / bf16 route outputs with the owning ranks over
+NCCL (weak scaling: tokens per GPU fixed).  Each step is timed with CUDA events
+on every rank; the reported time is the max over ranks.
 """
 
 from __future__ import annotations
@@ -147,6 +149,8 @@ def _traffic_record(workload: str):
 # our arm
 # ---------------------------------------------------------------------------
 def run_ours(args, world, rank, local):
+    if world > 1:
+        return run_ours_ep(args, world, rank, local)
     import torch
     import torch.distributed as dist
 
@@ -287,7 +291,7 @@ def run_ours(args, world, rank, local):
                    "inter": cfg.inter, "routed_experts": cfg.n_routed, "topk": cfg.topk, "shared_experts": 1,
                    "routing": "uniform" if cfg.bias == "zero" else "zipf1.2",
                    "experts_touched": touched, "rows": rows, "l2": "flushed (256 MB write) between steps",
-                   "parallelism": "replicas" if world > 1 else "single",
+                   "parallelism": "single",
                    "cuda_graph": True},
         "stage_ms": dict(zip(["gate", "plan", "permute", "gemm1", "gemm2", "combine"],
                              [round(v, 5) for v in stage_ms])),
@@ -295,6 +299,146 @@ def run_ours(args, world, rank, local):
         "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 2), "unit": UNIT,
                 "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": y.numel() * 2,
                 "ms_per_step": round(e2e_ms, 5), "path": "MoE.forward_tokens -> dsv4_moe_forward (C ABI)"},
+        "clocks": clk,
+        "gpu_launches": launches_per_step * args.steps,
+    }
+    return result, cfg, layer, moe
+
+
+def run_ours_ep(args, world, rank, local):
+    """Expert-parallel layer over `world` GPUs (one process each)."""
+    import torch
+    import torch.distributed as dist
+
+    from spark_b200 import _lib
+    from spark_b200.ep import ep_moe_forward
+    from spark_b200.moe import packed_block_bytes
+    from spark_b200.synthetic import CONFIGS, build_moe, make_layer
+
+    dev = torch.device("cuda", local)
+    base = CONFIGS[args.workload]
+    if args.experts:
+        from dataclasses import replace as _replace
+
+        base = _replace(base, n_routed=args.experts)
+    T = args.tokens or (64 if args.workload == "decode" else 4096)
+    cfg = base.with_tokens(T)
+    layer = make_layer(cfg, seed=args.seed, device=dev)  # same weights on every rank
+    moe = build_moe(layer, device=dev)                   # own experts only
+    g = torch.Generator(device=dev).manual_seed(args.seed + 1000 * (rank + 1))
+    x = torch.randn(T, cfg.dim, generator=g, device=dev).to(torch.bfloat16)
+    lib = _lib.load()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    for _ in range(max(args.warmup, 3)):
+        y = ep_moe_forward(moe, x)
+    torch.cuda.synchronize()
+    _lib.raise_on_device_error()
+    n0 = lib.dsv4_kernel_launches()
+    y = ep_moe_forward(moe, x)
+    launches_per_step = lib.dsv4_kernel_launches() - n0
+    torch.cuda.synchronize()
+
+    # work this rank's experts do per step (from every rank's routing)
+    w_idx = moe.gate(x)[1].to(torch.int64).reshape(-1)
+    all_idx = torch.empty(world * w_idx.numel(), dtype=torch.int64, device=dev)
+    dist.all_gather_into_tensor(all_idx, w_idx)
+    e0_, e1_ = moe.experts_start_idx, moe.experts_end_idx
+    local_routes = int(((all_idx >= e0_) & (all_idx < e1_)).sum())
+    touched = int(torch.unique(all_idx[(all_idx >= e0_) & (all_idx < e1_)]).numel())
+    global_touched = int(torch.unique(all_idx).numel())
+
+    lib.dsv4_profile_enable(1)
+    stage = torch.zeros(6, dtype=torch.float64)
+    buf = (ctypes.c_float * 6)()
+    times = []
+    clocks = ClockSampler(local)
+    dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    for _ in range(args.steps):
+        flush.fill_(1)
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        y = ep_moe_forward(moe, x)
+        e1.record()
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+        lib.dsv4_profile_read(buf, 6)
+        stage += torch.tensor(list(buf), dtype=torch.float64)
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = clocks.stop()
+    lib.dsv4_profile_enable(0)
+    _lib.raise_on_device_error()
+    ms_local = sum(times) / len(times)
+    stage_ms = (stage / args.steps).tolist()
+    gemm_ms_local = stage_ms[3] + stage_ms[4]
+    t = torch.tensor([ms_local, gemm_ms_local], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, gemm_ms = float(t[0]), float(t[1])
+
+    # end to end: pinned host tokens in, MoE.forward over NCCL, result to the host
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty_like(x_host).pin_memory()
+    e2e = []
+    for i in range(args.warmup + args.steps):
+        flush.fill_(1)
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        xd = x_host.to(dev, non_blocking=True)
+        yd = moe(xd.view(1, T, -1)).view(T, -1)
+        y_host.copy_(yd, non_blocking=True)
+        e1.record()
+        e1.synchronize()
+        if i >= args.warmup:
+            e2e.append(e0.elapsed_time(e1))
+    t = torch.tensor([sum(e2e) / len(e2e)], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+
+    peaks, peak_src = _peaks()
+    H, I = cfg.dim, cfg.inter
+    shared_bytes = 3 * I * H + 3 * (I // 128) * (H // 128)
+    if args.workload == "decode":
+        gemm_bytes = touched * packed_block_bytes(H, I) + shared_bytes
+        achieved = gemm_bytes / (gemm_ms_local * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                "kernel": "expert_gemm_kernel (GEMM1 + GEMM2) of rank 0's owned experts, per layer",
+                "algorithmic_bytes": gemm_bytes, "kernel_ms": round(gemm_ms_local, 4), "peak_source": peak_src}
+    else:
+        flops = (local_routes + T) * 3 * 2.0 * H * I
+        fp8_peak = 2 * peaks.get("bf16_tflops", 1590.0)
+        achieved = flops / (gemm_ms_local * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": fp8_peak, "unit": "TFLOP/s",
+                "frac": round(achieved / fp8_peak, 4), "traffic": None,
+                "kernel": "expert_gemm_kernel (GEMM1 + GEMM2) of rank 0's owned experts",
+                "algorithmic_flops": flops, "kernel_ms": round(gemm_ms_local, 4),
+                "peak_source": f"{peak_src} bf16 x2 (dense FP8 rate)"}
+    rb = lib.dsv4_ep_row_bytes(H, cfg.topk)
+    result = {
+        "metric": METRIC, "value": round(world * T / (ms * 1e-3), 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "e2m1/e4m3 x e4m3 -> f32 (bf16 out)",
+        "data": "synthetic (seeded; random-init weights of the V4-Flash MoE shapes)",
+        "config": {"workload": f"{args.workload}_moe_layer", "tokens_per_gpu": T, "hidden": H, "inter": I,
+                   "routed_experts": cfg.n_routed, "topk": cfg.topk, "shared_experts": 1,
+                   "routing": "uniform" if cfg.bias == "zero" else "zipf1.2",
+                   "experts_touched": global_touched, "rank0_experts_touched": touched,
+                   "rank0_routes": local_routes, "l2": "flushed (256 MB write) between steps",
+                   "parallelism": f"ep{world}", "exchange": "NCCL all-to-all: FP8 rows "
+                   f"({rb} B per token and owning rank), bf16 route outputs ({2 * H} B per route)",
+                   "cuda_graph": False},
+        "stage_ms_rank0": dict(zip(["unpack", "plan", "scatter", "gemm1", "gemm2", "return_gather"],
+                                   [round(v, 5) for v in stage_ms])),
+        "roofline": roof,
+        "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 2), "unit": UNIT,
+                "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": y.numel() * 2,
+                "ms_per_step": round(e2e_ms, 5), "path": "MoE.forward -> spark_b200.ep (C ABI + NCCL)"},
         "clocks": clk,
         "gpu_launches": launches_per_step * args.steps,
     }

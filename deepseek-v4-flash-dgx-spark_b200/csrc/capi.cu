@@ -128,10 +128,12 @@ static int validate(const dsv4_moe_layer* L) {
   return DSV4_OK;
 }
 
-static Plan make_plan(const dsv4_moe_layer* L, int T) {
+// E_local < 0: the whole layer (E = n_routed, gate included); otherwise the
+// local experts of an expert-parallel rank (no gate).
+static Plan make_plan(const dsv4_moe_layer* L, int T, int E_local = -1) {
   Plan p{};
   p.T = T;
-  p.E = L->n_routed;
+  p.E = E_local < 0 ? L->n_routed : E_local;
   p.k = L->topk;
   p.H = L->hidden;
   p.I = L->inter;
@@ -143,7 +145,7 @@ static Plan make_plan(const dsv4_moe_layer* L, int T) {
   const long long atom_groups = p.max_rows / 32 + 4;
   const long long nchunks = T > 0 ? (T + route_chunk_tokens(T) - 1) / route_chunk_tokens(T) : 0;
   long long sz[19] = {
-      (long long)T * p.E * 4,                 // logits
+      (long long)T * (p.E > p.k ? p.E : p.k) * 4,  // logits (expert parallel: return rows)
       (long long)T * p.k * 4,                 // weights
       (long long)T * p.k * 8,                 // indices
       (long long)(p.E + 1) * 4,               // counts
@@ -158,8 +160,9 @@ static Plan make_plan(const dsv4_moe_layer* L, int T) {
       (long long)p.max_rows * p.I,            // hq
       atom_groups * (p.I / 512) * 512,        // hsf
       (long long)p.max_rows * p.H * 2,        // O
-      gate_partials_bytes(T, p.H, p.E, num_sms(),
-                          L->gate_w && !L->gate_w_fp32 && p.E == 256),  // gate partial logits
+      E_local < 0 ? gate_partials_bytes(T, p.H, p.E, num_sms(),
+                                        L->gate_w && !L->gate_w_fp32 && p.E == 256)
+                  : 0,                        // gate partial logits
       (long long)p.E * nchunks * 4,           // per-chunk expert counts
       (long long)p.E * nchunks * 4,           // per-chunk segment offsets
       16,                                     // plan control words
@@ -580,6 +583,140 @@ int dsv4_build_shared_scale_atoms(const uint8_t* w1_scale, const uint8_t* w2_sca
   if ((rc = launch_build_sf_fp8(w1_scale, inter, hidden, shared_sf, nsm, st))) return rc;
   if ((rc = launch_build_sf_fp8(w3_scale, inter, hidden, shared_sf + sc, nsm, st))) return rc;
   return launch_build_sf_fp8(w2_scale, hidden, inter, shared_sf + 2 * sc, nsm, st);
+}
+
+// ---------------------------------------------------------------------------
+// expert parallelism (ep.cu): dispatch, owning-rank forward, combine
+// ---------------------------------------------------------------------------
+static int ep_check(const dsv4_moe_layer* L, int rank, int world) {
+  int rc = validate(L);
+  if (rc) return rc;
+  if (world < 1 || world > 8 || rank < 0 || rank >= world) return DSV4_ERR_ARG;
+  if (L->n_routed % world) return DSV4_ERR_ARG;
+  return DSV4_OK;
+}
+
+long long dsv4_ep_row_bytes(int hidden, int topk) {
+  if (hidden <= 0 || hidden % 512 || topk <= 0 || topk > 8) return -1;
+  return ep_row_bytes(hidden, topk);
+}
+
+long long dsv4_ep_dispatch_workspace_bytes(int T, int world) {
+  if (T < 0 || world < 1 || world > 8) return -1;
+  return ep_dispatch_workspace(T, world);
+}
+
+int dsv4_ep_dispatch(const void* x, const int64_t* indices, const float* weights, int T,
+                     int hidden, int topk, int n_routed, int world, void* send,
+                     long long send_rows, int* send_counts, int* ret_pos, void* workspace,
+                     long long workspace_bytes, void* stream) {
+  if (T < 0 || hidden <= 0 || hidden % 512 || topk <= 0 || topk > 8 || world < 1 || world > 8 ||
+      n_routed <= 0 || n_routed > 512 || n_routed % world || topk > n_routed || !send_counts)
+    return DSV4_ERR_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  bind_device(send_counts);
+  if (T == 0) return cudaMemsetAsync(send_counts, 0, 2 * world * sizeof(int), st) == cudaSuccess
+                         ? DSV4_OK : DSV4_ERR_CUDA;
+  if (!x || !indices || !weights || !send || !ret_pos) return DSV4_ERR_ARG;
+  if (send_rows < (long long)T * (world < topk ? world : topk)) return DSV4_ERR_WORKSPACE;
+  if (!workspace || workspace_bytes < ep_dispatch_workspace(T, world)) return DSV4_ERR_WORKSPACE;
+  return launch_ep_dispatch(x, indices, weights, T, hidden, topk, n_routed, world,
+                            static_cast<uint8_t*>(send), send_counts, ret_pos,
+                            static_cast<uint8_t*>(workspace), num_sms(), st);
+}
+
+long long dsv4_ep_expert_workspace_bytes(const dsv4_moe_layer* L, int world, int T_own, int R) {
+  if (ep_check(L, 0, world) || T_own < 0 || R < 0) return -1;
+  return make_plan(L, T_own + R, L->n_routed / world).total;
+}
+
+int dsv4_ep_expert_forward(const dsv4_moe_layer* L, int rank, int world, const void* x_own,
+                           int T_own, const void* recv, int R, const int* recv_counts,
+                           void* ret_send, long long ret_rows, void* workspace,
+                           long long workspace_bytes, void* stream) {
+  int rc = ep_check(L, rank, world);
+  if (rc) return rc;
+  if (T_own < 0 || R < 0 || (T_own && !x_own) || (R && (!recv || !recv_counts || !ret_send)) ||
+      ret_rows < 0)
+    return DSV4_ERR_ARG;
+  if (!L->arena || !L->arena_sf || !L->expert_slot || L->slot_stride % 32 || L->n_slots <= 0)
+    return DSV4_ERR_ARG;
+  if (L->n_shared && (!L->shared_w1 || !L->shared_w2 || !L->shared_w3 || !L->shared_sf))
+    return DSV4_ERR_ARG;
+  const int T = T_own + R;
+  if (T == 0) return DSV4_OK;
+  const int e_count = L->n_routed / world, e_begin = rank * e_count;
+  const Plan p = make_plan(L, T, e_count);
+  if (!workspace || workspace_bytes < p.total) return DSV4_ERR_WORKSPACE;
+  bind_device(workspace);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* ret_dst = reinterpret_cast<int*>(ws + p.off[0]);
+  float* w_local = reinterpret_cast<float*>(ws + p.off[1]);
+  int64_t* idx_local = reinterpret_cast<int64_t*>(ws + p.off[2]);
+  int* counts = reinterpret_cast<int*>(ws + p.off[3]);
+  int* seg_start = reinterpret_cast<int*>(ws + p.off[4]);
+  int* n_tiles = reinterpret_cast<int*>(ws + p.off[5]);
+  int* route_slot = reinterpret_cast<int*>(ws + p.off[6]);
+  int* slot_token = reinterpret_cast<int*>(ws + p.off[7]);
+  float* slot_weight = reinterpret_cast<float*>(ws + p.off[8]);
+  int4* tiles = reinterpret_cast<int4*>(ws + p.off[9]);
+  uint8_t* xq = ws + p.off[10];
+  uint8_t* xsf = ws + p.off[11];
+  uint8_t* hq = ws + p.off[12];
+  uint8_t* hsf = ws + p.off[13];
+  __nv_bfloat16* O = reinterpret_cast<__nv_bfloat16*>(ws + p.off[14]);
+  int* chunk_cnt = reinterpret_cast<int*>(ws + p.off[16]);
+  int* chunk_base = reinterpret_cast<int*>(ws + p.off[17]);
+  int* ctrl = reinterpret_cast<int*>(ws + p.off[18]);
+  const int nsm = num_sms();
+  const int H = p.H, k = p.k;
+  const int shared_rows = p.S ? T_own : 0;
+  const uint8_t* rows_in = static_cast<const uint8_t*>(recv);
+  // profile stages here: unpack, plan, scatter, GEMM1, GEMM2, return gather
+  stage_mark(0, st);
+  if ((rc = launch_ep_unpack(rows_in, R, T_own, k, H, e_begin, e_count, recv_counts, world,
+                             idx_local, w_local, ret_dst, st)))
+    return rc;
+  stage_mark(1, st);
+  if ((rc = launch_route_plan(idx_local, T, k, e_count, 1, shared_rows, p.block_n, p.max_rows,
+                              p.max_tiles, chunk_cnt, chunk_base, ctrl, counts, seg_start, tiles,
+                              n_tiles, slot_token, slot_weight, st)))
+    return rc;
+  stage_mark(2, st);
+  if ((rc = launch_route_scatter(x_own, T_own, rows_in, ep_row_bytes(H, k), idx_local, w_local, T,
+                                 k, e_count, H, shared_rows, seg_start, chunk_base, ctrl,
+                                 route_slot, slot_token, slot_weight, xq, xsf, nsm, st)))
+    return rc;
+  stage_mark(3, st);
+  if ((rc = run_expert_gemms(L, tiles, n_tiles, slot_weight, xq, xsf, hq, hsf, O, H, p.max_rows,
+                             p.max_tiles, p.block_n, L->expert_slot + e_begin, e_count, nsm, st)))
+    return rc;
+  rc = launch_ep_return_gather(O, H, route_slot, ret_dst, T * k, ret_rows, ret_send, nsm, st);
+  stage_mark(6, st);
+  return rc;
+}
+
+int dsv4_ep_combine(const dsv4_moe_layer* L, int rank, int world, const void* ret_recv,
+                    const int* ret_pos, const int64_t* indices, int T_own, int R,
+                    const void* workspace, long long workspace_bytes, void* y, void* stream) {
+  int rc = ep_check(L, rank, world);
+  if (rc) return rc;
+  if (T_own < 0 || R < 0) return DSV4_ERR_ARG;
+  if (T_own == 0) return DSV4_OK;
+  // every token has at least one route, so with T_own > 0 rows always return
+  if (!ret_recv || !ret_pos || !indices || !y || !workspace) return DSV4_ERR_ARG;
+  const int e_count = L->n_routed / world;
+  const Plan p = make_plan(L, T_own + R, e_count);
+  if (workspace_bytes < p.total) return DSV4_ERR_WORKSPACE;
+  bind_device(y);
+  const uint8_t* ws = static_cast<const uint8_t*>(workspace);
+  const int* seg_start = reinterpret_cast<const int*>(ws + p.off[4]);
+  const void* O = ws + p.off[14];
+  // routed rows from the return buffer, the shared row from this rank's own output
+  return launch_combine(ret_recv, p.H, ret_pos, indices, T_own, p.k,
+                        p.S ? seg_start + e_count : nullptr, y, static_cast<cudaStream_t>(stream),
+                        O);
 }
 
 }  // extern "C"

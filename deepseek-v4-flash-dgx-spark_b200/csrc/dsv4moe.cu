@@ -6,5 +6,6 @@
 #include "expert_gemm.cu"
 #include "gate_gemm.cu"
 #include "materialize.cu"
+#include "ep.cu"
 #include "capi.cu"
 #include "no_alloc.cu"

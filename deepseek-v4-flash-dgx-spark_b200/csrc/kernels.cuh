@@ -56,8 +56,21 @@ int launch_single_segment_plan(int T, int seg, int block_n, int rows_pad, const 
                                int* total_rows, cudaStream_t st);
 int launch_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* s, int num_sms,
                      cudaStream_t st);
+// expert parallelism (ep.cu)
+long long ep_row_bytes(int H, int k);
+long long ep_dispatch_workspace(int T, int world);
+int launch_ep_dispatch(const void* x, const int64_t* indices, const float* weights, int T, int H,
+                       int k, int E, int world, uint8_t* send, int* send_counts, int* ret_pos,
+                       uint8_t* ws, int num_sms, cudaStream_t st);
+int launch_ep_unpack(const uint8_t* recv, int R, int T_own, int k, int H, int e_begin, int e_count,
+                     const int* recv_counts, int world, int64_t* idx_local, float* w_local,
+                     int* ret_dst, cudaStream_t st);
+int launch_ep_return_gather(const void* O, int H, const int* route_slot, const int* ret_dst,
+                            int n_routes, long long ret_rows, void* ret, int num_sms,
+                            cudaStream_t st);
 int launch_combine(const void* O, int H, const int* route_slot, const int64_t* indices, int T,
-                   int k, const int* shared_base, void* y, cudaStream_t st);
+                   int k, const int* shared_base, void* y, cudaStream_t st,
+                   const void* O_shared = nullptr);
 int launch_materialize(const uint8_t* slab, const long long* src_off, const int* dst_slot, int n,
                        long long block_bytes, uint8_t* arena, long long slot_stride, int hidden,
                        int inter, uint8_t* sf, long long sf_slot_stride, void* bf16_out,

@@ -157,6 +157,36 @@ __global__ void __launch_bounds__(kScanThreads) route_scan_kernel(
 // rows 32g .. 32g+127 for k tiles 4q .. 4q+3, row r / tile kt at byte
 // (r%32)*16 + ((r/32)-g)*4 + kt%4, so one quad of one row is 4 consecutive
 // bytes in each of the (up to) four atoms that contain the row.
+// act_quant of one quad (4 k tiles) of a row held as 16 bf16 per lane (lane l:
+// elements 16l..16l+15): codes of the lane's 16 elements and, in every lane,
+// the biased ue8m0 scale byte of its k tile (l / 8).
+__device__ __forceinline__ void quad_quant(const uint4 raw[2], int lane, uint4* code, uint32_t* sc) {
+  float v[16];
+  const __nv_bfloat16* b0 = reinterpret_cast<const __nv_bfloat16*>(&raw[0]);
+  const __nv_bfloat16* b1 = reinterpret_cast<const __nv_bfloat16*>(&raw[1]);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    v[i] = __bfloat162float(b0[i]);
+    v[8 + i] = __bfloat162float(b1[i]);
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+  for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const int e = act_scale_exp(amax);
+  const float inv = exp2i(-e);
+  uint32_t w[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    w[j] = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[j] |= static_cast<uint32_t>(f32_to_e4m3(v[4 * j + i] * inv)) << (8 * i);
+  }
+  *code = make_uint4(w[0], w[1], w[2], w[3]);
+  *sc = static_cast<uint32_t>(e + 127);
+}
+
 constexpr int kQuadsInFlight = 2;
 constexpr int kQuantGroup = 8;  // k tiles of loads in flight in quant_row; the least a scatter CTA takes
 
@@ -186,33 +216,7 @@ __device__ __forceinline__ void scatter_row(const __nv_bfloat16* __restrict__ xr
 #pragma unroll
     for (int g = 0; g < kQuadsInFlight; ++g) {
       if (qa + g >= q1) break;
-      if (xrow) {
-        float v[16];
-        const __nv_bfloat16* b0 = reinterpret_cast<const __nv_bfloat16*>(&raw[g][0]);
-        const __nv_bfloat16* b1 = reinterpret_cast<const __nv_bfloat16*>(&raw[g][1]);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          v[i] = __bfloat162float(b0[i]);
-          v[8 + i] = __bfloat162float(b1[i]);
-        }
-        float amax = 0.f;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
-#pragma unroll
-        for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        const int e = act_scale_exp(amax);
-        const float inv = exp2i(-e);
-        uint32_t w[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          w[j] = 0;
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            w[j] |= static_cast<uint32_t>(f32_to_e4m3(v[4 * j + i] * inv)) << (8 * i);
-        }
-        code[g] = make_uint4(w[0], w[1], w[2], w[3]);
-        sc[g] = static_cast<uint32_t>(e + 127);
-      }
+      if (xrow) quad_quant(raw[g], lane, &code[g], &sc[g]);
       // the quad's four scales, k tile j held by lane 8j
       const uint32_t s4 = __shfl_sync(0xffffffffu, sc[g], 0) | (__shfl_sync(0xffffffffu, sc[g], 8) << 8) |
                           (__shfl_sync(0xffffffffu, sc[g], 16) << 16) |
@@ -382,6 +386,7 @@ __global__ void __launch_bounds__(512) combine_kernel(const __nv_bfloat16* __res
                                                       const int* __restrict__ route_slot,
                                                       const int64_t* __restrict__ indices, int T,
                                                       int k, const int* __restrict__ shared_base,
+                                                      const __nv_bfloat16* __restrict__ Osh,
                                                       __nv_bfloat16* __restrict__ y) {
   const int t = blockIdx.x;
   if (t >= T) return;
@@ -423,7 +428,7 @@ __global__ void __launch_bounds__(512) combine_kernel(const __nv_bfloat16* __res
       for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], __bfloat162float(b[i]));
     }
     if (sh >= 0) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(O + (size_t)sh * H + c * 8);
+      const uint4 raw = *reinterpret_cast<const uint4*>(Osh + (size_t)sh * H + c * 8);
       const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], __bfloat162float(b[i]));
@@ -535,11 +540,13 @@ int launch_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* s, int nu
 }
 
 int launch_combine(const void* O, int H, const int* route_slot, const int64_t* indices, int T,
-                   int k, const int* shared_base, void* y, cudaStream_t st) {
+                   int k, const int* shared_base, void* y, cudaStream_t st, const void* O_shared) {
   if (T <= 0) return DSV4_OK;
+  const __nv_bfloat16* o = static_cast<const __nv_bfloat16*>(O);
+  const __nv_bfloat16* osh = O_shared ? static_cast<const __nv_bfloat16*>(O_shared) : o;
   count_launch();
-  combine_kernel<<<T, H / 8 < 512 ? H / 8 : 512, 0, st>>>(static_cast<const __nv_bfloat16*>(O), H, route_slot, indices,
-                                    T, k, shared_base, static_cast<__nv_bfloat16*>(y));
+  combine_kernel<<<T, H / 8 < 512 ? H / 8 : 512, 0, st>>>(o, H, route_slot, indices, T, k, shared_base,
+                                                          osh, static_cast<__nv_bfloat16*>(y));
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
 

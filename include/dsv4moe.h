@@ -232,6 +232,55 @@ DSV4_API int dsv4_read_into_and_copy(int fd, void* staging, long long staging_ca
                             long long* copied_bytes, double* read_seconds, double* copy_seconds,
                             int* err_no);
 
+/* ------------------------------------------------------------------------
+ * Expert parallelism over W ranks (W <= 8; rank r owns experts
+ * [r*E/W, (r+1)*E/W), spark_runtime/lazy_official_runtime.py:956-965).
+ * Replaces the reference's replicated tokens + dist.all_reduce(y) (:999-1000)
+ * with a dispatch of FP8 rows to the owning ranks and a return of every
+ * route's bf16 output row; the host moves the buffers (NCCL all-to-all):
+ *
+ *   1 dsv4_ep_dispatch       (source)  send rows + send_counts [W][2] (rows,
+ *                                      routes per destination) + ret_pos
+ *   2 exchange send_counts -> recv_counts; rows: send -> recv (row_bytes each)
+ *   3 dsv4_ep_expert_forward (owner)   recv rows + own tokens' shared expert
+ *                                      -> ret_send [sum recv routes][H] bf16
+ *   4 exchange ret_send -> ret_recv (bf16 rows, H each; split by routes)
+ *   5 dsv4_ep_combine        (source)  y [T_own][H] bf16
+ *
+ * Steps 3 and 5 share one workspace of dsv4_ep_expert_workspace_bytes(L, W,
+ * T_own, R), R = rows received.  The result is bit-identical to
+ * dsv4_moe_forward on the same tokens and routing.
+ * ---------------------------------------------------------------------- */
+/* Bytes of one send row: H e4m3 codes, H/128 ue8m0 scales, topk route
+ * entries {int32 expert (-1: another rank's), f32 weight, int32 return
+ * index}, padded to 16. */
+DSV4_API long long dsv4_ep_row_bytes(int hidden, int topk);
+DSV4_API long long dsv4_ep_dispatch_workspace_bytes(int T, int world);
+/* send: >= T*min(world, topk) rows of dsv4_ep_row_bytes; rows for rank d
+ * start at the sum of earlier ranks' row counts, tokens in order.
+ * send_counts: device int32 [world][2].  ret_pos: device int32 [T][topk],
+ * the row of the return buffer (blocks in rank order) holding each route. */
+DSV4_API int dsv4_ep_dispatch(const void* x, const int64_t* indices, const float* weights, int T,
+                              int hidden, int topk, int n_routed, int world, void* send,
+                              long long send_rows, int* send_counts, int* ret_pos,
+                              void* workspace, long long workspace_bytes, void* stream);
+DSV4_API long long dsv4_ep_expert_workspace_bytes(const dsv4_moe_layer* L, int world, int T_own,
+                                                  int R);
+/* x_own: this rank's T_own tokens (bf16, for the shared expert); recv: R
+ * received rows in source-rank order; recv_counts: device int32 [world][2]
+ * as received.  ret_send: >= ret_rows bf16 rows of H, filled for every
+ * received route (blocks by source rank). */
+DSV4_API int dsv4_ep_expert_forward(const dsv4_moe_layer* L, int rank, int world,
+                                    const void* x_own, int T_own, const void* recv, int R,
+                                    const int* recv_counts, void* ret_send, long long ret_rows,
+                                    void* workspace, long long workspace_bytes, void* stream);
+/* y[t] = bf16( sum over t's routes in ascending expert id of ret_recv[ret_pos]
+ * + t's shared row ), as the single GPU combine. */
+DSV4_API int dsv4_ep_combine(const dsv4_moe_layer* L, int rank, int world, const void* ret_recv,
+                             const int* ret_pos, const int64_t* indices, int T_own, int R,
+                             const void* workspace, long long workspace_bytes, void* y,
+                             void* stream);
+
 #ifdef __cplusplus
 }
 #endif

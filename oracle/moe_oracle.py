@@ -288,8 +288,13 @@ def quantized_linear(x_bf16: np.ndarray, w_dense: np.ndarray) -> np.ndarray:
     product is accumulated in float64 and rounded once (device: fp32 tensor-core
     accumulation), then the result is rounded to bf16."""
     q, s = act_quant(x_bf16)
-    a = act_dequant(q, s).astype(np.float64)
-    return round_bf16((a @ w_dense.astype(np.float64).T).astype(np.float32))
+    return dequant_linear(act_dequant(q, s), w_dense)
+
+
+def dequant_linear(a: np.ndarray, w_dense: np.ndarray) -> np.ndarray:
+    """The GEMM of ``quantized_linear`` on already quantized-and-dequantized
+    activations ``a``."""
+    return round_bf16((a.astype(np.float64) @ w_dense.astype(np.float64).T).astype(np.float32))
 
 
 def silu(x: np.ndarray) -> np.ndarray:
@@ -303,9 +308,17 @@ def expert_forward(x_bf16: np.ndarray, ew: ExpertWeights, route_w: np.ndarray | 
     u = clamp(u, -limit, limit), g = min(g, limit); h = silu(g) * u, times the
     routing weight when given (applied before w2, in fp32); h is cast to bf16
     and fed through w2.  Returns bf16 values as fp32 [n, H]."""
+    q, s = act_quant(x_bf16)
+    return expert_forward_dequant(act_dequant(q, s), ew, route_w, swiglu_limit, dense)
+
+
+def expert_forward_dequant(a: np.ndarray, ew: ExpertWeights, route_w: np.ndarray | None,
+                           swiglu_limit: float, dense=None) -> np.ndarray:
+    """``expert_forward`` from the dequantized act_quant of its input (the form
+    in which an expert-parallel rank receives the rows)."""
     w1, w2, w3 = dense if dense is not None else ew.dense()
-    g = quantized_linear(x_bf16, w1)
-    u = quantized_linear(x_bf16, w3)
+    g = dequant_linear(a, w1)
+    u = dequant_linear(a, w3)
     if swiglu_limit and swiglu_limit > 0:
         lim = np.float32(swiglu_limit)
         u = np.clip(u, -lim, lim)
@@ -416,6 +429,98 @@ def moe_forward_ep(x_bf16_per_rank: list, mw: MoEWeights, world: int, routing_pe
         routing = None if routing_per_rank is None else routing_per_rank[r]
         res.append(moe_forward(x, mw, routing)[0])
     return res
+
+
+# ---------------------------------------------------------------------------
+# Expert parallelism: dispatch / owning-rank forward / combine.  Rank r owns
+# experts [r*E/W, (r+1)*E/W) (lazy_official_runtime.py:956-965); instead of
+# replicating tokens and all-reducing y (:999-1000), each token's act_quant
+# row travels once to every rank owning one of its experts and every route's
+# bf16 output row travels back.  Row format (one send row):
+#   [0,H) e4m3 codes | [H,H+H/128) ue8m0 scale bytes |
+#   k x {int32 expert (-1 = another rank's), f32 weight, int32 return index}
+#   | zero padding to a multiple of 16 bytes.
+# ---------------------------------------------------------------------------
+EP_META = np.dtype([("e", "<i4"), ("w", "<f4"), ("r", "<i4")])
+
+
+def ep_row_bytes(hidden: int, topk: int) -> int:
+    return -(-(hidden + hidden // 128 + EP_META.itemsize * topk) // 16) * 16
+
+
+def ep_dispatch(x_bf16: np.ndarray, weights: np.ndarray, indices: np.ndarray, n_experts: int, world: int):
+    """-> (send [rows, row_bytes] u8, send_counts [world, 2] (rows, routes), ret_pos [T, k]).
+
+    Rows for rank d follow those for ranks < d; inside, tokens in order.  A
+    route's return index counts the routes to rank d in token order, then k
+    order; ret_pos adds the routes to earlier ranks."""
+    x = np.asarray(x_bf16, np.float32)
+    T, H = x.shape
+    k = indices.shape[1]
+    per = n_experts // world
+    dst = np.asarray(indices) // per
+    q, s = act_quant(x) if T else (np.zeros((0, H), np.uint8), np.zeros((0, H // 128), np.uint8))
+    rows = [(d, t, [j for j in range(k) if dst[t, j] == d]) for d in range(world) for t in range(T)]
+    rows = [r for r in rows if r[2]]
+    counts = np.zeros((world, 2), np.int32)
+    for d, _, js in rows:
+        counts[d, 0] += 1
+        counts[d, 1] += len(js)
+    route_base = np.concatenate([[0], np.cumsum(counts[:, 1])[:-1]]).astype(np.int64)
+    rb = ep_row_bytes(H, k)
+    send = np.zeros((len(rows), rb), np.uint8)
+    ret_pos = np.full((T, k), -1, np.int32)
+    nxt = np.zeros(world, np.int64)
+    for n, (d, t, js) in enumerate(rows):
+        send[n, :H] = q[t]
+        send[n, H:H + H // 128] = s[t]
+        meta = np.zeros(k, EP_META)
+        meta["e"], meta["r"] = -1, -1
+        for j in js:
+            meta[j] = (indices[t, j], weights[t, j], nxt[d])
+            ret_pos[t, j] = route_base[d] + nxt[d]
+            nxt[d] += 1
+        send[n, H + H // 128:H + H // 128 + EP_META.itemsize * k] = meta.view(np.uint8)
+    return send, counts, ret_pos
+
+
+def ep_expert_forward(mw: MoEWeights, n_experts: int, rank: int, world: int, x_own: np.ndarray,
+                      recv: np.ndarray, recv_counts: np.ndarray, dense_cache=None):
+    """Owning rank: every received route's output row, placed in the return
+    buffer (blocks by source rank, return index inside), and the shared
+    expert over this rank's own tokens.  -> (ret_send [routes, H], shared [T_own, H])."""
+    H = np.asarray(x_own).shape[1]
+    k = mw.topk
+    per = n_experts // world
+    n_routes = int(np.sum(recv_counts[:, 1]))
+    ret = np.zeros((n_routes, H), np.float32)
+    src_of_row = np.repeat(np.arange(world), recv_counts[:, 0])
+    route_base = np.concatenate([[0], np.cumsum(recv_counts[:, 1])[:-1]]).astype(np.int64)
+    R = recv.shape[0]
+    if R:
+        meta = np.ascontiguousarray(recv[:, H + H // 128:H + H // 128 + EP_META.itemsize * k]).view(EP_META)
+        a = act_dequant(recv[:, :H], recv[:, H:H + H // 128])
+        for e in sorted(set(int(v) for v in meta["e"].reshape(-1) if v >= 0)):
+            assert rank * per <= e < (rank + 1) * per, "route sent to the wrong rank"
+            rows, top = np.nonzero(meta["e"] == e)
+            dense = dense_cache(e) if dense_cache is not None else None
+            out = expert_forward_dequant(a[rows], mw.experts[e], meta["w"][rows, top], mw.swiglu_limit, dense)
+            ret[route_base[src_of_row[rows]] + meta["r"][rows, top]] = out
+    shared_dense = dense_cache("shared") if dense_cache is not None else None
+    x_own = np.asarray(x_own, np.float32)
+    shared = (expert_forward(x_own, mw.shared, None, mw.swiglu_limit, shared_dense) if x_own.shape[0]
+              else np.zeros((0, H), np.float32))
+    return ret, shared
+
+
+def ep_combine(ret_recv: np.ndarray, ret_pos: np.ndarray, indices: np.ndarray, shared: np.ndarray) -> np.ndarray:
+    """y[t] = bf16( sum over t's routes in ascending expert id of ret_recv[ret_pos] + shared[t] )."""
+    T, k = indices.shape
+    y = np.zeros((T, shared.shape[1]), np.float32)
+    for t in range(T):
+        for j in np.argsort(indices[t], kind="stable"):
+            y[t] = (y[t] + ret_recv[ret_pos[t, j]]).astype(np.float32)
+    return round_bf16((y + shared).astype(np.float32))
 
 
 # ---------------------------------------------------------------------------

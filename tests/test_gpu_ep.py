@@ -1,0 +1,150 @@
+"""Expert parallelism through the C ABI on one GPU: W ranks are emulated in one
+process (every rank's arena view is the same fully materialized arena, the
+all-to-all exchanges are slices and concatenations), so the device dispatch,
+owning-rank forward and combine are checked without a second GPU:
+
+* send rows (codes, scales, route entries), counts and ret_pos equal the
+  oracle's ``ep_dispatch`` byte for byte;
+* the expert-parallel output equals ``dsv4_moe_forward`` on the same tokens
+  bit for bit.
+
+The real multi-process run over NCCL is ``test_ep_nccl_two_gpus`` (needs 2 GPUs)."""
+
+import ctypes
+import os
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as O
+
+pytestmark = pytest.mark.gpu
+REPO = Path(__file__).resolve().parent.parent
+
+
+def _lib():
+    from spark_b200 import _lib as L
+
+    return L
+
+
+def _dispatch(lib, x, w, idx, E, W):
+    L = _lib()
+    T, H = x.shape
+    k = idx.shape[1]
+    rb = lib.dsv4_ep_row_bytes(H, k)
+    send = torch.zeros((max(T * min(W, k), 1), rb), dtype=torch.uint8, device=x.device)
+    counts = torch.empty((W, 2), dtype=torch.int32, device=x.device)
+    ret_pos = torch.empty((max(T, 1), k), dtype=torch.int32, device=x.device)
+    ws = torch.empty(max(lib.dsv4_ep_dispatch_workspace_bytes(T, W), 1), dtype=torch.uint8, device=x.device)
+    L.check(lib.dsv4_ep_dispatch(L.ptr(x), L.ptr(idx), L.ptr(w), T, H, k, E, W, L.ptr(send), send.shape[0],
+                                 L.ptr(counts), L.ptr(ret_pos), L.ptr(ws), ws.numel(), L.stream_ptr()),
+            "dsv4_ep_dispatch")
+    return send, counts, ret_pos
+
+
+def _emulated_ep(moe, xs, routings, W):
+    """Run the five expert-parallel steps for W emulated ranks; returns each
+    rank's y and its dispatch outputs."""
+    L = _lib()
+    lib = L.load()
+    E, H = moe.n_routed_experts, moe.dim
+    d = moe.layer_desc()
+    disp = [_dispatch(lib, x, r[0], r[1], E, W) for x, r in zip(xs, routings)]
+    counts = [c.cpu() for _, c, _ in disp]
+    # rows: block for rank d inside source s's send buffer
+    row_off = [np.concatenate([[0], np.cumsum(c[:, 0].numpy())]) for c in counts]
+    route_off = [np.concatenate([[0], np.cumsum(c[:, 1].numpy())]) for c in counts]
+    rets, states = [], []
+    for dst in range(W):
+        recv = torch.cat([disp[s][0][row_off[s][dst]:row_off[s][dst + 1]] for s in range(W)])
+        recv_counts = torch.stack([counts[s][dst] for s in range(W)]).to(torch.int32).cuda()
+        R = recv.shape[0]
+        n_ret = int(sum(int(counts[s][dst, 1]) for s in range(W)))
+        T = xs[dst].shape[0]
+        ws = torch.empty(max(lib.dsv4_ep_expert_workspace_bytes(ctypes.byref(d), W, T, R), 1), dtype=torch.uint8,
+                         device="cuda")
+        ret_send = torch.empty((max(n_ret, 1), H), dtype=torch.bfloat16, device="cuda")
+        L.check(lib.dsv4_ep_expert_forward(ctypes.byref(d), dst, W, L.ptr(xs[dst]), T, L.ptr(recv.contiguous()), R,
+                                           L.ptr(recv_counts), L.ptr(ret_send), n_ret, L.ptr(ws), ws.numel(),
+                                           L.stream_ptr()), "dsv4_ep_expert_forward")
+        rets.append((ret_send, recv_counts.cpu()))
+        states.append((ws, R))
+    ys = []
+    for s in range(W):
+        # return block of rank d for source s: after the routes d received from sources < s
+        parts = []
+        for dst in range(W):
+            rc = rets[dst][1]
+            base = int(rc[:s, 1].sum())
+            parts.append(rets[dst][0][base:base + int(rc[s, 1])])
+        ret_recv = torch.cat(parts).contiguous()
+        y = torch.empty_like(xs[s])
+        ws, R = states[s]
+        L.check(lib.dsv4_ep_combine(ctypes.byref(d), s, W, L.ptr(ret_recv), L.ptr(disp[s][2]),
+                                    L.ptr(routings[s][1]), xs[s].shape[0], R, L.ptr(ws), ws.numel(), L.ptr(y),
+                                    L.stream_ptr()), "dsv4_ep_combine")
+        ys.append(y)
+    torch.cuda.synchronize()
+    return ys, disp
+
+
+@pytest.mark.parametrize("name,W,tokens", [("cpu_ref", 2, (9, 4)), ("cpu_ref", 4, (1, 0, 40, 300)),
+                                           ("decode", 8, (64, 64, 64, 64, 64, 64, 64, 64)),
+                                           ("decode", 2, (1100, 7))])
+def test_emulated_ep_is_bit_identical_to_single_gpu(cuda_device, name, W, tokens):
+    from spark_b200.synthetic import CONFIGS, build_moe, make_layer
+
+    L = _lib()
+    cfg = CONFIGS[name].with_tokens(max(tokens))
+    layer = make_layer(cfg, seed=2, device="cpu")
+    moe = build_moe(layer, device=cuda_device)
+    E, k, H = cfg.n_routed, cfg.topk, cfg.dim
+    xs, routings = [], []
+    for r, n in enumerate(tokens):
+        g = torch.Generator().manual_seed(50 + r)
+        x = torch.randn(n, H, generator=g).to(torch.bfloat16).to(cuda_device)
+        w, idx = moe.gate(x) if n else (torch.empty(0, k, device=cuda_device),
+                                        torch.empty(0, k, dtype=torch.int64, device=cuda_device))
+        xs.append(x.contiguous())
+        routings.append((w.float().contiguous(), idx.to(torch.int64).contiguous()))
+    ys, disp = _emulated_ep(moe, xs, routings, W)
+    L.raise_on_device_error()
+    for r, (x, (w, idx)) in enumerate(zip(xs, routings)):
+        if x.shape[0] == 0:
+            continue
+        y_ref = moe.forward_tokens(x, routing=(w, idx))
+        torch.cuda.synchronize()
+        assert torch.equal(ys[r].view(torch.int16), y_ref.view(torch.int16)), r
+        # dispatch bytes against the oracle (the defined part of each row)
+        send, counts, ret_pos = disp[r]
+        o_send, o_counts, o_ret = O.ep_dispatch(x.float().cpu().numpy(), w.cpu().numpy(), idx.cpu().numpy(), E, W)
+        assert np.array_equal(counts.cpu().numpy(), o_counts)
+        assert np.array_equal(ret_pos[:x.shape[0]].cpu().numpy(), o_ret)
+        used = H + H // 128 + 12 * k
+        assert np.array_equal(send[:o_send.shape[0], :used].cpu().numpy(), o_send[:, :used])
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_ep_nccl_two_gpus():
+    """Two processes, one GPU each, NCCL all-to-all: every rank's MoE.forward
+    equals the single-GPU layer on its tokens bit for bit."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=f"{REPO}:{REPO / 'deepseek-v4-flash-dgx-spark_b200'}")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
+           str(REPO / "tests" / "ep_nccl_worker.py")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=400)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert r.stdout.count("EP_OK") == 2, r.stdout[-3000:]
