@@ -278,6 +278,16 @@ __device__ __forceinline__ uint8_t f32_to_e4m3(float x) {
   return static_cast<uint8_t>(__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3));
 }
 
+// Four fp32 -> e4m3fn codes (RNE, saturating), a in the low byte.  One
+// cvt.rn.satfinite.e4m3x2.f32 converts a pair: its first source goes to the
+// upper byte.
+__device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d) {
+  uint16_t lo, hi;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(b), "f"(a));
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(d), "f"(c));
+  return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+}
+
 // ceil(log2(v)) for a positive normal fp32 v, exact (from the bit pattern).
 __device__ __forceinline__ int ceil_log2_exact(float v) {
   const uint32_t u = __float_as_uint(v);

@@ -44,20 +44,23 @@ struct GemmCfg {
   static constexpr int TILE_BYTES = A_BYTES + B_BYTES;
   static constexpr int SF_STAGE = 1536;          // [act scales 512][weight scales 2 x 512]
   static constexpr int STAGE_BYTES = TILE_BYTES + SF_STAGE;
-  static constexpr int SMEM_BUDGET = 200 * 1024;
-  static constexpr int STAGES0 = SMEM_BUDGET / STAGE_BYTES;
+  static constexpr int CTRL_BYTES = 256;
+  // the whole 227 KB a CTA may hold: decode is bound by the weight bytes in
+  // flight per SM, and an e2m1 box takes twice its global bytes in smem
+  static constexpr int SMEM_MAX = 232448;
+  static constexpr int STAGES0 = (SMEM_MAX - 1024 - CTRL_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES0 > 8 ? 8 : STAGES0;
   static constexpr int ACC_COLS = 256;
   static constexpr int SFA_COL = 256;            // activation scales: 4 columns
   static constexpr int SFB_COL = 260;            // weight scales: 8 columns (256 rows)
   static constexpr int TMEM_COLS = 512;
-  static constexpr int CTRL_BYTES = 256;
   static constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + CTRL_BYTES;
   static_assert(A_BYTES % 1024 == 0, "tiles must keep 1024-byte alignment");
   // the M = 128 MMA reads 128 rows (16 KB) from the A base; they must stay in the stage
   static_assert(128 * 128 <= TILE_BYTES, "A window leaves the stage");
   static_assert(BM == 32 || BM == 64 || BM == 128, "activation rows per tile");
   static_assert(STAGES >= 2, "need at least two stages");
+  static_assert(SMEM_BYTES <= SMEM_MAX, "over the per-CTA shared memory limit");
 };
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
@@ -345,7 +348,9 @@ __global__ void __launch_bounds__(192, 1)
               ub = fminf(fmaxf(ub, -lim), lim);
               gb = fminf(gb, lim);
             }
-            const float s = gb / (1.0f + expf(-gb));
+            // silu with the hardware exp2 and reciprocal: a few ulp of fp32, far
+            // below the bf16 rounding of h that follows
+            const float s = __fdividef(gb, 1.0f + __expf(-gb));
             const float hv = bf16_round((s * ub) * wr);
             amax = fmaxf(amax, fabsf(hv));
             pk[j] = __float_as_uint(hv);
@@ -358,13 +363,8 @@ __global__ void __launch_bounds__(192, 1)
             uint32_t wds[4];
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
-              uint32_t word = 0;
-#pragma unroll
-              for (int b = 0; b < 4; ++b)
-                word |= static_cast<uint32_t>(
-                            f32_to_e4m3(__uint_as_float(pk[16 * v + 4 * t + b]) * inv))
-                        << (8 * b);
-              wds[t] = word;
+              const float* f = reinterpret_cast<const float*>(&pk[16 * v + 4 * t]);
+              wds[t] = e4m3x4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv);
             }
             *reinterpret_cast<uint4*>(dst + 16 * v) = make_uint4(wds[0], wds[1], wds[2], wds[3]);
           }

@@ -178,11 +178,8 @@ __device__ __forceinline__ void quad_quant(const uint4 raw[2], int lane, uint4* 
   const float inv = exp2i(-e);
   uint32_t w[4];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    w[j] = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) w[j] |= static_cast<uint32_t>(f32_to_e4m3(v[4 * j + i] * inv)) << (8 * i);
-  }
+  for (int j = 0; j < 4; ++j)
+    w[j] = e4m3x4(v[4 * j] * inv, v[4 * j + 1] * inv, v[4 * j + 2] * inv, v[4 * j + 3] * inv);
   *code = make_uint4(w[0], w[1], w[2], w[3]);
   *sc = static_cast<uint32_t>(e + 127);
 }
