@@ -177,24 +177,31 @@ def run_ours(args, world, rank, local):
     def step():
         moe.forward_tokens(x, workspace=ws, out=y)
 
-    # warm-up, then capture the layer in a CUDA graph (launch-bound at decode sizes)
+    # warm-up, then capture the layer in CUDA graphs (launch-bound at decode sizes):
+    # `graph` is the timed layer; `graph_prof` adds the library's stage events
+    # and is replayed separately for the per-stage times
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
     _lib.raise_on_device_error()
-    lib.dsv4_profile_enable(1)
-    graph = torch.cuda.CUDAGraph()
     s = torch.cuda.Stream(device=dev)
     s.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(s):
-        step()  # profiling events exist before capture
-    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
     n_launch0 = lib.dsv4_kernel_launches()
     with torch.cuda.graph(graph, stream=s):
         step()
     launches_per_step = lib.dsv4_kernel_launches() - n_launch0  # kernels in the captured layer
+    lib.dsv4_profile_enable(1)
+    with torch.cuda.stream(s):
+        step()  # profiling events exist before capture
+    torch.cuda.current_stream().wait_stream(s)
+    graph_prof = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph_prof, stream=s):
+        step()
     graph.replay()
+    graph_prof.replay()
     torch.cuda.synchronize()
+    lib.dsv4_profile_enable(0)
 
     # touched experts of this batch (for the algorithmic-bytes count)
     offs = (ctypes.c_longlong * 17)()
@@ -205,8 +212,6 @@ def run_ours(args, world, rank, local):
     rows = int(counts.sum()) + T
 
     # timed region
-    stage = torch.zeros(6, dtype=torch.float64)
-    buf = (ctypes.c_float * 6)()
     times = []
     clocks = ClockSampler(local)
     if world > 1:
@@ -222,19 +227,28 @@ def run_ours(args, world, rank, local):
         e1.record()
         e1.synchronize()
         times.append(e0.elapsed_time(e1))
-        lib.dsv4_profile_read(buf, 6)
-        stage += torch.tensor(list(buf), dtype=torch.float64)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
-    lib.dsv4_profile_enable(0)
     _lib.raise_on_device_error()
     ms = sum(times) / len(times)
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+
+    # per-stage times (library events on the launching stream), outside the timed region
+    lib.dsv4_profile_enable(1)
+    stage = torch.zeros(6, dtype=torch.float64)
+    buf = (ctypes.c_float * 6)()
+    for _ in range(args.steps):
+        flush.fill_(1)
+        graph_prof.replay()
+        torch.cuda.synchronize()
+        lib.dsv4_profile_read(buf, 6)
+        stage += torch.tensor(list(buf), dtype=torch.float64)
+    lib.dsv4_profile_enable(0)
     stage_ms = (stage / args.steps).tolist()
 
     # end to end through the C ABI with host buffers (pinned), copies inside the timed region
@@ -478,6 +492,58 @@ def _sweep(args, local):
         out[f"{wl}_T{T}"] = {"ms": round(ms, 4), "tokens_per_s": round(T / (ms * 1e-3), 1)}
         del moe, layer, ws, y
         torch.cuda.empty_cache()
+    out.update(_materializer(args, dev, flush))
+    return out
+
+
+def _materializer(args, dev, flush):
+    """The packed-slab materializer on one layer: 256 packed expert blocks (a
+    slab already in HBM) -> a 256-slot FP4 arena plus scale atoms, and the same
+    with the exact bf16 decode of every weight.  HBM roofline: the block is
+    read once, the slot, atoms (and bf16 weights) written once."""
+    import torch
+
+    from spark_b200 import _lib
+    from spark_b200.moe import ExpertArena, packed_block_bytes
+    from spark_b200.synthetic import routed_blocks
+
+    lib = _lib.load()
+    H, I, n = 4096, 2048, 256
+    nb = packed_block_bytes(H, I)
+    slab = routed_blocks(n, H, I, args.seed + 9, dev).reshape(-1)
+    arena = ExpertArena(n, H, I, device=dev)
+    off = torch.arange(n, dtype=torch.int64, device=dev) * nb
+    slots = torch.arange(n, dtype=torch.int32, device=dev)
+    bf16_stride = 3 * I * H
+    bf16 = torch.empty(n * bf16_stride, dtype=torch.bfloat16, device=dev)
+    peak = _peaks()[0]["hbm_gbs"]
+    out = {}
+    for name, dst in (("materialize_fp4_arena_256", None), ("materialize_fp4_and_bf16_256", bf16)):
+        def run():
+            _lib.check(lib.dsv4_materialize(_lib.ptr(slab), _lib.ptr(off), _lib.ptr(slots), n, H, I,
+                                            _lib.ptr(arena.buffer), arena.slot_stride, _lib.ptr(arena.sf),
+                                            arena.sf_stride, _lib.ptr(dst), bf16_stride if dst is not None else 0,
+                                            _lib.stream_ptr()), "dsv4_materialize")
+        for _ in range(2):
+            run()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(5):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            run()
+            e1.record()
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        ms = statistics.median(ts)
+        nbytes = n * (2 * nb + arena.sf_stride) + (n * bf16_stride * 2 if dst is not None else 0)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"ms": round(ms, 4), "bytes": nbytes, "GB_per_s": round(gbs, 1),
+                     "frac_of_measured_hbm": round(gbs / peak, 4)}
+    _lib.raise_on_device_error()
+    del slab, arena, bf16
+    torch.cuda.empty_cache()
     return out
 
 
@@ -562,7 +628,7 @@ def main():
             except Exception as exc:  # keep the headline line even if a sweep case fails
                 res["sweep"] = {"error": repr(exc)}
         if not args.no_cpu_baseline:
-            n = 4 if args.workload == "decode" else 8
+            n = 12  # about 10-15 s of host work
             rate, dt = cpu_layer_rate(args.workload, n, args.seed, os.cpu_count())
             res["cpu_baseline"] = {"value": round(rate, 3), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
                                    "sample": f"{n} tokens of the {args.workload} layer, {dt:.1f} s "

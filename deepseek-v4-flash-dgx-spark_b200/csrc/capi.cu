@@ -68,31 +68,39 @@ static bool tc_gate_ok(const void* x, const void* w, int w_fp32, int H, int E) {
          (reinterpret_cast<uintptr_t>(w) & 15) == 0;
 }
 
-static long long gate_partials_bytes(int T, int H, int E, int nsm, bool tc) {
-  if (!tc || T >= kFusedGateTokens || T <= 0) return 0;
+static long long gate_partials_bytes(int T, int H, int E, int nsm, bool tc, bool allow_fused = true) {
+  if (!tc || T <= 0 || (allow_fused && T >= kFusedGateTokens)) return 0;
   int bm, ks;
   gate_gemm_split_shape(T, H, E, nsm, &bm, &ks);
   return (long long)ks * T * E * 4;
 }
 
+// Hash-routed layers (hash_table != nullptr) never take the fused path: the
+// experts come from the table, so the logits go through partials (or the SIMT
+// kernel) and the table lookup happens in the top-k kernel.
 static int gate_route(const void* x, const void* w, int w_fp32, const float* bias, int T, int H,
                       int E, int k, float route_scale, float* logits, float* weights,
                       int64_t* indices, float* partials, long long partials_bytes, int nsm,
-                      cudaStream_t st) {
+                      cudaStream_t st, const int64_t* hash_table = nullptr,
+                      const int64_t* input_ids = nullptr, long long vocab = 0) {
+  const bool hashed = hash_table != nullptr;
   if (tc_gate_ok(x, w, w_fp32, H, E)) {
-    const long long need = gate_partials_bytes(T, H, E, nsm, true);
+    const long long need = gate_partials_bytes(T, H, E, nsm, true, !hashed);
     if (need > 0 && partials && partials_bytes >= need) {
       int bm, ks;
       gate_gemm_split_shape(T, H, E, nsm, &bm, &ks);
       int rc = launch_gate_gemm_partials(x, w, T, H, E, partials, nsm, st);
       if (rc) return rc;
-      return launch_gate_topk(partials, bias, T, E, k, route_scale, weights, indices, st, ks, logits);
+      return launch_gate_topk(partials, bias, T, E, k, route_scale, weights, indices, st, ks, logits,
+                              hash_table, input_ids, vocab);
     }
-    return launch_gate_gemm_topk(x, w, T, H, bias, k, route_scale, logits, weights, indices, nsm, st);
+    if (!hashed)
+      return launch_gate_gemm_topk(x, w, T, H, bias, k, route_scale, logits, weights, indices, nsm, st);
   }
   int rc = launch_gate_logits(x, w, w_fp32, T, H, E, logits, st);
   if (rc) return rc;
-  return launch_gate_topk(logits, bias, T, E, k, route_scale, weights, indices, st);
+  return launch_gate_topk(logits, bias, T, E, k, route_scale, weights, indices, st, 1, nullptr,
+                          hash_table, input_ids, vocab);
 }
 
 // ---------------------------------------------------------------------------
@@ -340,14 +348,17 @@ int dsv4_device_error(int clear, int* code) {
 }
 
 int dsv4_profile_enable(int enable) {
-  if (enable && !g_profile) {
+  // The events are created once and never destroyed: a CUDA graph captured
+  // with profiling on keeps recording them whenever it is replayed, so they
+  // must outlive every such graph (disabling only stops new captures and
+  // launches from marking stages).
+  static bool created = false;
+  if (enable && !created) {
     for (int i = 0; i < kStageEvents; ++i)
       if (cudaEventCreate(&g_stage_ev[i]) != cudaSuccess) return DSV4_ERR_CUDA;
-    g_profile = true;
-  } else if (!enable && g_profile) {
-    for (int i = 0; i < kStageEvents; ++i) cudaEventDestroy(g_stage_ev[i]);
-    g_profile = false;
+    created = true;
   }
+  g_profile = enable != 0;
   return DSV4_OK;
 }
 
@@ -416,6 +427,26 @@ int dsv4_gate_route(const void* x, const void* w, int w_is_fp32, const float* bi
                     static_cast<cudaStream_t>(stream));
 }
 
+long long dsv4_gate_hash_workspace_bytes(const void* w, int w_is_fp32, int T, int H, int E) {
+  if (T < 0 || H <= 0 || E <= 0) return -1;
+  return gate_partials_bytes(T, H, E, num_sms(), !w_is_fp32 && E == 256 && H % 64 == 0 && w, false);
+}
+
+int dsv4_gate_route_hash(const void* x, const void* w, int w_is_fp32, const int64_t* tid2eid,
+                         long long vocab, const int64_t* input_ids, int T, int H, int E, int topk,
+                         float route_scale, float* logits, float* weights, int64_t* indices,
+                         void* workspace, long long workspace_bytes, void* stream) {
+  if (!x || !w || !tid2eid || !input_ids || !logits || !weights || !indices || T < 0 || H <= 0 ||
+      H % 8 || E <= 0 || topk <= 0 || vocab <= 0)
+    return DSV4_ERR_ARG;
+  if (E > 512 || topk > 8 || topk > E || H > 8192) return DSV4_ERR_UNSUPPORTED;
+  if (T == 0) return DSV4_OK;
+  bind_device(logits);
+  return gate_route(x, w, w_is_fp32, nullptr, T, H, E, topk, route_scale, logits, weights, indices,
+                    static_cast<float*>(workspace), workspace ? workspace_bytes : 0, num_sms(),
+                    static_cast<cudaStream_t>(stream), tid2eid, input_ids, vocab);
+}
+
 int dsv4_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* scale, void* stream) {
   if (!x || !q || !scale || M < 0 || K <= 0 || K % 128) return DSV4_ERR_ARG;
   bind_device(q);
@@ -455,7 +486,7 @@ int dsv4_moe_forward(const dsv4_moe_layer* L, const void* x, int T, void* y,
   uint8_t* hsf = ws + p.off[13];
   __nv_bfloat16* O = reinterpret_cast<__nv_bfloat16*>(ws + p.off[14]);
   const int nsm = num_sms();
-  const int H = p.H, I = p.I, E = p.E, k = p.k;
+  const int H = p.H, E = p.E, k = p.k;
 
   const float* rw = routing_weights;
   const int64_t* ri = routing_indices;

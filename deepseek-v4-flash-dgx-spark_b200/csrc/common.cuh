@@ -13,6 +13,7 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <utility>
 
 #include "dsv4moe.h"
 
@@ -29,6 +30,15 @@ constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s
 // its kernels once), read by dsv4_kernel_launches().
 inline std::atomic<long long> g_kernel_launches{0};
 inline void count_launch() { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
+
+// The one launch point of the library's kernels (counted for
+// dsv4_kernel_launches()).
+template <typename... KArgs, typename... Args>
+inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                     Args&&... args) {
+  count_launch();
+  kernel<<<grid, block, smem, st>>>(std::forward<Args>(args)...);
+}
 
 __device__ __forceinline__ void record_error(int code) {
   atomicCAS(&g_dsv4_device_error, 0, code);

@@ -348,18 +348,18 @@ int launch_ep_dispatch(const void* x, const int64_t* indices, const float* weigh
   int* row_pos = reinterpret_cast<int*>(ws + 256 + 2 * series + 256);
   const long long rb = ep_row_bytes(H, k);
   if (cudaMemsetAsync(ctrl, 0, 16, st) != cudaSuccess) return DSV4_ERR_CUDA;
-  count_launch();
-  ep_count_kernel<<<nchunks, kEpChunk, 0, st>>>(indices, T, k, E, world, nchunks, cc, cb,
+  launch_k(ep_count_kernel, nchunks, kEpChunk, 0, st,
+           indices, T, k, E, world, nchunks, cc, cb,
                                                send_counts, dst_base, ctrl);
-  count_launch();
-  ep_plan_kernel<<<nchunks, kEpChunk, 0, st>>>(indices, weights, T, k, E, world, H, rb, nchunks,
+  launch_k(ep_plan_kernel, nchunks, kEpChunk, 0, st,
+           indices, weights, T, k, E, world, H, rb, nchunks,
                                               cb, dst_base, row_pos, send, ret_pos, ctrl);
   const int KQ = H / 512;
   int qsplit = (int)((8LL * num_sms * 8 + T - 1) / T);  // about 8 warps per SM slot
   qsplit = qsplit < 1 ? 1 : (qsplit > KQ ? KQ : qsplit);
   const long long warps = (long long)T * qsplit;
-  count_launch();
-  ep_pack_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
+  launch_k(ep_pack_kernel, (unsigned)((warps + 7) / 8), 256, 0, st,
+           static_cast<const __nv_bfloat16*>(x),
                                                               T, H, world, rb, row_pos, qsplit,
                                                               send);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
@@ -370,8 +370,8 @@ int launch_ep_unpack(const uint8_t* recv, int R, int T_own, int k, int H, int e_
                      int* ret_dst, cudaStream_t st) {
   const int n = T_own + R;
   if (n <= 0) return DSV4_OK;
-  count_launch();
-  ep_unpack_kernel<<<(n + 255) / 256, 256, 0, st>>>(recv, R, T_own, k, H, ep_row_bytes(H, k), e_begin,
+  launch_k(ep_unpack_kernel, (n + 255) / 256, 256, 0, st,
+           recv, R, T_own, k, H, ep_row_bytes(H, k), e_begin,
                                                     e_count, recv_counts, world, idx_local,
                                                     w_local, ret_dst);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
@@ -383,8 +383,8 @@ int launch_ep_return_gather(const void* O, int H, const int* route_slot, const i
   if (n_routes <= 0) return DSV4_OK;
   int grid = (n_routes + 7) / 8;
   grid = grid < num_sms * 8 ? grid : num_sms * 8;
-  count_launch();
-  ep_return_gather_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(O), H, route_slot,
+  launch_k(ep_return_gather_kernel, grid, 256, 0, st,
+           static_cast<const __nv_bfloat16*>(O), H, route_slot,
                                                 ret_dst, n_routes, ret_rows,
                                                 static_cast<__nv_bfloat16*>(ret));
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;

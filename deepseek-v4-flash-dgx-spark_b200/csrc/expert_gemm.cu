@@ -475,8 +475,8 @@ static int launch_one(const CUtensorMap& a0, const CUtensorMap& a1, const CUtens
       return DSV4_ERR_CUDA;
     attr_set = true;
   }
-  count_launch();
-  expert_gemm_kernel<BM, GATED><<<grid, 192, C::SMEM_BYTES, st>>>(a0, a1, s0, s1, b, args);
+  launch_k(expert_gemm_kernel<BM, GATED>, grid, 192, C::SMEM_BYTES, st,
+           a0, a1, s0, s1, b, args);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
 

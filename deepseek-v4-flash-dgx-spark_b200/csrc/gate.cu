@@ -137,7 +137,10 @@ __global__ void __launch_bounds__(512) gate_topk_kernel(const float* __restrict_
                                                         const float* __restrict__ bias, int T,
                                                         int E, int k, float route_scale,
                                                         float* __restrict__ weights,
-                                                        int64_t* __restrict__ indices) {
+                                                        int64_t* __restrict__ indices,
+                                                        const int64_t* __restrict__ hash_table,
+                                                        const int64_t* __restrict__ input_ids,
+                                                        long long vocab) {
   // One CTA per token, one thread per expert: each thread sums its expert's
   // split-K slices in slice order (loads issued kSliceBatch at a time so they
   // are in flight together), then warp 0 selects the top k from shared memory.
@@ -163,6 +166,30 @@ __global__ void __launch_bounds__(512) gate_topk_kernel(const float* __restrict_
   }
   __syncthreads();
   if (threadIdx.x >= 32) return;
+  if (hash_table) {
+    // hash-routed layer: the experts are the table row of the token id (rank
+    // order of the row), the weights their scores renormalised in that order
+    const long long id = input_ids[t];
+    int e = -1;
+    if (lane < k) {
+      if (id >= 0 && id < vocab) {
+        const int64_t v = hash_table[id * k + lane];
+        if (v >= 0 && v < E) e = static_cast<int>(v);
+      }
+      if (e < 0) record_error(DSV4_DEVERR_BAD_INDEX);
+    }
+    const float w = e >= 0 ? s_score[e] : 0.f;
+    float total = 0.f;
+    for (int r = 0; r < k; ++r) {
+      const float wr = __shfl_sync(0xffffffffu, w, r);
+      total = (r == 0) ? wr : __fadd_rn(total, wr);
+    }
+    if (lane < k) {
+      weights[(size_t)t * k + lane] = e >= 0 ? __fmul_rn(__fdiv_rn(w, total), route_scale) : 0.f;
+      indices[(size_t)t * k + lane] = e;
+    }
+    return;
+  }
   float score[kMaxExpertsPerLane], sel[kMaxExpertsPerLane];
   const int per = (E + 31) / 32;
 #pragma unroll
@@ -232,14 +259,14 @@ int launch_gate_logits(const void* x, const void* w, int w_is_fp32, int T, int H
   if (w_is_fp32) {
     cudaFuncSetAttribute(gate_logits_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
-    count_launch();
-    gate_logits_kernel<true><<<grid, kGateThreads, smem, st>>>(static_cast<const __nv_bfloat16*>(x), w, T,
+    launch_k(gate_logits_kernel<true>, grid, kGateThreads, smem, st,
+             static_cast<const __nv_bfloat16*>(x), w, T,
                                                       H, E, logits);
   } else {
     cudaFuncSetAttribute(gate_logits_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
-    count_launch();
-    gate_logits_kernel<false><<<grid, kGateThreads, smem, st>>>(static_cast<const __nv_bfloat16*>(x), w,
+    launch_k(gate_logits_kernel<false>, grid, kGateThreads, smem, st,
+             static_cast<const __nv_bfloat16*>(x), w,
                                                        T, H, E, logits);
   }
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
@@ -247,12 +274,12 @@ int launch_gate_logits(const void* x, const void* w, int w_is_fp32, int T, int H
 
 int launch_gate_topk(const float* logits, const float* bias, int T, int E, int k,
                      float route_scale, float* weights, int64_t* indices, cudaStream_t st,
-                     int nsplit, float* logits_out) {
+                     int nsplit, float* logits_out, const int64_t* hash_table,
+                     const int64_t* input_ids, long long vocab) {
   const int threads = std::min(kMaxExpertsPerLane * 32, (E + 31) / 32 * 32);
   if (T > 0) {
-    count_launch();
-    gate_topk_kernel<<<T, threads, 0, st>>>(logits, nsplit, logits_out, bias, T, E, k, route_scale,
-                                            weights, indices);
+    launch_k(gate_topk_kernel, T, threads, 0, st, logits, nsplit, logits_out, bias, T, E, k,
+             route_scale, weights, indices, hash_table, input_ids, vocab);
   }
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }

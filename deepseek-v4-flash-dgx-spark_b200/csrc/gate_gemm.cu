@@ -286,9 +286,8 @@ static int launch_gate_gemm_cfg(const void* x, const void* w, int T, int H, int 
   }
   const int items = (T + BM - 1) / BM * (E / NE) * ksplit;
   const int grid = items < num_sms ? items : num_sms;
-  count_launch();
-  gate_gemm_kernel<BM, NE, FUSED><<<grid, 192, C::SMEM_BYTES, st>>>(
-      tx, tw, T, H, E, ksplit, bias, k, route_scale, out, weights, indices);
+  launch_k(gate_gemm_kernel<BM, NE, FUSED>, grid, 192, C::SMEM_BYTES, st,
+           tx, tw, T, H, E, ksplit, bias, k, route_scale, out, weights, indices);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
 

@@ -31,7 +31,9 @@ int launch_gate_logits(const void* x, const void* w, int w_is_fp32, int T, int H
                        float* logits, cudaStream_t st);
 int launch_gate_topk(const float* logits, const float* bias, int T, int E, int k,
                      float route_scale, float* weights, int64_t* indices, cudaStream_t st,
-                     int nsplit = 1, float* logits_out = nullptr);
+                     int nsplit = 1, float* logits_out = nullptr,
+                     const int64_t* hash_table = nullptr, const int64_t* input_ids = nullptr,
+                     long long vocab = 0);
 int launch_gate_gemm_partials(const void* x, const void* w, int T, int H, int E, float* partials,
                               int num_sms, cudaStream_t st);
 void gate_gemm_split_shape(int T, int H, int E, int num_sms, int* bm, int* ksplit);

@@ -52,13 +52,116 @@ __global__ void __launch_bounds__(256) route_count_kernel(const int64_t* __restr
   for (int e = threadIdx.x; e < E; e += blockDim.x) chunk_cnt[(size_t)e * nchunks + c] = hist[e];
 }
 
+// Segment layout of one CTA from the per-segment counts s_cnt[0..NS) (shared
+// memory): padded segment starts and tile bases by a warp-0 scan, then the
+// tile list, the padding rows and the published counts.  A failed plan (an
+// invalid index seen earlier, or more rows / tiles than the workspace holds)
+// records a device error, sets ctrl[2] and emits no tiles.
+__device__ void plan_layout(int* s_cnt, int* s_start, int* s_tbase, int NS, int block_n,
+                            int max_rows, int max_tiles, int bad, int* __restrict__ counts,
+                            int* __restrict__ seg_start, int4* __restrict__ tiles,
+                            int* __restrict__ n_tiles, int* __restrict__ slot_token,
+                            float* __restrict__ slot_weight, int* __restrict__ ctrl) {
+  __shared__ int s_fail;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
+  __syncthreads();
+  if (warp == 0) {
+    int row_run = 0, tile_run = 0;
+    for (int s0 = 0; s0 < NS; s0 += 32) {
+      const int s = s0 + lane;
+      const int c = s < NS ? s_cnt[s] : 0;
+      const int rows = (c + kSegAlign - 1) / kSegAlign * kSegAlign;
+      const int nt = (c + block_n - 1) / block_n;
+      int r_inc = rows, t_inc = nt;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int a = __shfl_up_sync(0xffffffffu, r_inc, o);
+        const int b = __shfl_up_sync(0xffffffffu, t_inc, o);
+        if (lane >= o) {
+          r_inc += a;
+          t_inc += b;
+        }
+      }
+      if (s < NS) {
+        s_start[s] = row_run + r_inc - rows;
+        s_tbase[s] = tile_run + t_inc - nt;
+      }
+      row_run += __shfl_sync(0xffffffffu, r_inc, 31);
+      tile_run += __shfl_sync(0xffffffffu, t_inc, 31);
+    }
+    if (lane == 0) {
+      s_start[NS] = row_run;
+      s_tbase[NS] = tile_run;
+      s_fail = bad || row_run > max_rows || tile_run > max_tiles;
+      if (s_fail) record_error(bad ? DSV4_DEVERR_BAD_INDEX : DSV4_DEVERR_PLAN_OVERFLOW);
+      ctrl[2] = s_fail;
+    }
+  }
+  __syncthreads();
+  if (s_fail) {
+    if (tid == 0) *n_tiles = 0;
+    return;
+  }
+  for (int s = tid; s <= NS; s += nthr) {
+    seg_start[s] = s_start[s];
+    if (s < NS) counts[s] = s_cnt[s];
+  }
+  for (int s = warp; s < NS; s += nthr / 32) {
+    const int c = s_cnt[s], base = s_start[s], nt = s_tbase[s + 1] - s_tbase[s];
+    for (int m = lane; m < nt; m += 32)
+      tiles[s_tbase[s] + m] = make_int4(s, base + m * block_n, min(block_n, c - m * block_n), 0);
+    for (int r = base + c + lane; r < s_start[s + 1]; r += 32) {
+      slot_token[r] = -1;
+      slot_weight[r] = 0.f;
+    }
+  }
+  if (tid == 0) *n_tiles = s_tbase[NS];
+}
+
+// Small batches: count, per-chunk scan and layout in one CTA, every count in
+// shared memory ([nchunks][E], at most kSmallPlanInts).  Produces the same
+// plan and chunk offsets as route_count + route_scan.
+constexpr int kSmallPlanInts = 10240;  // with the layout arrays, under 48 KB of static smem
+
+__global__ void __launch_bounds__(1024) route_plan_small_kernel(
+    const int64_t* __restrict__ indices, int T, int k, int E, int allow_skip, int shared_rows,
+    int chunk, int nchunks, int block_n, int max_rows, int max_tiles,
+    int* __restrict__ chunk_base, int* __restrict__ counts, int* __restrict__ seg_start,
+    int4* __restrict__ tiles, int* __restrict__ n_tiles, int* __restrict__ slot_token,
+    float* __restrict__ slot_weight, int* __restrict__ ctrl) {
+  __shared__ int cnt[kSmallPlanInts];
+  __shared__ int s_cnt[kMaxSegments], s_start[kMaxSegments + 1], s_tbase[kMaxSegments + 1];
+  __shared__ int s_bad;
+  const int tid = threadIdx.x;
+  for (int i = tid; i < nchunks * E; i += blockDim.x) cnt[i] = 0;
+  if (tid == 0) s_bad = 0;
+  __syncthreads();
+  for (int i = tid; i < T * k; i += blockDim.x) {
+    const int64_t v = indices[i];
+    if (v >= 0 && v < E) atomicAdd(&cnt[(i / k / chunk) * E + (int)v], 1);
+    else if (!(allow_skip && v == -1)) s_bad = 1;
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += blockDim.x) {
+    int run = 0;
+    for (int c = 0; c < nchunks; ++c) {
+      chunk_base[(size_t)e * nchunks + c] = run;
+      run += cnt[c * E + e];
+    }
+    s_cnt[e] = run;
+  }
+  if (tid == 0) s_cnt[E] = shared_rows;
+  plan_layout(s_cnt, s_start, s_tbase, E + 1, block_n, max_rows, max_tiles, s_bad, counts,
+              seg_start, tiles, n_tiles, slot_token, slot_weight, ctrl);
+}
+
 __global__ void __launch_bounds__(kScanThreads) route_scan_kernel(
     const int* __restrict__ chunk_cnt, int nchunks, int E, int shared_rows, int block_n,
     int max_rows, int max_tiles, int* __restrict__ chunk_base, int* __restrict__ counts,
     int* __restrict__ seg_start, int4* __restrict__ tiles, int* __restrict__ n_tiles,
     int* __restrict__ slot_token, float* __restrict__ slot_weight, int* __restrict__ ctrl) {
   __shared__ int s_cnt[kMaxSegments], s_start[kMaxSegments + 1], s_tbase[kMaxSegments + 1];
-  __shared__ int s_last, s_fail;
+  __shared__ int s_last;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // one warp per expert: exclusive scan of its chunk counts in chunk (token) order
   const int e = blockIdx.x * (kScanThreads / 32) + warp;
@@ -88,64 +191,10 @@ __global__ void __launch_bounds__(kScanThreads) route_scan_kernel(
   __threadfence();
 
   // the last CTA: padded segment offsets, tiles, padding rows
-  const int NS = E + 1;
-  for (int s = tid; s < NS; s += kScanThreads)
-    s_cnt[s] = s < E ? __ldcg(counts + s) : shared_rows;
-  __syncthreads();
-  if (warp == 0) {
-    int row_run = 0, tile_run = 0;
-    for (int s0 = 0; s0 < NS; s0 += 32) {
-      const int s = s0 + lane;
-      const int c = s < NS ? s_cnt[s] : 0;
-      const int rows = (c + kSegAlign - 1) / kSegAlign * kSegAlign;
-      const int nt = (c + block_n - 1) / block_n;
-      int r_inc = rows, t_inc = nt;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int a = __shfl_up_sync(0xffffffffu, r_inc, o);
-        const int b = __shfl_up_sync(0xffffffffu, t_inc, o);
-        if (lane >= o) {
-          r_inc += a;
-          t_inc += b;
-        }
-      }
-      if (s < NS) {
-        s_start[s] = row_run + r_inc - rows;
-        s_tbase[s] = tile_run + t_inc - nt;
-      }
-      row_run += __shfl_sync(0xffffffffu, r_inc, 31);
-      tile_run += __shfl_sync(0xffffffffu, t_inc, 31);
-    }
-    if (lane == 0) {
-      s_start[NS] = row_run;
-      s_tbase[NS] = tile_run;
-      const int bad = __ldcg(ctrl + 1);
-      s_fail = bad || row_run > max_rows || tile_run > max_tiles;
-      if (s_fail) {
-        record_error(bad ? DSV4_DEVERR_BAD_INDEX : DSV4_DEVERR_PLAN_OVERFLOW);
-        ctrl[2] = 1;
-      }
-    }
-  }
-  __syncthreads();
-  if (s_fail) {
-    if (tid == 0) *n_tiles = 0;
-    return;
-  }
-  for (int s = tid; s <= NS; s += kScanThreads) {
-    seg_start[s] = s_start[s];
-    if (s < NS) counts[s] = s_cnt[s];
-  }
-  for (int s = warp; s < NS; s += kScanThreads / 32) {
-    const int c = s_cnt[s], base = s_start[s], nt = s_tbase[s + 1] - s_tbase[s];
-    for (int m = lane; m < nt; m += 32)
-      tiles[s_tbase[s] + m] = make_int4(s, base + m * block_n, min(block_n, c - m * block_n), 0);
-    for (int r = base + c + lane; r < s_start[s + 1]; r += 32) {
-      slot_token[r] = -1;
-      slot_weight[r] = 0.f;
-    }
-  }
-  if (tid == 0) *n_tiles = s_tbase[NS];
+  for (int s = tid; s < E; s += kScanThreads) s_cnt[s] = __ldcg(counts + s);
+  if (tid == 0) s_cnt[E] = shared_rows;
+  plan_layout(s_cnt, s_start, s_tbase, E + 1, block_n, max_rows, max_tiles, __ldcg(ctrl + 1), counts,
+              seg_start, tiles, n_tiles, slot_token, slot_weight, ctrl);
 }
 
 // Per-128 act_quant of one token row by one warp, the codes and scales written
@@ -471,12 +520,20 @@ int launch_route_plan(const int64_t* indices, int T, int k, int E, int allow_ski
   if (T <= 0 || k > kMaxK || E + 1 > kMaxSegments) return DSV4_ERR_ARG;
   const int chunk = route_chunk_tokens(T);
   const int nchunks = (T + chunk - 1) / chunk;
+  if (nchunks * E <= kSmallPlanInts) {
+    launch_k(route_plan_small_kernel, 1, 1024, 0, st,
+             indices, T, k, E, allow_skip, shared_rows, chunk,
+                                                nchunks, block_n, max_rows, max_tiles, chunk_base,
+                                                counts, seg_start, tiles, n_tiles, slot_token,
+                                                slot_weight, ctrl);
+    return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
+  }
   if (cudaMemsetAsync(ctrl, 0, 4 * sizeof(int), st) != cudaSuccess) return DSV4_ERR_CUDA;
-  count_launch();
-  route_count_kernel<<<nchunks, 256, 0, st>>>(indices, T, k, E, allow_skip, chunk, nchunks,
+  launch_k(route_count_kernel, nchunks, 256, 0, st,
+           indices, T, k, E, allow_skip, chunk, nchunks,
                                               chunk_cnt, ctrl);
-  count_launch();
-  route_scan_kernel<<<(E + kScanThreads / 32 - 1) / (kScanThreads / 32), kScanThreads, 0, st>>>(chunk_cnt, nchunks, E, shared_rows, block_n,
+  launch_k(route_scan_kernel, (E + kScanThreads / 32 - 1) / (kScanThreads / 32), kScanThreads, 0, st,
+           chunk_cnt, nchunks, E, shared_rows, block_n,
                                                 max_rows, max_tiles, chunk_base, counts, seg_start,
                                                 tiles, n_tiles, slot_token, slot_weight, ctrl);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
@@ -495,9 +552,8 @@ int launch_route_scatter(const void* x, int n_x_rows, const uint8_t* rows_in,
   int ksplit = (4 * num_sms) / nchunks;
   ksplit = ksplit < 1 ? 1 : (ksplit > KT / kQuantGroup ? KT / kQuantGroup : ksplit);
   if (ksplit < 1) ksplit = 1;
-  count_launch();
-  route_scatter_kernel<<<dim3(nchunks, ksplit), 256, 0, st>>>(
-      static_cast<const __nv_bfloat16*>(x), n_x_rows, rows_in, rows_in_stride, indices, weights, T,
+  launch_k(route_scatter_kernel, dim3(nchunks, ksplit), 256, 0, st,
+           static_cast<const __nv_bfloat16*>(x), n_x_rows, rows_in, rows_in_stride, indices, weights, T,
       k, E, H, shared_rows, chunk, nchunks, seg_start, chunk_base, ctrl, route_slot, slot_token,
       slot_weight, xq, sfb);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
@@ -509,8 +565,8 @@ int launch_permute_quant(const void* x, int H, const int* slot_token, const int*
   int grid = (max_rows + warps - 1) / warps;
   grid = grid < num_sms * 8 ? grid : num_sms * 8;
   if (grid < 1) grid = 1;
-  count_launch();
-  permute_quant_kernel<<<grid, warps * 32, 0, st>>>(static_cast<const __nv_bfloat16*>(x), H,
+  launch_k(permute_quant_kernel, grid, warps * 32, 0, st,
+           static_cast<const __nv_bfloat16*>(x), H,
                                                     slot_token, total_rows_ptr, xq, sfb);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
@@ -519,9 +575,9 @@ int launch_single_segment_plan(int T, int seg, int block_n, int rows_pad, const 
                                int* slot_token, float* slot_weight, int4* tiles, int* n_tiles,
                                int* total_rows, cudaStream_t st) {
   const int grid = (rows_pad + 255) / 256;
-  count_launch();
-  single_segment_plan_kernel<<<grid > 0 ? grid : 1, 256, 0, st>>>(
-      T, seg, block_n, rows_pad, w, slot_token, slot_weight, tiles, n_tiles, total_rows);
+  const int grid1 = grid > 0 ? grid : 1;
+  launch_k(single_segment_plan_kernel, grid1, 256, 0, st,
+           T, seg, block_n, rows_pad, w, slot_token, slot_weight, tiles, n_tiles, total_rows);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
 
@@ -531,8 +587,8 @@ int launch_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* s, int nu
   int grid = (M + warps - 1) / warps;
   grid = grid < num_sms * 8 ? grid : num_sms * 8;
   if (grid < 1) return DSV4_OK;
-  count_launch();
-  act_quant_kernel<<<grid, warps * 32, 0, st>>>(static_cast<const __nv_bfloat16*>(x), M, K, q, s);
+  launch_k(act_quant_kernel, grid, warps * 32, 0, st,
+           static_cast<const __nv_bfloat16*>(x), M, K, q, s);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
 
@@ -541,8 +597,9 @@ int launch_combine(const void* O, int H, const int* route_slot, const int64_t* i
   if (T <= 0) return DSV4_OK;
   const __nv_bfloat16* o = static_cast<const __nv_bfloat16*>(O);
   const __nv_bfloat16* osh = O_shared ? static_cast<const __nv_bfloat16*>(O_shared) : o;
-  count_launch();
-  combine_kernel<<<T, H / 8 < 512 ? H / 8 : 512, 0, st>>>(o, H, route_slot, indices, T, k, shared_base,
+  const int threads = H / 8 < 512 ? H / 8 : 512;
+  launch_k(combine_kernel, T, threads, 0, st,
+           o, H, route_slot, indices, T, k, shared_base,
                                                           osh, static_cast<__nv_bfloat16*>(y));
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }

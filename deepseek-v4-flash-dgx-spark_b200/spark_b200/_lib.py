@@ -101,6 +101,9 @@ _SIGNATURES = {
         [c_int, c_vp, c_ll, c_ll, c_ll, ctypes.POINTER(c_vp), c_llp, c_llp, c_llp, c_int, c_int, c_vp,
          c_llp, c_llp, c_dp, c_dp, c_ip],
     ),
+    "dsv4_gate_hash_workspace_bytes": (c_ll, [c_vp, c_int, c_int, c_int, c_int]),
+    "dsv4_gate_route_hash": (c_int, [c_vp, c_vp, c_int, c_vp, c_ll, c_vp, c_int, c_int, c_int, c_int, c_float,
+                                     c_vp, c_vp, c_vp, c_vp, c_ll, c_vp]),
     "dsv4_ep_row_bytes": (c_ll, [c_int, c_int]),
     "dsv4_ep_dispatch_workspace_bytes": (c_ll, [c_int, c_int]),
     "dsv4_ep_dispatch": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp, c_ll, c_vp, c_vp,

@@ -50,6 +50,8 @@ class ModelArgs:
     score_func: str = "sigmoid"
     gate_dtype: torch.dtype = torch.bfloat16
     gate_bias: bool = True
+    n_hash_layers: int = 0          # layers [0, n_hash_layers) route by gate.tid2eid[input_ids]
+    vocab_size: int = 129280
 
 
 # ---------------------------------------------------------------------------
@@ -311,9 +313,14 @@ class Gate(nn.Module):
         if args.score_func != "sigmoid":
             raise RuntimeError(f"unsupported score function {args.score_func!r}")
         device = device or "cuda"
+        self.hashed = layer_id < args.n_hash_layers
         self.weight = nn.Parameter(torch.zeros(self.n_experts, self.dim, dtype=args.gate_dtype, device=device),
                                    requires_grad=False)
-        if args.gate_bias:
+        if self.hashed:  # checkpoint tensor gate.tid2eid [vocab, k] int64; no correction bias
+            self.register_buffer("tid2eid", torch.zeros(args.vocab_size, self.topk, dtype=torch.int64,
+                                                        device=device))
+            self.register_parameter("bias", None)
+        elif args.gate_bias:
             self.bias = nn.Parameter(torch.zeros(self.n_experts, dtype=torch.float32, device=device),
                                      requires_grad=False)
         else:
@@ -345,6 +352,20 @@ class Gate(nn.Module):
         idx = torch.empty(T, self.topk, dtype=torch.int64, device=x.device)
         lib = _lib.load()
         fp32 = int(self.weight.dtype == torch.float32)
+        if self.hashed:
+            if input_ids is None:
+                raise RuntimeError(f"layer {self.layer_id} routes by token id: input_ids is required")
+            ids = input_ids.reshape(-1).to(device=x.device, dtype=torch.int64).contiguous()
+            if ids.numel() != T:
+                raise RuntimeError("input_ids must hold one id per token")
+            need = lib.dsv4_gate_hash_workspace_bytes(ptr(self.weight), fp32, T, self.dim, self.n_experts)
+            ws = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device) if need > 0 else None
+            check(lib.dsv4_gate_route_hash(ptr(x), ptr(self.weight), fp32, ptr(self.tid2eid), self.tid2eid.shape[0],
+                                           ptr(ids), T, self.dim, self.n_experts, self.topk, self.route_scale,
+                                           ptr(logits), ptr(w), ptr(idx), ptr(ws), max(need, 0), stream_ptr()),
+                  "dsv4_gate_route_hash")
+            self.last_logits = logits
+            return w, idx
         need = lib.dsv4_gate_workspace_bytes(ptr(self.weight), fp32, T, self.dim, self.n_experts)
         ws = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device) if need > 0 else None
         check(lib.dsv4_gate_route(ptr(x), ptr(self.weight), fp32, ptr(self.bias), T, self.dim, self.n_experts,
@@ -458,10 +479,11 @@ class MoE(nn.Module):
         if x2.dtype != torch.bfloat16:
             x2 = x2.to(torch.bfloat16)
         x2 = x2.contiguous()
+        routing = self.gate(x2, input_ids) if self.gate.hashed else None
         if self.world == 1:
-            y = self.forward_tokens(x2)
+            y = self.forward_tokens(x2, routing=routing)
         else:
             from .ep import ep_moe_forward
 
-            y = ep_moe_forward(self, x2)
+            y = ep_moe_forward(self, x2, routing=routing)
         return y.type_as(x).view(shape)

@@ -140,18 +140,20 @@ def make_layer(cfg: LayerConfig, seed: int = 0, device="cpu") -> dict:
     return {"cfg": cfg, "x": x, "gate_w": gate_w, "gate_bias": gate_bias, "blocks": blocks, "shared": shared}
 
 
-def build_moe(layer: dict, device="cuda", layer_id: int = 3, group=None) -> MoE:
+def build_moe(layer: dict, device="cuda", layer_id: int = 3, group=None, args: ModelArgs | None = None) -> MoE:
     """A ``MoE`` whose arena is filled by the device materializer from the
     synthetic packed blocks (uploaded as one slab) and whose gate and shared
     expert hold the synthetic tensors.  Under torch.distributed the layer is
     split over ``group`` (default: the world) and each rank materializes only
-    the experts it owns."""
+    the experts it owns.  ``args`` overrides the layer's ModelArgs (e.g. for
+    a hash-routed layer, whose gate has no bias)."""
     cfg: LayerConfig = layer["cfg"]
     dev = torch.device(device)
-    moe = MoE(layer_id, cfg.args(), device=dev, group=group)
+    moe = MoE(layer_id, args or cfg.args(), device=dev, group=group)
     with torch.no_grad():
         moe.gate.weight.copy_(layer["gate_w"].to(dev))
-        moe.gate.bias.copy_(layer["gate_bias"].to(dev))
+        if moe.gate.bias is not None:
+            moe.gate.bias.copy_(layer["gate_bias"].to(dev))
         sh = moe.shared_experts
         for name in ("w1", "w2", "w3"):
             getattr(sh, name).weight.view(torch.uint8).copy_(layer["shared"][f"{name}.weight"].to(dev))

@@ -128,7 +128,9 @@ DSV4_API int dsv4_expert_forward(const dsv4_moe_layer* L, int expert, const void
  * forward records library-owned CUDA events between its kernels (as graph
  * nodes when the stream is being captured).  dsv4_profile_read waits for the
  * last forward and returns 6 durations in ms: gate, plan, permute, GEMM1,
- * GEMM2, combine. */
+ * GEMM2, combine.  The events are created on first enable and live until
+ * the process exits, so graphs captured while profiling stay valid after
+ * profiling is disabled. */
 DSV4_API int dsv4_profile_enable(int enable);
 DSV4_API int dsv4_profile_read(float* stage_ms, int n);
 
@@ -173,6 +175,19 @@ DSV4_API int dsv4_gate_route(const void* x, const void* w, int w_is_fp32, const 
                              int H, int E, int topk, float route_scale, float* logits,
                              float* weights, int64_t* indices, void* workspace,
                              long long workspace_bytes, void* stream);
+
+/* Hash-routed layers (the official Gate with gate.tid2eid, layers 0-2 of the
+ * checkpoint, weight-manifest.csv:3): the experts of token t are the row
+ * tid2eid[input_ids[t]] ([vocab][topk] int64, in row order); the weights are
+ * their sigmoid scores renormalised to sum 1 in row order, times route_scale.
+ * logits [T][E] fp32 are written as for dsv4_gate_route.  Invalid ids or
+ * table entries latch DSV4_DEVERR_BAD_INDEX and give index -1, weight 0. */
+DSV4_API long long dsv4_gate_hash_workspace_bytes(const void* w, int w_is_fp32, int T, int H, int E);
+DSV4_API int dsv4_gate_route_hash(const void* x, const void* w, int w_is_fp32, const int64_t* tid2eid,
+                                  long long vocab, const int64_t* input_ids, int T, int H, int E,
+                                  int topk, float route_scale, float* logits, float* weights,
+                                  int64_t* indices, void* workspace, long long workspace_bytes,
+                                  void* stream);
 
 /* Official kernel.act_quant(x, 128, "ue8m0") (scripts/smoke_official_kernels.py:
  * 44-49): bf16 [M,K] -> e4m3 codes [M,K] + ue8m0 scales [M,K/128]. */

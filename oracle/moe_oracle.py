@@ -247,6 +247,22 @@ def route_from_logits(logits: np.ndarray, bias: np.ndarray | None, topk: int,
     return wts, idx.astype(np.int64)
 
 
+def hash_route(logits: np.ndarray, tid2eid: np.ndarray, input_ids: np.ndarray, route_scale: float):
+    """Hash-routed layers (gate.tid2eid [vocab, k], weight-manifest.csv:3; the
+    official Gate's hash mode is absent here, so this is the restated choice):
+    experts = tid2eid[input_id] in row order; weights = their canonical
+    sigmoid scores renormalised to sum 1 in row order (fp32), x route_scale."""
+    idx = np.asarray(tid2eid)[np.asarray(input_ids).reshape(-1)].astype(np.int64)
+    T, k = idx.shape
+    scores = sigmoid_canonical(np.asarray(logits, np.float32))
+    w = scores[np.arange(T)[:, None], idx].astype(np.float32)
+    total = w[:, 0].copy()
+    for j in range(1, k):
+        total = (total + w[:, j]).astype(np.float32)
+    w = ((w / total[:, None]).astype(np.float32) * np.float32(route_scale)).astype(np.float32)
+    return w, idx
+
+
 def gate_forward(x, w, bias, topk, route_scale):
     logits = gate_logits(x, w)
     wts, idx = route_from_logits(logits, bias, topk, route_scale)

@@ -357,12 +357,14 @@ def _plan_from_ws(ws, offs, T, k, E):
 
 @pytest.mark.parametrize("name,T,pattern", [("cpu_ref", 1, "random"), ("cpu_ref", 37, "random"),
                                             ("cpu_ref", 300, "one_hot"), ("cpu_ref", 1500, "random"),
-                                            ("decode", 64, "random"), ("decode", 1100, "skewed")])
+                                            ("decode", 64, "random"), ("decode", 1100, "skewed"),
+                                            ("decode", 2048, "random")])
 def test_route_plan_matches_oracle(cuda_device, name, T, pattern):
     """counts, padded segment starts, every route's slot, every slot's token
     (-1 on padding) and the tile list equal the oracle's stable counting sort;
     covers one chunk, ragged chunks, both chunk sizes and a segment holding
-    every token."""
+    every token.  Up to 40 chunks x 256 experts the plan is built by one CTA,
+    beyond that (T=2048) by the multi-CTA count / scan kernels."""
     from spark_b200.synthetic import CONFIGS, build_moe, make_layer
 
     cfg = CONFIGS[name].with_tokens(T)
@@ -394,3 +396,61 @@ def test_route_plan_matches_oracle(cuda_device, name, T, pattern):
     for key in ("counts", "seg_start", "route_slot", "slot_token"):
         assert np.array_equal(got[key], ref[key]), key
     assert got["tiles"] == ref["tiles"]
+
+
+# ---------------------------------------------------------------------------
+# hash-routed layers (gate.tid2eid)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("name,T", [("cpu_ref", 5), ("decode", 1), ("decode", 37), ("decode", 3000)])
+def test_hash_gate_bit_exact_on_device_logits(cuda_device, name, T):
+    """Indices are the table rows of the token ids; weights equal the oracle's
+    hash routing on the device's own logits bit for bit (SIMT logits for the
+    fp32 gate, tensor-core partials otherwise, also above the fused size)."""
+    from dataclasses import replace
+
+    from spark_b200.moe import Gate
+    from spark_b200.synthetic import CONFIGS, make_layer
+
+    cfg = CONFIGS[name].with_tokens(T)
+    layer = make_layer(cfg, seed=5, device="cpu")
+    args = replace(cfg.args(), n_hash_layers=3, vocab_size=1000)
+    gate = Gate(0, args, device=cuda_device)
+    g = torch.Generator().manual_seed(T)
+    table = torch.stack([torch.randperm(cfg.n_routed, generator=g)[:cfg.topk] for _ in range(1000)])
+    ids = torch.randint(0, 1000, (T,), generator=g)
+    with torch.no_grad():
+        gate.weight.copy_(layer["gate_w"].to(cuda_device))
+        gate.tid2eid.copy_(table.to(cuda_device))
+    w, idx = gate(layer["x"].to(cuda_device), ids.to(cuda_device))
+    torch.cuda.synchronize()
+    _no_device_error()
+    logits = gate.last_logits.cpu().numpy()
+    ref_logits = O.gate_logits(layer["x"].float().numpy(), layer["gate_w"].float().numpy())
+    assert np.max(np.abs(logits - ref_logits)) < 1e-4
+    w_ref, i_ref = O.hash_route(logits, table.numpy(), ids.numpy(), cfg.route_scale)
+    assert np.array_equal(idx.cpu().numpy(), i_ref)
+    assert np.array_equal(w.cpu().numpy().view(np.uint32), w_ref.view(np.uint32))
+
+
+def test_hash_layer_forward_matches_oracle(cuda_device):
+    """MoE.forward of a hash-routed layer: routing from the table, experts and
+    combine as in the top-k layers."""
+    from dataclasses import replace
+
+    from spark_b200.synthetic import CONFIGS, build_moe, make_layer
+
+    cfg = CONFIGS["cpu_ref"].with_tokens(40)
+    layer = make_layer(cfg, seed=6, device="cpu")
+    moe = build_moe(layer, device=cuda_device, layer_id=0, args=replace(cfg.args(), n_hash_layers=3, vocab_size=64))
+    g = torch.Generator().manual_seed(1)
+    table = torch.stack([torch.randperm(cfg.n_routed, generator=g)[:cfg.topk] for _ in range(64)])
+    ids = torch.randint(0, 64, (1, 40), generator=g)
+    with torch.no_grad():
+        moe.gate.tid2eid.copy_(table.to(cuda_device))
+    y = moe(layer["x"].view(1, 40, -1).to(cuda_device), ids.to(cuda_device))
+    torch.cuda.synchronize()
+    _no_device_error()
+    w_ref, i_ref = O.hash_route(moe.gate.last_logits.cpu().numpy(), table.numpy(), ids.numpy(), cfg.route_scale)
+    mw = _oracle_weights(layer, sorted(set(i_ref.reshape(-1).tolist())))
+    y_ref = O.moe_forward(layer["x"].float().numpy(), mw, routing=(w_ref, i_ref))[0]
+    assert _rel_err(_bf16_np(y.view(40, -1)), y_ref) <= TOL

@@ -58,3 +58,16 @@ def test_model_args_defaults_are_v4_flash_shapes():
     assert (a.dim, a.moe_inter_dim, a.n_routed_experts, a.n_activated_experts, a.n_shared_experts) == (
         4096, 2048, 256, 6, 1)
     assert torch.float4_e2m1fn_x2 == FP4
+
+
+def test_hash_layer_gate_has_the_checkpoint_tensors():
+    """Layers below n_hash_layers hold gate.tid2eid [vocab, k] int64 and no
+    correction bias (weight-manifest.csv:3 vs :4724); later layers the bias."""
+    from spark_b200.moe import Gate
+
+    args = ModelArgs(dim=256, n_routed_experts=16, n_activated_experts=4, n_hash_layers=3, vocab_size=100)
+    g0 = Gate(0, args, device="cpu")
+    assert g0.hashed and tuple(g0.tid2eid.shape) == (100, 4) and g0.tid2eid.dtype == torch.int64
+    assert set(g0.state_dict()) == {"weight", "tid2eid"}
+    g3 = Gate(3, args, device="cpu")
+    assert not g3.hashed and set(g3.state_dict()) == {"weight", "bias"}

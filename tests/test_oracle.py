@@ -145,3 +145,17 @@ def test_route_plan_follows_torch_where_order():
     s0 = int(p["seg_start"][E])
     assert np.array_equal(p["slot_token"][s0:s0 + T], np.arange(T))
     assert sum(t[2] for t in p["tiles"]) == T * k + T
+
+
+def test_hash_route_uses_the_table_and_renormalises():
+    rng = np.random.default_rng(3)
+    T, E, k, vocab = 9, 16, 4, 50
+    logits = rng.standard_normal((T, E)).astype(np.float32)
+    table = np.stack([rng.permutation(E)[:k] for _ in range(vocab)])
+    ids = rng.integers(0, vocab, T)
+    w, idx = O.hash_route(logits, table, ids, 2.5)
+    assert np.array_equal(idx, table[ids])
+    assert np.allclose(w.sum(1), 2.5, rtol=1e-6)
+    s = O.sigmoid_canonical(logits)
+    assert np.allclose(w / 2.5, s[np.arange(T)[:, None], idx] / s[np.arange(T)[:, None], idx].sum(1, keepdims=True),
+                       rtol=1e-6)
