@@ -4,6 +4,7 @@
 #include "gate.cu"
 #include "route.cu"
 #include "expert_gemm.cu"
+#include "expert_gemm_pair.cu"
 #include "gate_gemm.cu"
 #include "materialize.cu"
 #include "ep.cu"

@@ -42,19 +42,26 @@ struct GemmCfg {
   static constexpr int B_HALF = 128 * 128;       // one 128-row weight box in smem
   static constexpr int B_BYTES = 2 * B_HALF;     // N = 256 weight rows
   static constexpr int TILE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int SF_STAGE = 1536;          // [act scales 512][weight scales 2 x 512]
-  static constexpr int STAGE_BYTES = TILE_BYTES + SF_STAGE;
+  // scale atoms of a group of four k tiles, loaded with the group's first
+  // tile into one of two ring slots: [act 512][weight half 0: 4 x 512][half 1: 4 x 512].
+  // A slot is refilled 8 k tiles after its last use, which the producer's
+  // stage wait already covers while STAGES <= 8.
+  static constexpr int SF_GROUP = 512 + 2 * 2048;
+  static constexpr int SF_RING = 2 * SF_GROUP;
+  static constexpr int STAGE_BYTES = TILE_BYTES;
   static constexpr int CTRL_BYTES = 256;
   // the whole 227 KB a CTA may hold: decode is bound by the weight bytes in
   // flight per SM, and an e2m1 box takes twice its global bytes in smem
   static constexpr int SMEM_MAX = 232448;
-  static constexpr int STAGES0 = (SMEM_MAX - 1024 - CTRL_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES0 = (SMEM_MAX - 1024 - CTRL_BYTES - SF_RING) / STAGE_BYTES;
   static constexpr int STAGES = STAGES0 > 8 ? 8 : STAGES0;
   static constexpr int ACC_COLS = 256;
-  static constexpr int SFA_COL = 256;            // activation scales: 4 columns
-  static constexpr int SFB_COL = 260;            // weight scales: 8 columns (256 rows)
+  // TMEM scale columns, two sets used by alternate k-tile groups: activation
+  // scales 4 columns, weight scales 4 k tiles x 8 columns (256 rows)
+  static constexpr int SFA_COL = 256;
+  static constexpr int SFB_COL = 264;
   static constexpr int TMEM_COLS = 512;
-  static constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + CTRL_BYTES;
+  static constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + SF_RING + CTRL_BYTES;
   static_assert(A_BYTES % 1024 == 0, "tiles must keep 1024-byte alignment");
   // the M = 128 MMA reads 128 rows (16 KB) from the A base; they must stay in the stage
   static_assert(128 * 128 <= TILE_BYTES, "A window leaves the stage");
@@ -129,7 +136,7 @@ __global__ void __launch_bounds__(192, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* tile_base = smem;
   uint8_t* sf_base = smem + (size_t)C::STAGES * C::TILE_BYTES;
-  uint8_t* ctrl = sf_base + (size_t)C::STAGES * C::SF_STAGE;
+  uint8_t* ctrl = sf_base + C::SF_RING;
   uint64_t* full = reinterpret_cast<uint64_t*>(ctrl);
   uint64_t* empty = full + C::STAGES;
   uint64_t* acc_full = empty + C::STAGES;
@@ -176,6 +183,7 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
+      int sf_slot = 1;  // ring slot of the current k-tile group (flips at each group)
       ItemInfo cur, nxt;
       if ((int)blockIdx.x < total) cur = decode_item<GATED>(args, blockIdx.x, NB, KT);
       for (int w = blockIdx.x; w < total && !*abort_flag; w += step) {
@@ -185,16 +193,18 @@ __global__ void __launch_bounds__(192, 1)
         const size_t g0 = (size_t)(cur.row0 >> 5);
         // transaction bytes count what the TMA reads from global memory: an e2m1
         // box is 8 KB there even though it spreads to 16 KB (16U4_ALIGN16B) in smem
-        const uint32_t tx_base = C::A_BYTES + 2u * (cur.shared ? C::B_HALF : C::B_HALF / 2) + 1024u;
+        const uint32_t tx_base = C::A_BYTES + 2u * (cur.shared ? C::B_HALF : C::B_HALF / 2);
         for (int kt = 0; kt < KT; ++kt) {
           if (!mbar_wait(&empty[stage], phase ^ 1, DSV4_DEVERR_TIMEOUT_PRODUCER)) {
             *abort_flag = 1;
             break;
           }
           uint8_t* st = tile_base + (size_t)stage * C::TILE_BYTES;
-          uint8_t* sf = sf_base + (size_t)stage * C::SF_STAGE;
-          const bool sfa_tile = (kt & 3) == 0;  // one k-packed activation scale atom per 4 tiles
-          mbar_arrive_expect_tx(&full[stage], tx_base + (sfa_tile ? 512u : 0u));
+          // the first k tile of each group of four carries the group's scale atoms
+          const bool sf_tile = (kt & 3) == 0;
+          if (sf_tile) sf_slot ^= 1;
+          uint8_t* sf = sf_base + (size_t)sf_slot * C::SF_GROUP;
+          mbar_arrive_expect_tx(&full[stage], tx_base + (sf_tile ? 512u + 4096u : 0u));
           tma_load_2d(st, &tmX, &full[stage], kt * 128, cur.row0);
           uint8_t* b = st + C::A_BYTES;
           if (cur.shared) {
@@ -205,10 +215,11 @@ __global__ void __launch_bounds__(192, 1)
             tma_load_3d(b + C::B_HALF, GATED ? &tmW1 : &tmW0, &full[stage], kt * 128, cur.r1,
                         cur.slot);
           }
-          if (sfa_tile)
+          if (sf_tile) {
             bulk_load(sf, args.sfb + (g0 * KT4 + (kt >> 2)) * 512, 512, &full[stage]);
-          bulk_load(sf + 512, cur.sfb0 + (size_t)kt * 512, 512, &full[stage]);
-          bulk_load(sf + 1024, cur.sfb1 + (size_t)kt * 512, 512, &full[stage]);
+            bulk_load(sf + 512, cur.sfb0 + (size_t)kt * 512, 2048, &full[stage]);
+            bulk_load(sf + 2560, cur.sfb1 + (size_t)kt * 512, 2048, &full[stage]);
+          }
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1;
@@ -229,6 +240,7 @@ __global__ void __launch_bounds__(192, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t aphase = 0;
+      int sf_slot = 1;  // follows the producer's ring slot
       const uint32_t sfa_t = tmem + C::SFA_COL;
       const uint32_t sfb_t = tmem + C::SFB_COL;
       int4 tl_next = make_int4(0, 0, 0, 0);
@@ -250,16 +262,27 @@ __global__ void __launch_bounds__(192, 1)
           }
           tc_fence_after();
           const uint8_t* st = tile_base + (size_t)stage * C::TILE_BYTES;
-          const uint8_t* sf = sf_base + (size_t)stage * C::SF_STAGE;
-          if ((kt & 3) == 0) tc_cp_sf(sfa_t, sdesc_sf(smem_u32(sf)));
-          tc_cp_sf(sfb_t, sdesc_sf(smem_u32(sf + 512)));
-          tc_cp_sf(sfb_t + 4, sdesc_sf(smem_u32(sf + 1024)));
+          // one burst of scale copies per four k tiles, into the column set the
+          // previous group's MMAs are not reading
+          if ((kt & 3) == 0) sf_slot ^= 1;
+          const uint8_t* sf = sf_base + (size_t)sf_slot * C::SF_GROUP;
+          const uint32_t set = sf_slot;
+          const uint32_t sfa_k = sfa_t + 4 * set;
+          const uint32_t sfb_k = sfb_t + 32 * set + 8 * (kt & 3);
+          if ((kt & 3) == 0) {
+            tc_cp_sf(sfa_k, sdesc_sf(smem_u32(sf)));
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              tc_cp_sf(sfb_k + 8 * j, sdesc_sf(smem_u32(sf + 512 + 512 * j)));
+              tc_cp_sf(sfb_k + 8 * j + 4, sdesc_sf(smem_u32(sf + 2560 + 512 * j)));
+            }
+          }
           const uint64_t adesc = sdesc_k_sw128(smem_u32(st));
           const uint64_t bdesc = sdesc_k_sw128(smem_u32(st + C::A_BYTES));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint32_t idesc = idesc_mxf8f6f4(0u, b_fmt, 256, kt & 3, kk);
-            tc_mma_mxf8f6f4(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, sfa_t, sfb_t,
+            tc_mma_mxf8f6f4(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, sfa_k, sfb_k,
                             (kt > 0 || kk > 0) ? 1u : 0u);
           }
           tc_commit(&empty[stage]);
@@ -309,26 +332,33 @@ __global__ void __launch_bounds__(192, 1)
       const bool warp_rows = q * 32 < nrows;  // TMEM lanes of this quarter hold real rows
       uint32_t pk[128];                       // packed bf16 pairs out of TMEM
       if (warp_rows) {
+        // 64 columns in flight per wait: the accumulator goes back to the MMA
+        // warp after four load round trips instead of sixteen
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          float a[16], b[16];
-          if (GATED) {  // pk[j] = (bf16 g_j, bf16 u_j) for j = 16c .. 16c+15
-            tmem_ld16(taddr + 16 * c, a);
-            tmem_ld16(taddr + 128 + 16 * c, b);
+        for (int c = 0; c < 4; ++c) {
+          uint32_t a[32], b[32];
+          if (GATED) {  // pk[j] = (bf16 g_j, bf16 u_j) for j = 32c .. 32c+31
+            tmem_ld32_issue(taddr + 32 * c, a);
+            tmem_ld32_issue(taddr + 128 + 32 * c, b);
+            tmem_wait_ld2(a, b);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const __nv_bfloat162 v = __floats2bfloat162_rn(a[i], b[i]);
-              pk[16 * c + i] = *reinterpret_cast<const uint32_t*>(&v);
+            for (int i = 0; i < 32; ++i) {
+              const __nv_bfloat162 v =
+                  __floats2bfloat162_rn(__uint_as_float(a[i]), __uint_as_float(b[i]));
+              pk[32 * c + i] = *reinterpret_cast<const uint32_t*>(&v);
             }
           } else {      // pk[j] = bf16 outputs (2j, 2j+1)
-            tmem_ld16(taddr + 32 * c, a);
-            tmem_ld16(taddr + 32 * c + 16, b);
+            tmem_ld32_issue(taddr + 64 * c, a);
+            tmem_ld32_issue(taddr + 64 * c + 32, b);
+            tmem_wait_ld2(a, b);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const __nv_bfloat162 v0 = __floats2bfloat162_rn(a[2 * i], a[2 * i + 1]);
-              const __nv_bfloat162 v1 = __floats2bfloat162_rn(b[2 * i], b[2 * i + 1]);
-              pk[16 * c + i] = *reinterpret_cast<const uint32_t*>(&v0);
-              pk[16 * c + 8 + i] = *reinterpret_cast<const uint32_t*>(&v1);
+            for (int i = 0; i < 16; ++i) {
+              const __nv_bfloat162 v0 =
+                  __floats2bfloat162_rn(__uint_as_float(a[2 * i]), __uint_as_float(a[2 * i + 1]));
+              const __nv_bfloat162 v1 =
+                  __floats2bfloat162_rn(__uint_as_float(b[2 * i]), __uint_as_float(b[2 * i + 1]));
+              pk[32 * c + i] = *reinterpret_cast<const uint32_t*>(&v0);
+              pk[32 * c + 16 + i] = *reinterpret_cast<const uint32_t*>(&v1);
             }
           }
         }

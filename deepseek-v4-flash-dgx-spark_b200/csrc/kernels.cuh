@@ -85,6 +85,13 @@ int launch_build_sf_fp8(const uint8_t* scale, int rows, int K, uint8_t* atoms, i
 int make_tmap_fp4_arena(CUtensorMap* m, const void* base, int K, int rows, int slots,
                         long long slot_stride, int l2_promotion);
 int make_tmap_u8(CUtensorMap* m, const void* base, int K, int rows, int box_rows);
+struct PairMaps;
+int make_tmap_atoms(CUtensorMap* m, const void* base, long long bytes, int box_rows);
+int pair_clusters_resident(bool gated);
+int launch_expert_gemm_pair(bool gated, const PairMaps& maps, const GemmArgs& args,
+                            long long sfs_row_off0, long long sfs_row_off1,
+                            long long sfw_row_off0, long long sfw_row_off1, int clusters,
+                            cudaStream_t st);
 int launch_expert_gemm(bool gated, int block_n, const CUtensorMap& a0, const CUtensorMap& a1,
                        const CUtensorMap& s0, const CUtensorMap& s1, const CUtensorMap& b,
                        const GemmArgs& args, int grid, cudaStream_t st);

@@ -7,6 +7,7 @@ logits.
 """
 
 import ctypes
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -224,7 +225,8 @@ def _oracle_weights(layer, experts):
     return mw
 
 
-@pytest.mark.parametrize("name,T", [("cpu_ref", 4), ("cpu_ref", 300), ("decode", 1), ("decode", 8)])
+@pytest.mark.parametrize("name,T", [("cpu_ref", 4), ("cpu_ref", 300), ("cpu_ref", 1000),
+                                    ("decode", 1), ("decode", 8)])
 def test_moe_layer(cuda_device, name, T):
     from spark_b200.synthetic import CONFIGS, build_moe, make_layer
 
@@ -454,3 +456,41 @@ def test_hash_layer_forward_matches_oracle(cuda_device):
     mw = _oracle_weights(layer, sorted(set(i_ref.reshape(-1).tolist())))
     y_ref = O.moe_forward(layer["x"].float().numpy(), mw, routing=(w_ref, i_ref))[0]
     assert _rel_err(_bf16_np(y.view(40, -1)), y_ref) <= TOL
+
+
+_PAIR_CHILD = r"""
+import sys, numpy as np, torch
+sys.path[:0] = [sys.argv[1], sys.argv[1] + "/deepseek-v4-flash-dgx-spark_b200"]
+from spark_b200.synthetic import CONFIGS, build_moe, make_layer
+cfg = CONFIGS["cpu_ref"].with_tokens(int(sys.argv[2]))
+layer = make_layer(cfg, seed=11, device="cpu")
+moe = build_moe(layer, device=torch.device("cuda", 0))
+y = moe.forward_tokens(layer["x"].cuda(), workspace=torch.empty(moe.workspace_bytes(cfg.tokens), dtype=torch.uint8, device="cuda"))
+torch.cuda.synchronize()
+from spark_b200 import _lib
+_lib.raise_on_device_error()
+np.save(sys.argv[3], y.view(torch.int16).cpu().numpy())
+"""
+
+
+@pytest.mark.parametrize("T", [600, 1000])
+def test_pair_gemm_bit_identical_to_single_cta_gemm(cuda_device, tmp_path, T):
+    """The CTA-pair grouped GEMM (256-row tiles, cta_group::2) and the
+    single-CTA GEMM (128-row tiles) compute every output row with the same
+    block-scaled products in the same k order: the layer outputs must be
+    bit-identical.  DSV4_BLOCK_N picks the tile size at library load, so each
+    form runs in its own process."""
+    import os
+    import subprocess
+    import sys
+
+    repo = str(Path(__file__).resolve().parent.parent)
+    outs = {}
+    for bn in ("256", "128"):
+        env = dict(os.environ, DSV4_BLOCK_N=bn)
+        f = tmp_path / f"y_{bn}.npy"
+        r = subprocess.run([sys.executable, "-c", _PAIR_CHILD, repo, str(T), str(f)], env=env,
+                           capture_output=True, text=True, timeout=600)
+        assert r.returncode == 0, r.stderr[-2000:]
+        outs[bn] = np.load(f)
+    assert np.array_equal(outs["256"], outs["128"])
