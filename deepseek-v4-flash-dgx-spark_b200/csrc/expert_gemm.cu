@@ -123,6 +123,70 @@ __device__ __forceinline__ ItemInfo decode_item(const GemmArgs& a, int w, int NB
   return it;
 }
 
+// TMA producer of the grouped expert GEMMs (one elected thread): per work
+// item and 128-wide k tile, the activation box, the two 128-row weight boxes
+// and, on the first k tile of each group of four, the group's scale atoms.
+template <class C, bool GATED>
+__device__ __forceinline__ void gemm_produce(const CUtensorMap* tmW0p, const CUtensorMap* tmW1p,
+                                             const CUtensorMap* tmS0p, const CUtensorMap* tmS1p,
+                                             const CUtensorMap* tmXp, const GemmArgs& args,
+                                             uint8_t* tile_base, uint8_t* sf_base, uint64_t* full,
+                                             uint64_t* empty, volatile int* abort_flag, int NB,
+                                             int KT, int KT4, int total, int step) {
+  int stage = 0;
+  uint32_t phase = 0;
+  int sf_slot = 1;  // ring slot of the current k-tile group (flips at each group)
+  ItemInfo cur, nxt;
+  if ((int)blockIdx.x < total) cur = decode_item<GATED>(args, blockIdx.x, NB, KT);
+  for (int w = blockIdx.x; w < total && !*abort_flag; w += step) {
+    // the next item's descriptor loads are issued now and used one item
+    // later, so their latency hides behind this item's k loop
+    if (w + step < total) nxt = decode_item<GATED>(args, w + step, NB, KT);
+    const size_t g0 = (size_t)(cur.row0 >> 5);
+    // transaction bytes count what the TMA reads from global memory: an e2m1
+    // box is 8 KB there even though it spreads to 16 KB (16U4_ALIGN16B) in smem
+    const uint32_t tx_base = C::A_BYTES + 2u * (cur.shared ? C::B_HALF : C::B_HALF / 2);
+    for (int kt = 0; kt < KT; ++kt) {
+      if (!mbar_wait(&empty[stage], phase ^ 1, DSV4_DEVERR_TIMEOUT_PRODUCER)) {
+        *abort_flag = 1;
+        break;
+      }
+      uint8_t* st = tile_base + (size_t)stage * C::TILE_BYTES;
+      // the first k tile of each group of four carries the group's scale atoms
+      const bool sf_tile = (kt & 3) == 0;
+      if (sf_tile) sf_slot ^= 1;
+      uint8_t* sf = sf_base + (size_t)sf_slot * C::SF_GROUP;
+      mbar_arrive_expect_tx(&full[stage], tx_base + (sf_tile ? 512u + 4096u : 0u));
+      tma_load_2d(st, tmXp, &full[stage], kt * 128, cur.row0);
+      uint8_t* b = st + C::A_BYTES;
+      if (cur.shared) {
+        tma_load_2d(b, tmS0p, &full[stage], kt * 128, cur.r0);
+        tma_load_2d(b + C::B_HALF, GATED ? tmS1p : tmS0p, &full[stage], kt * 128, cur.r1);
+      } else {
+        tma_load_3d(b, tmW0p, &full[stage], kt * 128, cur.r0, cur.slot);
+        tma_load_3d(b + C::B_HALF, GATED ? tmW1p : tmW0p, &full[stage], kt * 128, cur.r1,
+                    cur.slot);
+      }
+      if (sf_tile) {
+        bulk_load(sf, args.sfb + (g0 * KT4 + (kt >> 2)) * 512, 512, &full[stage]);
+        bulk_load(sf + 512, cur.sfb0 + (size_t)kt * 512, 2048, &full[stage]);
+        bulk_load(sf + 2560, cur.sfb1 + (size_t)kt * 512, 2048, &full[stage]);
+      }
+      if (++stage == C::STAGES) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+    cur = nxt;
+  }
+  if (*abort_flag) {
+    // let copies already in flight land before the CTA can exit
+    const uint64_t t0 = globaltimer();
+    while (globaltimer() - t0 < 10000000ull) {
+    }
+  }
+}
+
 template <int BM, bool GATED>
 __global__ void __launch_bounds__(192, 1)
     expert_gemm_kernel(const __grid_constant__ CUtensorMap tmW0,
@@ -180,60 +244,9 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      int sf_slot = 1;  // ring slot of the current k-tile group (flips at each group)
-      ItemInfo cur, nxt;
-      if ((int)blockIdx.x < total) cur = decode_item<GATED>(args, blockIdx.x, NB, KT);
-      for (int w = blockIdx.x; w < total && !*abort_flag; w += step) {
-        // the next item's descriptor loads are issued now and used one item
-        // later, so their latency hides behind this item's k loop
-        if (w + step < total) nxt = decode_item<GATED>(args, w + step, NB, KT);
-        const size_t g0 = (size_t)(cur.row0 >> 5);
-        // transaction bytes count what the TMA reads from global memory: an e2m1
-        // box is 8 KB there even though it spreads to 16 KB (16U4_ALIGN16B) in smem
-        const uint32_t tx_base = C::A_BYTES + 2u * (cur.shared ? C::B_HALF : C::B_HALF / 2);
-        for (int kt = 0; kt < KT; ++kt) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, DSV4_DEVERR_TIMEOUT_PRODUCER)) {
-            *abort_flag = 1;
-            break;
-          }
-          uint8_t* st = tile_base + (size_t)stage * C::TILE_BYTES;
-          // the first k tile of each group of four carries the group's scale atoms
-          const bool sf_tile = (kt & 3) == 0;
-          if (sf_tile) sf_slot ^= 1;
-          uint8_t* sf = sf_base + (size_t)sf_slot * C::SF_GROUP;
-          mbar_arrive_expect_tx(&full[stage], tx_base + (sf_tile ? 512u + 4096u : 0u));
-          tma_load_2d(st, &tmX, &full[stage], kt * 128, cur.row0);
-          uint8_t* b = st + C::A_BYTES;
-          if (cur.shared) {
-            tma_load_2d(b, &tmS0, &full[stage], kt * 128, cur.r0);
-            tma_load_2d(b + C::B_HALF, GATED ? &tmS1 : &tmS0, &full[stage], kt * 128, cur.r1);
-          } else {
-            tma_load_3d(b, &tmW0, &full[stage], kt * 128, cur.r0, cur.slot);
-            tma_load_3d(b + C::B_HALF, GATED ? &tmW1 : &tmW0, &full[stage], kt * 128, cur.r1,
-                        cur.slot);
-          }
-          if (sf_tile) {
-            bulk_load(sf, args.sfb + (g0 * KT4 + (kt >> 2)) * 512, 512, &full[stage]);
-            bulk_load(sf + 512, cur.sfb0 + (size_t)kt * 512, 2048, &full[stage]);
-            bulk_load(sf + 2560, cur.sfb1 + (size_t)kt * 512, 2048, &full[stage]);
-          }
-          if (++stage == C::STAGES) {
-            stage = 0;
-            phase ^= 1;
-          }
-        }
-        cur = nxt;
-      }
-      if (*abort_flag) {
-        // let copies already in flight land before the CTA can exit
-        const uint64_t t0 = globaltimer();
-        while (globaltimer() - t0 < 10000000ull) {
-        }
-      }
-    }
+    if (lane == 0)
+      gemm_produce<C, GATED>(&tmW0, &tmW1, &tmS0, &tmS1, &tmX, args, tile_base, sf_base, full, empty,
+                             abort_flag, NB, KT, KT4, total, step);
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {

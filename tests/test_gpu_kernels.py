@@ -458,19 +458,36 @@ def test_hash_layer_forward_matches_oracle(cuda_device):
     assert _rel_err(_bf16_np(y.view(40, -1)), y_ref) <= TOL
 
 
-_PAIR_CHILD = r"""
+_CHILD = r"""
 import sys, numpy as np, torch
 sys.path[:0] = [sys.argv[1], sys.argv[1] + "/deepseek-v4-flash-dgx-spark_b200"]
 from spark_b200.synthetic import CONFIGS, build_moe, make_layer
-cfg = CONFIGS["cpu_ref"].with_tokens(int(sys.argv[2]))
+cfg = CONFIGS[sys.argv[2]].with_tokens(int(sys.argv[3]))
 layer = make_layer(cfg, seed=11, device="cpu")
 moe = build_moe(layer, device=torch.device("cuda", 0))
 y = moe.forward_tokens(layer["x"].cuda(), workspace=torch.empty(moe.workspace_bytes(cfg.tokens), dtype=torch.uint8, device="cuda"))
 torch.cuda.synchronize()
 from spark_b200 import _lib
 _lib.raise_on_device_error()
-np.save(sys.argv[3], y.view(torch.int16).cpu().numpy())
+np.save(sys.argv[4], y.view(torch.int16).cpu().numpy())
 """
+
+
+def _layer_bits_under_env(tmp_path, cfg_name, T, env_sets):
+    import os
+    import subprocess
+    import sys
+
+    repo = str(Path(__file__).resolve().parent.parent)
+    outs = []
+    for i, extra in enumerate(env_sets):
+        env = dict(os.environ, **extra)
+        f = tmp_path / f"y_{i}.npy"
+        r = subprocess.run([sys.executable, "-c", _CHILD, repo, cfg_name, str(T), str(f)], env=env,
+                           capture_output=True, text=True, timeout=600)
+        assert r.returncode == 0, r.stderr[-2000:]
+        outs.append(np.load(f))
+    return outs
 
 
 @pytest.mark.parametrize("T", [600, 1000])
@@ -480,17 +497,5 @@ def test_pair_gemm_bit_identical_to_single_cta_gemm(cuda_device, tmp_path, T):
     block-scaled products in the same k order: the layer outputs must be
     bit-identical.  DSV4_BLOCK_N picks the tile size at library load, so each
     form runs in its own process."""
-    import os
-    import subprocess
-    import sys
-
-    repo = str(Path(__file__).resolve().parent.parent)
-    outs = {}
-    for bn in ("256", "128"):
-        env = dict(os.environ, DSV4_BLOCK_N=bn)
-        f = tmp_path / f"y_{bn}.npy"
-        r = subprocess.run([sys.executable, "-c", _PAIR_CHILD, repo, str(T), str(f)], env=env,
-                           capture_output=True, text=True, timeout=600)
-        assert r.returncode == 0, r.stderr[-2000:]
-        outs[bn] = np.load(f)
-    assert np.array_equal(outs["256"], outs["128"])
+    a, b = _layer_bits_under_env(tmp_path, "cpu_ref", T, [{"DSV4_BLOCK_N": "256"}, {"DSV4_BLOCK_N": "128"}])
+    assert np.array_equal(a, b)
