@@ -74,7 +74,7 @@ def _weights():
 
 
 def _tokens(cfg, rank, case):
-    n = {"balanced": (5, 7), "empty_rank": (6, 0), "one_sided": (4, 3)}[case][rank]
+    n = {"balanced": (5, 7, 3, 6), "empty_rank": (6, 0), "one_sided": (4, 3, 2, 5)}[case][rank]
     g = torch.Generator().manual_seed(100 + rank)
     return torch.randn(n, cfg.dim, generator=g).to(torch.bfloat16)
 
@@ -111,9 +111,9 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("case", ["balanced", "empty_rank", "one_sided"])
-def test_ep_forward_two_gloo_ranks_matches_single_device(case):
-    world = 2
+@pytest.mark.parametrize("case,world", [("balanced", 2), ("empty_rank", 2), ("one_sided", 2),
+                                        ("balanced", 4), ("one_sided", 4)])
+def test_ep_forward_gloo_ranks_matches_single_device(case, world):
     ctx = mp.get_context("spawn")
     with ctx.Manager() as mgr:
         results = mgr.dict()
