@@ -658,6 +658,10 @@ int dsv4_materialize(const uint8_t* slab, const long long* src_off, const int* d
   if (arena && slot_stride < block) return DSV4_ERR_ARG;
   if (arena_sf && sf_slot_stride < 3LL * inter * hidden / 32) return DSV4_ERR_ARG;
   if (arena && slot_stride % 16) return DSV4_ERR_ARG;
+  // 16-byte vector loads and stores throughout
+  if ((reinterpret_cast<uintptr_t>(slab) & 15) || (reinterpret_cast<uintptr_t>(arena) & 15) ||
+      (reinterpret_cast<uintptr_t>(bf16_out) & 15) || (bf16_out && bf16_slot_stride % 8))
+    return DSV4_ERR_ARG;
   bind_device(slab);
   return launch_materialize(slab, src_off, dst_slot, n, block, arena, slot_stride, hidden, inter,
                             arena_sf, sf_slot_stride, bf16_out, bf16_slot_stride, num_sms(),

@@ -15,7 +15,8 @@ namespace dsv4 {
 
 // 16-byte vector copy of n blocks, block i from slab + src_off[i] to
 // arena + dst_slot[i] * slot_stride.  HBM-bound: grid-stride over 16-byte
-// chunks of the concatenated blocks.
+// chunks of the concatenated blocks.  A block whose source offset is not
+// 16-byte aligned is skipped and latches DSV4_DEVERR_MISALIGNED.
 __global__ void __launch_bounds__(256) materialize_copy_kernel(
     const uint8_t* __restrict__ slab, const long long* __restrict__ src_off,
     const int* __restrict__ dst_slot, int n, long long block_bytes, uint8_t* __restrict__ arena,
@@ -26,7 +27,12 @@ __global__ void __launch_bounds__(256) materialize_copy_kernel(
        c += (long long)gridDim.x * blockDim.x) {
     const int b = (int)(c / chunks_per_block);
     const long long o = (c - (long long)b * chunks_per_block) << 4;
-    const uint4 v = __ldcs(reinterpret_cast<const uint4*>(slab + src_off[b] + o));
+    const long long so = src_off[b];
+    if (so & 15) {
+      if (o == 0) record_error(DSV4_DEVERR_MISALIGNED);
+      continue;
+    }
+    const uint4 v = __ldcs(reinterpret_cast<const uint4*>(slab + so + o));
     __stcs(reinterpret_cast<uint4*>(arena + (long long)dst_slot[b] * slot_stride + o), v);
   }
 }
@@ -88,43 +94,93 @@ __global__ void __launch_bounds__(256) build_sf_fp8_kernel(const uint8_t* __rest
   }
 }
 
+constexpr int kDecodeGroupsPerThread = 8;
+
+// bf16 bits of the two e2m1 codes of byte v (low nibble first) at scale 1.
+__device__ __forceinline__ uint32_t e2m1_pair_bf16_bits(uint32_t v) {
+  uint32_t out = 0;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t c = (v >> (4 * h)) & 0xF, mag = c & 7, e2 = mag >> 1;
+    // 0.5 = 2^-1 (exponent field 126); otherwise (1 + m/2) * 2^(e2-1)
+    const uint32_t bits = mag == 0 ? 0u : (e2 == 0 ? (126u << 7) : (((126u + e2) << 7) | ((mag & 1) << 6)));
+    out |= (bits | ((c & 8) << 12)) << (16 * h);
+  }
+  return out;
+}
+
 // Exact bf16 decode of the three fp4 weights of n experts:
 // out + dst_slot[i] * out_slot_stride + {w1, w2, w3} as [rows, K] bf16.
+// blockIdx.y = expert * 3 + weight (packed order w1, w2, w3).  One thread
+// decodes one ue8m0 scale group: 32 codes (16 bytes, coalesced), one scale
+// byte, 64 bytes of bf16 out.  e2m1 x 2^(s-127) is exact in bf16; for
+// 16 <= s <= 239 every nonzero result is a normal bf16, so the product is the
+// scale-1 bit pattern (a 256-entry byte -> bf16x2 table) with s - 127 added to
+// both exponent fields; other scale bytes take the float path.
 __global__ void __launch_bounds__(256) decode_bf16_kernel(
     const uint8_t* __restrict__ src, const long long* __restrict__ src_off,
-    const int* __restrict__ dst_slot, int n, int hidden, int inter,
-    __nv_bfloat16* __restrict__ out, long long out_slot_stride) {
+    const int* __restrict__ dst_slot, int hidden, int inter, __nv_bfloat16* __restrict__ out,
+    long long out_slot_stride) {
+  __shared__ uint32_t lut[256];
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = e2m1_pair_bf16_bits(i);
+  __syncthreads();
+  const int b = blockIdx.y / 3, wsel = blockIdx.y % 3;
   const long long w_elems = (long long)inter * hidden;
-  const long long scale_bytes = w_elems / 32;
-  const long long per_expert = 3 * w_elems / 8;  // 8-element groups
-  const long long total = per_expert * n;
-  for (long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x; g < total;
-       g += (long long)gridDim.x * blockDim.x) {
-    const int b = (int)(g / per_expert);
-    long long e8 = g - (long long)b * per_expert;
-    const int wsel = (int)(e8 / (w_elems / 8));  // 0 = w1, 1 = w2, 2 = w3 (packed order)
-    e8 -= (long long)wsel * (w_elems / 8);
-    const int K = wsel == 1 ? inter : hidden;
-    const long long elem = e8 * 8;
-    const long long row = elem / K;
-    const int k = (int)(elem % K);
-    const uint8_t* blk = src + src_off[b];
-    const uint8_t* scale = blk + (long long)wsel * scale_bytes;
-    const uint8_t* wgt = blk + 3 * scale_bytes + (long long)wsel * (w_elems / 2);
-    const float sc = exp2i((int)scale[row * (K / 32) + k / 32] - 127);
-    const uint32_t codes = *reinterpret_cast<const uint32_t*>(wgt + row * (K / 2) + k / 2);
-    uint4 o;
-    __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&o);
+  const long long groups = w_elems / 32;  // scale groups of one weight (= its scale bytes)
+  if (src_off[b] & 15) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) record_error(DSV4_DEVERR_MISALIGNED);
+    return;
+  }
+  const uint8_t* blk = src + src_off[b];
+  const uint8_t* scale = blk + (long long)wsel * groups;
+  const uint4* codes = reinterpret_cast<const uint4*>(blk + 3 * groups + (long long)wsel * (w_elems / 2));
+  uint4* o = reinterpret_cast<uint4*>(out + (long long)dst_slot[b] * out_slot_stride +
+                                      (long long)wsel * w_elems);
+  // short CTAs (kDecodeGroupsPerThread strided groups per thread) so the many
+  // CTAs of a launch balance over the SMs without a long partial last wave
+#pragma unroll 2
+  for (int j = 0; j < kDecodeGroupsPerThread; ++j) {
+    const long long g = ((long long)blockIdx.x * kDecodeGroupsPerThread + j) * blockDim.x + threadIdx.x;
+    if (g >= groups) break;
+    const int s = __ldcs(scale + g);
+    const uint4 c4 = __ldcs(codes + g);
+    const uint32_t cw[4] = {c4.x, c4.y, c4.z, c4.w};
+    if (s >= 16 && s <= 239) {
+      const uint32_t d = (uint32_t)((s - 127) << 7) & 0xFFFFu;
+      const uint32_t dpair = d | (d << 16);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t c = (codes >> (4 * i)) & 0xF;
-      // e2m1: exponent bits 2..1, mantissa bit 0; subnormal when exponent = 0
-      const uint32_t ex = (c >> 1) & 3, m = c & 1;
-      const float mag = ex == 0 ? 0.5f * (float)m : exp2i((int)ex - 1) * (1.0f + 0.5f * (float)m);
-      ob[i] = __float2bfloat16_rn((c & 8) ? -mag * sc : mag * sc);
+      for (int q = 0; q < 4; ++q) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t x = lut[(cw[q] >> (8 * i)) & 0xFF];
+          const uint32_t nz = __vcmpne2(x & 0x7FFF7FFFu, 0u);  // +-0 keeps its exponent
+          pk[i] = __vadd2(x, dpair & nz);
+        }
+        __stcs(o + 4 * g + q, make_uint4(pk[0], pk[1], pk[2], pk[3]));
+      }
+    } else {
+      const float sc = exp2i(s - 127);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float v[2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t c = (cw[q] >> (8 * i + 4 * h)) & 0xF;
+            // e2m1: exponent bits 2..1, mantissa bit 0; subnormal when exponent = 0
+            const uint32_t ex = (c >> 1) & 3, m = c & 1;
+            const float mag = ex == 0 ? 0.5f * (float)m : exp2i((int)ex - 1) * (1.0f + 0.5f * (float)m);
+            v[h] = (c & 8) ? -mag * sc : mag * sc;
+          }
+          const __nv_bfloat162 p = __floats2bfloat162_rn(v[0], v[1]);
+          pk[i] = *reinterpret_cast<const uint32_t*>(&p);
+        }
+        __stcs(o + 4 * g + q, make_uint4(pk[0], pk[1], pk[2], pk[3]));
+      }
     }
-    *reinterpret_cast<uint4*>(out + (long long)dst_slot[b] * out_slot_stride +
-                              (long long)wsel * w_elems + elem) = o;
   }
 }
 
@@ -154,11 +210,13 @@ int launch_materialize(const uint8_t* slab, const long long* src_off, const int*
                                                                  sf_slot_stride);
   }
   if (bf16_out) {
-    const long long groups = 3LL * inter * hidden / 8 * n;
+    if (3LL * n > 65535) return DSV4_ERR_UNSUPPORTED;
+    const long long per_cta = 256LL * kDecodeGroupsPerThread;
+    const dim3 grid((unsigned)(((long long)inter * hidden / 32 + per_cta - 1) / per_cta), 3 * n);
     count_launch();
-    decode_bf16_kernel<<<grid_for(groups, num_sms), 256, 0, st>>>(
-        slab, src_off, dst_slot, n, hidden, inter, static_cast<__nv_bfloat16*>(bf16_out),
-        bf16_slot_stride);
+    decode_bf16_kernel<<<grid, 256, 0, st>>>(slab, src_off, dst_slot, hidden, inter,
+                                             static_cast<__nv_bfloat16*>(bf16_out),
+                                             bf16_slot_stride);
   }
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }

@@ -41,6 +41,7 @@ DEVERR_NAMES = {
     103: "epilogue wait timed out",
     104: "expert index out of range",
     105: "routing plan exceeds its workspace",
+    106: "materializer source offset not 16-byte aligned",
 }
 
 

@@ -48,6 +48,7 @@ extern "C" {
 #define DSV4_DEVERR_TIMEOUT_EPILOGUE 103
 #define DSV4_DEVERR_BAD_INDEX 104
 #define DSV4_DEVERR_PLAN_OVERFLOW 105
+#define DSV4_DEVERR_MISALIGNED 106  /* a materializer source offset is not 16-byte aligned */
 
 DSV4_API int dsv4_version(void);
 /* Number of kernels the library has enqueued in this process (every launch
@@ -201,7 +202,8 @@ DSV4_API int dsv4_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* sc
  * arena_sf, and (if bf16_out != NULL) their weights decoded exactly to bf16
  * ([I,H], [H,I], [I,H] in packed order w1, w2, w3 per slot).  Any of arena,
  * arena_sf, bf16_out may be NULL to skip that output.  src_off (int64) and
- * dst_slot (int32) are device arrays of length n; src_off % 16 == 0. */
+ * dst_slot (int32) are device arrays of length n; src_off % 16 == 0 (a block
+ * whose offset is not is skipped and latches DSV4_DEVERR_MISALIGNED). */
 DSV4_API int dsv4_materialize(const uint8_t* slab, const long long* src_off, const int* dst_slot, int n,
                      int hidden, int inter, uint8_t* arena, long long slot_stride,
                      uint8_t* arena_sf, long long sf_slot_stride, void* bf16_out,

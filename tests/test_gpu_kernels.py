@@ -187,6 +187,31 @@ def test_materialize_bit_exact(cuda_device):
         assert np.array_equal(bfn[s], ref_bf)
 
 
+def test_materialize_misaligned_offset_is_reported_not_loaded(cuda_device):
+    """A source offset that is not 16-byte aligned is skipped by the vector
+    copy / decode kernels and latched as DSV4_DEVERR_MISALIGNED; the slot keeps
+    its previous bytes and no misaligned load is issued."""
+    from spark_b200.moe import ExpertArena, packed_block_bytes
+    from spark_b200.synthetic import routed_blocks
+
+    H, I = 1024, 512
+    nb = packed_block_bytes(H, I)
+    blocks = routed_blocks(1, H, I, 3)
+    slab = torch.zeros(nb + 64, dtype=torch.uint8, device=cuda_device)
+    slab[8:8 + nb].copy_(blocks[0].to(cuda_device))
+    arena = ExpertArena(2, H, I, device=cuda_device)
+    arena.buffer.fill_(0x5A)
+    bf16 = torch.zeros(2, 3 * H * I, dtype=torch.bfloat16, device=cuda_device)
+    arena.materialize(slab, [8], [1], bf16_out=bf16)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="16-byte aligned"):
+        _no_device_error()
+    s = arena.slot_stride
+    assert bool((arena.buffer[s:s + nb] == 0x5A).all())
+    assert bool((bf16[1] == 0).all())
+    _no_device_error()  # the flag was read and cleared
+
+
 def test_shared_scale_atoms(cuda_device):
     from spark_b200.moe import Expert
     from spark_b200.synthetic import shared_expert
