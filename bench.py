@@ -54,6 +54,8 @@ def _parse():
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                   help="expert-parallel exchange (N>1): NVLink peer memory from the kernels, or NCCL all-to-all")
     p.add_argument("--experts", type=int, default=None,
                    help="routed experts per layer (default: the workload's 256); profiling runs use fewer")
     return p.parse_args()
@@ -343,6 +345,8 @@ def run_ours_ep(args, world, rank, local):
     x = torch.randn(T, cfg.dim, generator=g, device=dev).to(torch.bfloat16)
     lib = _lib.load()
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    if args.exchange == "peer":
+        moe.enable_peer_exchange(T)  # collective: every rank, same capacity
 
     for _ in range(max(args.warmup, 3)):
         y = ep_moe_forward(moe, x)
@@ -444,18 +448,28 @@ def run_ours_ep(args, world, rank, local):
                    "routing": "uniform" if cfg.bias == "zero" else "zipf1.2",
                    "experts_touched": global_touched, "rank0_experts_touched": touched,
                    "rank0_routes": local_routes, "l2": "flushed (256 MB write) between steps",
-                   "parallelism": f"ep{world}", "exchange": "NCCL all-to-all: FP8 rows "
-                   f"({rb} B per token and owning rank), bf16 route outputs ({2 * H} B per route)",
+                   "parallelism": f"ep{world}", "exchange": (
+                       "NVLink peer memory: the pack kernel stores FP8 rows into the owners' buffers, the "
+                       "return kernel stores bf16 route rows into the sources' (epoch flags, no host sync)"
+                       if args.exchange == "peer" else "NCCL all-to-all") +
+                   f"; {rb} B per token and owning rank, {2 * H} B per route",
                    "cuda_graph": False},
         "stage_ms_rank0": dict(zip(["unpack", "plan", "scatter", "gemm1", "gemm2", "return_gather"],
                                    [round(v, 5) for v in stage_ms])),
         "roofline": roof,
         "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 2), "unit": UNIT,
                 "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": y.numel() * 2,
-                "ms_per_step": round(e2e_ms, 5), "path": "MoE.forward -> spark_b200.ep (C ABI + NCCL)"},
+                "ms_per_step": round(e2e_ms, 5),
+                "path": "MoE.forward -> spark_b200.ep (C ABI, " +
+                        ("NVLink peer memory)" if args.exchange == "peer" else "NCCL)")},
         "clocks": clk,
         "gpu_launches": launches_per_step * args.steps,
     }
+    if getattr(moe, "peer_exchange", None) is not None:
+        torch.cuda.synchronize()
+        dist.barrier()  # no rank frees its buffer while a peer could still store into it
+        moe.peer_exchange.close()
+        moe.peer_exchange = None
     return result, cfg, layer, moe
 
 

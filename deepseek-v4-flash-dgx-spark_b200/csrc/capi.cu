@@ -1,6 +1,7 @@
 // extern "C" entry points of libdsv4moe.so (declared in include/dsv4moe.h).
 #include <stdio.h>
 #include <stdlib.h>
+#include <string.h>
 
 #include "kernels.cuh"
 
@@ -803,6 +804,201 @@ int dsv4_ep_expert_forward(const dsv4_moe_layer* L, int rank, int world, const v
   rc = launch_ep_return_gather(O, H, route_slot, ret_dst, T * k, ret_rows, ret_send, nsm, st);
   stage_mark(6, st);
   return rc;
+}
+
+// ---------------------------------------------------------------------------
+// expert parallelism over peer memory (NVLink P2P stores, bounded flag waits)
+// ---------------------------------------------------------------------------
+long long dsv4_ep_exchange_bytes(int hidden, int topk, int world, int cap_tokens) {
+  if (hidden <= 0 || hidden % 512 || topk <= 0 || topk > 8 || world <= 0 || world > 8 ||
+      cap_tokens <= 0 || (long long)cap_tokens * topk >= (1 << 24))
+    return -1;
+  return ep_exchange_bytes(hidden, topk, world, cap_tokens);
+}
+
+int dsv4_ep_exchange_alloc(int device, long long bytes, void** out) {
+  if (!out || bytes <= 0 || device < 0) return DSV4_ERR_ARG;
+  *out = nullptr;
+  if (cudaSetDevice(device) != cudaSuccess) return DSV4_ERR_CUDA;
+  void* p = nullptr;
+  if (cudaMalloc(&p, (size_t)bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return DSV4_ERR_CUDA;
+  }
+  if (cudaMemset(p, 0, (size_t)bytes) != cudaSuccess) {
+    cudaFree(p);
+    return DSV4_ERR_CUDA;
+  }
+  *out = p;
+  return DSV4_OK;
+}
+
+int dsv4_ep_exchange_free(void* p) {
+  if (!p) return DSV4_OK;
+  bind_device(p);
+  return cudaFree(p) == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
+}
+
+int dsv4_ipc_handle(const void* p, uint8_t* handle) {
+  if (!p || !handle) return DSV4_ERR_ARG;
+  bind_device(p);
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, const_cast<void*>(p)) != cudaSuccess) {
+    cudaGetLastError();
+    return DSV4_ERR_CUDA;
+  }
+  static_assert(sizeof(h) == DSV4_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  return DSV4_OK;
+}
+
+int dsv4_ipc_open(int device, const uint8_t* handle, void** out) {
+  if (!handle || !out || device < 0) return DSV4_ERR_ARG;
+  *out = nullptr;
+  if (cudaSetDevice(device) != cudaSuccess) return DSV4_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    cudaGetLastError();
+    return DSV4_ERR_CUDA;
+  }
+  *out = p;
+  return DSV4_OK;
+}
+
+int dsv4_ipc_close(void* p) {
+  if (!p) return DSV4_OK;
+  return cudaIpcCloseMemHandle(p) == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
+}
+
+long long dsv4_ep_p2p_dispatch_workspace_bytes(int T, int world) {
+  if (T < 0 || world <= 0 || world > 8) return -1;
+  return ep_dispatch_workspace(T, world) + 256;
+}
+
+int dsv4_ep_dispatch_p2p(const void* x, const int64_t* indices, const float* weights, int T,
+                         int hidden, int topk, int n_routed, int world, int rank,
+                         const uint64_t* peer_bases, int cap_tokens, int epoch, int* ret_pos,
+                         void* workspace, long long workspace_bytes, void* stream) {
+  if (world <= 0 || world > 8 || rank < 0 || rank >= world || n_routed % world || hidden % 512 ||
+      topk <= 0 || topk > 8 || !peer_bases || cap_tokens <= 0 || T < 0 || T > cap_tokens)
+    return DSV4_ERR_ARG;
+  if (T && (!x || !indices || !weights || !ret_pos)) return DSV4_ERR_ARG;
+  const long long need = ep_dispatch_workspace(T, world) + 256;
+  if (!workspace || workspace_bytes < need) return DSV4_ERR_WORKSPACE;
+  bind_device(workspace);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* send_counts = reinterpret_cast<int*>(ws + ep_dispatch_workspace(T, world));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (T == 0)  // no rows, but every owner still learns that nothing comes from this rank
+    return launch_ep_signal_empty(peer_bases, rank, world, send_counts, ws, epoch, st);
+  return launch_ep_dispatch(x, indices, weights, T, hidden, topk, n_routed, world, nullptr,
+                            send_counts, ret_pos, ws, num_sms(), st, peer_bases, rank, cap_tokens,
+                            epoch);
+}
+
+long long dsv4_ep_p2p_expert_workspace_bytes(const dsv4_moe_layer* L, int world, int T_own,
+                                             int cap_tokens) {
+  if (ep_check(L, 0, world) || T_own < 0 || cap_tokens <= 0) return -1;
+  return make_plan(L, T_own + world * cap_tokens, L->n_routed / world).total;
+}
+
+int dsv4_ep_expert_forward_p2p(const dsv4_moe_layer* L, int rank, int world, const void* x_own,
+                               int T_own, void* exchange, const uint64_t* peer_bases,
+                               int cap_tokens, int epoch, void* workspace,
+                               long long workspace_bytes, void* stream) {
+  int rc = ep_check(L, rank, world);
+  if (rc) return rc;
+  if (T_own < 0 || T_own > cap_tokens || (T_own && !x_own) || !exchange || !peer_bases ||
+      cap_tokens <= 0)
+    return DSV4_ERR_ARG;
+  if (!L->arena || !L->arena_sf || !L->expert_slot || L->slot_stride % 32 || L->n_slots <= 0)
+    return DSV4_ERR_ARG;
+  if (L->n_shared && (!L->shared_w1 || !L->shared_w2 || !L->shared_w3 || !L->shared_sf))
+    return DSV4_ERR_ARG;
+  const int T = T_own + world * cap_tokens;
+  const int e_count = L->n_routed / world, e_begin = rank * e_count;
+  const Plan p = make_plan(L, T, e_count);
+  if (!workspace || workspace_bytes < p.total) return DSV4_ERR_WORKSPACE;
+  bind_device(workspace);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* ret_dst = reinterpret_cast<int*>(ws + p.off[0]);
+  float* w_local = reinterpret_cast<float*>(ws + p.off[1]);
+  int64_t* idx_local = reinterpret_cast<int64_t*>(ws + p.off[2]);
+  int* counts = reinterpret_cast<int*>(ws + p.off[3]);
+  int* seg_start = reinterpret_cast<int*>(ws + p.off[4]);
+  int* n_tiles = reinterpret_cast<int*>(ws + p.off[5]);
+  int* route_slot = reinterpret_cast<int*>(ws + p.off[6]);
+  int* slot_token = reinterpret_cast<int*>(ws + p.off[7]);
+  float* slot_weight = reinterpret_cast<float*>(ws + p.off[8]);
+  int4* tiles = reinterpret_cast<int4*>(ws + p.off[9]);
+  uint8_t* xq = ws + p.off[10];
+  uint8_t* xsf = ws + p.off[11];
+  uint8_t* hq = ws + p.off[12];
+  uint8_t* hsf = ws + p.off[13];
+  __nv_bfloat16* O = reinterpret_cast<__nv_bfloat16*>(ws + p.off[14]);
+  int* chunk_cnt = reinterpret_cast<int*>(ws + p.off[16]);
+  int* chunk_base = reinterpret_cast<int*>(ws + p.off[17]);
+  int* ctrl = reinterpret_cast<int*>(ws + p.off[18]);
+  const int nsm = num_sms();
+  const int H = p.H, k = p.k;
+  const int shared_rows = p.S ? T_own : 0;
+  uint8_t* exch = static_cast<uint8_t*>(exchange);
+  stage_mark(0, st);
+  // every source's rows and counts are in place
+  if ((rc = launch_ep_wait(reinterpret_cast<const int*>(exch), world, epoch,
+                           DSV4_DEVERR_TIMEOUT_PEER, st)))
+    return rc;
+  if ((rc = launch_ep_unpack_p2p(exch, cap_tokens, T_own, k, H, e_begin, e_count, world,
+                                 idx_local, w_local, ret_dst, st)))
+    return rc;
+  stage_mark(1, st);
+  if ((rc = launch_route_plan(idx_local, T, k, e_count, 1, shared_rows, p.block_n, p.max_rows,
+                              p.max_tiles, chunk_cnt, chunk_base, ctrl, counts, seg_start, tiles,
+                              n_tiles, slot_token, slot_weight, st)))
+    return rc;
+  stage_mark(2, st);
+  if ((rc = launch_route_scatter(x_own, T_own, exch + kEpHeaderBytes, ep_row_bytes(H, k), idx_local,
+                                 w_local, T, k, e_count, H, shared_rows, seg_start, chunk_base,
+                                 ctrl, route_slot, slot_token, slot_weight, xq, xsf, nsm, st)))
+    return rc;
+  stage_mark(3, st);
+  if ((rc = run_expert_gemms(L, tiles, n_tiles, slot_weight, xq, xsf, hq, hsf, O, H, p.max_rows,
+                             p.max_tiles, p.block_n, L->expert_slot + e_begin, e_count, nsm, st)))
+    return rc;
+  rc = launch_ep_return_p2p(O, H, k, route_slot, ret_dst, T * k, peer_bases, rank, world,
+                            cap_tokens, epoch, nsm, st);
+  stage_mark(6, st);
+  return rc;
+}
+
+int dsv4_ep_combine_p2p(const dsv4_moe_layer* L, int rank, int world, const void* exchange,
+                        const int* ret_pos, const int64_t* indices, int T_own, int cap_tokens,
+                        int epoch, const void* workspace, long long workspace_bytes, void* y,
+                        void* stream) {
+  int rc = ep_check(L, rank, world);
+  if (rc) return rc;
+  if (T_own < 0 || T_own > cap_tokens || !exchange) return DSV4_ERR_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uint8_t* exch = static_cast<const uint8_t*>(exchange);
+  bind_device(exchange);
+  // every owner's return rows are in place (waited for even with no tokens, so
+  // the flags of this epoch are consumed in order)
+  if ((rc = launch_ep_wait(reinterpret_cast<const int*>(exch + kEpRetFlagOff), world, epoch,
+                           DSV4_DEVERR_TIMEOUT_PEER, st)))
+    return rc;
+  if (T_own == 0) return DSV4_OK;
+  if (!ret_pos || !indices || !y || !workspace) return DSV4_ERR_ARG;
+  const int e_count = L->n_routed / world;
+  const Plan p = make_plan(L, T_own + world * cap_tokens, e_count);
+  if (workspace_bytes < p.total) return DSV4_ERR_WORKSPACE;
+  const uint8_t* ws = static_cast<const uint8_t*>(workspace);
+  const int* seg_start = reinterpret_cast<const int*>(ws + p.off[4]);
+  const void* O = ws + p.off[14];
+  return launch_combine(exch + ep_return_region_off(p.H, p.k, world, cap_tokens), p.H, ret_pos,
+                        indices, T_own, p.k, p.S ? seg_start + e_count : nullptr, y, st, O);
 }
 
 int dsv4_ep_combine(const dsv4_moe_layer* L, int rank, int world, const void* ret_recv,

@@ -272,10 +272,10 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint
 }
 
 // ---------------------------------------------------------------------------
-// CTA pairs (cluster of 2) for cta_group::2 tensor-core work.  No TMA load in
-// this library uses .multicast::cluster; a pair's loads each fill the issuing
-// CTA's own shared memory and only their completion is reported to the
-// leader CTA's mbarrier.
+// CTA pairs (cluster of 2) for cta_group::2 tensor-core work.  Every load of
+// a pair fills the issuing CTA's own shared memory; only its completion is
+// reported to the leader CTA's mbarrier.  The one cluster-wide broadcast is
+// the MMA completion signal (tcgen05.commit to both CTAs' barriers).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

@@ -38,7 +38,37 @@ constexpr int kEpChunk = 256;  // tokens per dispatch chunk (8 warps, one token 
 constexpr int kEpMaxWorld = 8;
 constexpr int kEpMetaEntry = 12;
 
+// Exchange buffer of one rank (peer-memory expert parallelism), all offsets in
+// bytes from its base:
+//   [0, 32)        int32 disp_flag[8]: = epoch once source s's rows (and its
+//                  info below) are in place
+//   [32, 64)       int32 ret_flag[8]: = epoch once owner r's return rows are in place
+//   [64, 192)      int32 info[8][4] per source s: rows, routes, offset of its
+//                  return block from this rank in s's return region, unused
+//   [1024, ...)    receive region: source s's rows at s * cap_tokens rows
+//   then           return region: this rank's routes' bf16 output rows
+//                  (cap_tokens * topk rows of H), in owner-rank blocks
+constexpr int kEpHeaderBytes = 1024;
+constexpr int kEpRetFlagOff = 32;
+constexpr int kEpInfoOff = 64;
+
 long long ep_row_bytes(int H, int k) { return ((long long)H + H / 128 + (long long)kEpMetaEntry * k + 15) / 16 * 16; }
+
+// Where the send row `pos` for destination rank d lives.  Exchanged through
+// host collectives (bases == nullptr): row pos of the local send buffer.  Over
+// peer memory: row (pos - dst_base[2d]) of this rank's region in rank d's
+// exchange buffer (bases[d] = that buffer as mapped here, IPC for peers).
+struct EpPeerRows {
+  const uint64_t* bases;  // [world] exchange buffer base of every rank, or nullptr
+  int rank;               // this (source) rank
+  long long cap_bytes;    // one source region: cap_tokens * row_bytes
+  __device__ __forceinline__ uint8_t* row(uint8_t* send, int d, int pos, const int* dst_base,
+                                          long long row_bytes) const {
+    if (!bases) return send + (size_t)pos * row_bytes;
+    return reinterpret_cast<uint8_t*>(bases[d]) + kEpHeaderBytes + (long long)rank * cap_bytes +
+           (long long)(pos - dst_base[2 * d]) * row_bytes;
+  }
+};
 
 __device__ __forceinline__ int warp_excl_scan(int v, int lane, int* total) {
   int inc = v;
@@ -144,7 +174,7 @@ __global__ void __launch_bounds__(kEpChunk) ep_plan_kernel(
     const int64_t* __restrict__ indices, const float* __restrict__ weights, int T, int k, int E,
     int world, int H, long long row_bytes, int nchunks, const int* __restrict__ cb,
     const int* __restrict__ dst_base, int* __restrict__ row_pos, uint8_t* __restrict__ send,
-    int* __restrict__ ret_pos, int* __restrict__ ctrl) {
+    int* __restrict__ ret_pos, int* __restrict__ ctrl, EpPeerRows peer) {
   __shared__ int s_part[kEpChunk / 32][2 * kEpMaxWorld];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, c = blockIdx.x;
   const int t = c * kEpChunk + tid;
@@ -187,7 +217,7 @@ __global__ void __launch_bounds__(kEpChunk) ep_plan_kernel(
       pos = dst_base[2 * d] + cb[(size_t)(2 * d) * nchunks + c] + wrow + rrank[d];
       // route index inside the return block from rank d
       int ridx = cb[(size_t)(2 * d + 1) * nchunks + c] + wroute + rbase[d];
-      uint8_t* meta = send + (size_t)pos * row_bytes + meta_off;
+      uint8_t* meta = peer.row(send, d, pos, dst_base, row_bytes) + meta_off;
 #pragma unroll
       for (int j = 0; j < kMaxK; ++j) {
         if (j >= k) break;
@@ -213,7 +243,9 @@ __global__ void __launch_bounds__(kEpChunk) ep_plan_kernel(
 __global__ void __launch_bounds__(256) ep_pack_kernel(const __nv_bfloat16* __restrict__ x, int T,
                                                       int H, int world, long long row_bytes,
                                                       const int* __restrict__ row_pos,
-                                                      int qsplit, uint8_t* __restrict__ send) {
+                                                      int qsplit, uint8_t* __restrict__ send,
+                                                      const int* __restrict__ dst_base,
+                                                      EpPeerRows peer) {
   const int lane = threadIdx.x & 31;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int t = gw / qsplit, part = gw % qsplit;
@@ -252,7 +284,7 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const __nv_bfloat16* __res
 #pragma unroll
       for (int d = 0; d < kEpMaxWorld; ++d) {
         if (pos[d] < 0) continue;
-        uint8_t* row = send + (size_t)pos[d] * row_bytes;
+        uint8_t* row = peer.row(send, d, pos[d], dst_base, row_bytes);
         *reinterpret_cast<uint4*>(row + (size_t)(q + g) * 512 + lane * 16) = code;
         if (lane == 0) *reinterpret_cast<uint32_t*>(row + H + (q + g) * 4) = s4;
       }
@@ -328,6 +360,132 @@ __global__ void __launch_bounds__(256) ep_return_gather_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// peer-memory exchange: signals, bounded waits, unpack and return over NVLink
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Source: after its rows are in every owner's buffer (previous launch), tell
+// owner d how many rows / routes arrived and where their returns go, then
+// raise disp_flag[rank] there.  One lane per destination.
+__global__ void ep_signal_dispatch_kernel(const uint64_t* __restrict__ bases, int rank, int world,
+                                          const int* __restrict__ send_counts,
+                                          const int* __restrict__ dst_base, int epoch) {
+  const int d = threadIdx.x;
+  if (d >= world) return;
+  uint8_t* b = reinterpret_cast<uint8_t*>(bases[d]);
+  int* info = reinterpret_cast<int*>(b + kEpInfoOff) + 4 * rank;
+  info[0] = send_counts[2 * d];
+  info[1] = send_counts[2 * d + 1];
+  info[2] = dst_base[2 * d + 1];
+  __threadfence_system();
+  st_release_sys(reinterpret_cast<int*>(b) + rank, epoch);
+}
+
+// Owner: every route row is in its source's return region (previous launch);
+// raise ret_flag[rank] in every rank's buffer.
+__global__ void ep_signal_return_kernel(const uint64_t* __restrict__ bases, int rank, int world,
+                                        int epoch) {
+  const int d = threadIdx.x;
+  if (d >= world) return;
+  __threadfence_system();
+  st_release_sys(reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bases[d]) + kEpRetFlagOff) + rank,
+                 epoch);
+}
+
+// Bounded wait until flags[0..world) all equal epoch (one lane per flag).  On
+// timeout the lane records err_code and returns: the kernels that follow then
+// read whatever the buffer holds, the host sees the error.
+__global__ void ep_wait_kernel(const int* __restrict__ flags, int world, int epoch, int err_code) {
+  const int s = threadIdx.x;
+  if (s >= world) return;
+  const uint64_t t0 = globaltimer();
+  while (ld_acquire_sys(flags + s) != epoch) {
+    if (globaltimer() - t0 > kWaitTimeoutNs) {
+      record_error(err_code);
+      return;
+    }
+    __nanosleep(200);
+  }
+}
+
+// Owner, peer-memory form of ep_unpack_kernel: received row i sits in source
+// s = i / cap's region, valid when i % cap < info[s].rows.  A route's return
+// destination is encoded as (s << 24) | row in s's return region.
+__global__ void ep_unpack_p2p_kernel(const uint8_t* __restrict__ exch, int cap, int T_own, int k,
+                                     int H, long long row_bytes, int e_begin, int e_count,
+                                     int world, int ret_cap, int64_t* __restrict__ idx_local,
+                                     float* __restrict__ w_local, int* __restrict__ ret_dst) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  const int n = T_own + world * cap;
+  if (t >= n) return;
+  int s = -1, ii = 0;
+  if (t >= T_own) {
+    s = (t - T_own) / cap;
+    ii = (t - T_own) - s * cap;
+  }
+  const int* info = reinterpret_cast<const int*>(exch + kEpInfoOff);
+  const bool valid = s >= 0 && ii < info[4 * s];
+  if (!valid) {
+    for (int j = 0; j < k; ++j) {
+      idx_local[(size_t)t * k + j] = -1;
+      w_local[(size_t)t * k + j] = 0.f;
+      ret_dst[(size_t)t * k + j] = -1;
+    }
+    return;
+  }
+  const int routes = info[4 * s + 1], ret_off = info[4 * s + 2];
+  const uint8_t* meta = exch + kEpHeaderBytes + (size_t)(t - T_own) * row_bytes + H + H / 128;
+  for (int j = 0; j < k; ++j) {
+    const int32_t e = reinterpret_cast<const int32_t*>(meta + kEpMetaEntry * j)[0];
+    const float w = reinterpret_cast<const float*>(meta + kEpMetaEntry * j)[1];
+    const int32_t ri = reinterpret_cast<const int32_t*>(meta + kEpMetaEntry * j)[2];
+    int64_t le = -1;
+    int rd = -1;
+    if (e >= 0) {
+      const int dst = ret_off + ri;
+      if (e >= e_begin && e < e_begin + e_count && ri >= 0 && ri < routes && ret_off >= 0 &&
+          dst < ret_cap) {
+        le = e - e_begin;
+        rd = (s << 24) | dst;
+      } else {
+        record_error(DSV4_DEVERR_BAD_INDEX);
+      }
+    }
+    idx_local[(size_t)t * k + j] = le;
+    w_local[(size_t)t * k + j] = w;
+    ret_dst[(size_t)t * k + j] = rd;
+  }
+}
+
+// Owner: every received route's output row straight into its source's return
+// region over peer memory (one warp per route, 16-byte stores).
+__global__ void __launch_bounds__(256) ep_return_p2p_kernel(
+    const __nv_bfloat16* __restrict__ O, int H, const int* __restrict__ route_slot,
+    const int* __restrict__ ret_dst, int n_routes, const uint64_t* __restrict__ bases, int world,
+    long long ret_region_off, int ret_cap) {
+  const int lane = threadIdx.x & 31;
+  const int nwarps = (gridDim.x * blockDim.x) >> 5;
+  for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < n_routes; r += nwarps) {
+    const int d = ret_dst[r];
+    const int sl = route_slot[r];
+    if (d < 0 || sl < 0) continue;
+    const int s = d >> 24, row = d & 0xFFFFFF;
+    if (s >= world || row >= ret_cap) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(O + (size_t)sl * H);
+    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(bases[s]) + ret_region_off +
+                                          (size_t)row * H * 2);
+    for (int c = lane; c < H / 8; c += 32) dst[c] = src[c];
+  }
+}
+
+// ---------------------------------------------------------------------------
 // host launchers
 // ---------------------------------------------------------------------------
 long long ep_dispatch_workspace(int T, int world) {
@@ -336,9 +494,20 @@ long long ep_dispatch_workspace(int T, int world) {
   return 256 + 2 * series + 256 + ((long long)T * world * 4 + 255) / 256 * 256;
 }
 
+long long ep_exchange_bytes(int H, int k, int world, int cap) {
+  const long long recv = ((long long)world * cap * ep_row_bytes(H, k) + 255) / 256 * 256;
+  const long long ret = ((long long)cap * k * H * 2 + 255) / 256 * 256;
+  return kEpHeaderBytes + recv + ret;
+}
+
+long long ep_return_region_off(int H, int k, int world, int cap) {
+  return kEpHeaderBytes + ((long long)world * cap * ep_row_bytes(H, k) + 255) / 256 * 256;
+}
+
 int launch_ep_dispatch(const void* x, const int64_t* indices, const float* weights, int T, int H,
                        int k, int E, int world, uint8_t* send, int* send_counts, int* ret_pos,
-                       uint8_t* ws, int num_sms, cudaStream_t st) {
+                       uint8_t* ws, int num_sms, cudaStream_t st, const uint64_t* peer_bases,
+                       int rank, int cap, int epoch) {
   const int nchunks = (T + kEpChunk - 1) / kEpChunk;
   const long long series = (2LL * world * nchunks * 4 + 255) / 256 * 256;
   int* ctrl = reinterpret_cast<int*>(ws);
@@ -351,17 +520,60 @@ int launch_ep_dispatch(const void* x, const int64_t* indices, const float* weigh
   launch_k(ep_count_kernel, nchunks, kEpChunk, 0, st,
            indices, T, k, E, world, nchunks, cc, cb,
                                                send_counts, dst_base, ctrl);
-  launch_k(ep_plan_kernel, nchunks, kEpChunk, 0, st,
-           indices, weights, T, k, E, world, H, rb, nchunks,
-                                              cb, dst_base, row_pos, send, ret_pos, ctrl);
+  EpPeerRows peer{peer_bases, rank, (long long)cap * rb};
+  launch_k(ep_plan_kernel, nchunks, kEpChunk, 0, st, indices, weights, T, k, E, world, H, rb,
+           nchunks, cb, dst_base, row_pos, send, ret_pos, ctrl, peer);
   const int KQ = H / 512;
   int qsplit = (int)((8LL * num_sms * 8 + T - 1) / T);  // about 8 warps per SM slot
   qsplit = qsplit < 1 ? 1 : (qsplit > KQ ? KQ : qsplit);
   const long long warps = (long long)T * qsplit;
   launch_k(ep_pack_kernel, (unsigned)((warps + 7) / 8), 256, 0, st,
-           static_cast<const __nv_bfloat16*>(x),
-                                                              T, H, world, rb, row_pos, qsplit,
-                                                              send);
+           static_cast<const __nv_bfloat16*>(x), T, H, world, rb, row_pos, qsplit, send,
+           (const int*)dst_base, peer);
+  if (peer_bases)
+    launch_k(ep_signal_dispatch_kernel, 1, 32, 0, st, peer_bases, rank, world,
+             (const int*)send_counts, (const int*)dst_base, epoch);
+  return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
+}
+
+// A source with no tokens: zero counts and offsets, then the dispatch signal.
+int launch_ep_signal_empty(const uint64_t* peer_bases, int rank, int world, int* send_counts,
+                           uint8_t* ws, int epoch, cudaStream_t st) {
+  int* zero_base = reinterpret_cast<int*>(ws);  // [world][2] zeros (dst_base of no rows)
+  if (cudaMemsetAsync(send_counts, 0, 2 * world * sizeof(int), st) != cudaSuccess ||
+      cudaMemsetAsync(zero_base, 0, 2 * world * sizeof(int), st) != cudaSuccess)
+    return DSV4_ERR_CUDA;
+  launch_k(ep_signal_dispatch_kernel, 1, 32, 0, st, peer_bases, rank, world,
+           (const int*)send_counts, (const int*)zero_base, epoch);
+  return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
+}
+
+int launch_ep_wait(const int* flags, int world, int epoch, int err_code, cudaStream_t st) {
+  launch_k(ep_wait_kernel, 1, 32, 0, st, flags, world, epoch, err_code);
+  return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
+}
+
+int launch_ep_unpack_p2p(const uint8_t* exch, int cap, int T_own, int k, int H, int e_begin,
+                         int e_count, int world, int64_t* idx_local, float* w_local, int* ret_dst,
+                         cudaStream_t st) {
+  const int n = T_own + world * cap;
+  if (n <= 0) return DSV4_OK;
+  launch_k(ep_unpack_p2p_kernel, (n + 255) / 256, 256, 0, st, exch, cap, T_own, k, H,
+           ep_row_bytes(H, k), e_begin, e_count, world, cap * k, idx_local, w_local, ret_dst);
+  return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
+}
+
+int launch_ep_return_p2p(const void* O, int H, int k, const int* route_slot, const int* ret_dst,
+                         int n_routes, const uint64_t* bases, int rank, int world, int cap,
+                         int epoch, int num_sms, cudaStream_t st) {
+  if (n_routes > 0) {
+    int grid = (n_routes + 7) / 8;
+    grid = grid < num_sms * 8 ? grid : num_sms * 8;
+    launch_k(ep_return_p2p_kernel, grid, 256, 0, st, static_cast<const __nv_bfloat16*>(O), H,
+             route_slot, ret_dst, n_routes, bases, world, ep_return_region_off(H, k, world, cap),
+             cap * k);
+  }
+  launch_k(ep_signal_return_kernel, 1, 32, 0, st, bases, rank, world, epoch);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
 

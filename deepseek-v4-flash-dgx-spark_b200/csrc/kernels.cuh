@@ -63,7 +63,20 @@ long long ep_row_bytes(int H, int k);
 long long ep_dispatch_workspace(int T, int world);
 int launch_ep_dispatch(const void* x, const int64_t* indices, const float* weights, int T, int H,
                        int k, int E, int world, uint8_t* send, int* send_counts, int* ret_pos,
-                       uint8_t* ws, int num_sms, cudaStream_t st);
+                       uint8_t* ws, int num_sms, cudaStream_t st,
+                       const uint64_t* peer_bases = nullptr, int rank = 0, int cap = 0,
+                       int epoch = 0);
+long long ep_exchange_bytes(int H, int k, int world, int cap);
+long long ep_return_region_off(int H, int k, int world, int cap);
+int launch_ep_signal_empty(const uint64_t* peer_bases, int rank, int world, int* send_counts,
+                           uint8_t* ws, int epoch, cudaStream_t st);
+int launch_ep_wait(const int* flags, int world, int epoch, int err_code, cudaStream_t st);
+int launch_ep_unpack_p2p(const uint8_t* exch, int cap, int T_own, int k, int H, int e_begin,
+                         int e_count, int world, int64_t* idx_local, float* w_local, int* ret_dst,
+                         cudaStream_t st);
+int launch_ep_return_p2p(const void* O, int H, int k, const int* route_slot, const int* ret_dst,
+                         int n_routes, const uint64_t* bases, int rank, int world, int cap,
+                         int epoch, int num_sms, cudaStream_t st);
 int launch_ep_unpack(const uint8_t* recv, int R, int T_own, int k, int H, int e_begin, int e_count,
                      const int* recv_counts, int world, int64_t* idx_local, float* w_local,
                      int* ret_dst, cudaStream_t st);

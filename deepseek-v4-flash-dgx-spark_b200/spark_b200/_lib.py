@@ -42,6 +42,7 @@ DEVERR_NAMES = {
     104: "expert index out of range",
     105: "routing plan exceeds its workspace",
     106: "materializer source offset not 16-byte aligned",
+    107: "a peer rank's exchange flag did not arrive in time",
 }
 
 
@@ -114,6 +115,20 @@ _SIGNATURES = {
                                        c_vp, c_vp, c_ll, c_vp, c_ll, c_vp]),
     "dsv4_ep_combine": (c_int, [ctypes.POINTER(MoELayerDesc), c_int, c_int, c_vp, c_vp, c_vp, c_int, c_int,
                                 c_vp, c_ll, c_vp, c_vp]),
+    "dsv4_ep_exchange_bytes": (c_ll, [c_int, c_int, c_int, c_int]),
+    "dsv4_ep_exchange_alloc": (c_int, [c_int, c_ll, ctypes.POINTER(c_vp)]),
+    "dsv4_ep_exchange_free": (c_int, [c_vp]),
+    "dsv4_ipc_handle": (c_int, [c_vp, c_vp]),
+    "dsv4_ipc_open": (c_int, [c_int, c_vp, ctypes.POINTER(c_vp)]),
+    "dsv4_ipc_close": (c_int, [c_vp]),
+    "dsv4_ep_p2p_dispatch_workspace_bytes": (c_ll, [c_int, c_int]),
+    "dsv4_ep_dispatch_p2p": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_int,
+                                     c_int, c_vp, c_vp, c_ll, c_vp]),
+    "dsv4_ep_p2p_expert_workspace_bytes": (c_ll, [ctypes.POINTER(MoELayerDesc), c_int, c_int, c_int]),
+    "dsv4_ep_expert_forward_p2p": (c_int, [ctypes.POINTER(MoELayerDesc), c_int, c_int, c_vp, c_int, c_vp, c_vp,
+                                           c_int, c_int, c_vp, c_ll, c_vp]),
+    "dsv4_ep_combine_p2p": (c_int, [ctypes.POINTER(MoELayerDesc), c_int, c_int, c_vp, c_vp, c_vp, c_int, c_int,
+                                    c_int, c_vp, c_ll, c_vp, c_vp]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

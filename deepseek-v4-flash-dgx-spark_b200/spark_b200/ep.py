@@ -22,6 +22,10 @@ The device work sits behind an ``ops`` object; ``CudaEPOps`` drives
 libdsv4moe.so, and the CPU tests substitute an implementation of the same
 buffer formats to exercise this orchestration over ``gloo``.  Row exchanges
 carry bf16 rows as their bytes so every backend moves them unchanged.
+
+``PeerExchange`` / ``ep_forward_peer`` run the same five steps with the two
+exchanges done by the kernels over NVLink peer memory (IPC-mapped buffers,
+epoch flags with bounded waits): no host collective and no host sync per call.
 """
 
 from __future__ import annotations
@@ -134,6 +138,129 @@ def ep_forward(ops, x: torch.Tensor, group=None, routing=None) -> torch.Tensor:
     return ops.combine(ret_recv, ret_pos, indices, x, R, state)
 
 
+class PeerExchange:
+    """Exchange buffers of one expert-parallel layer over peer memory.
+
+    Every rank allocates one buffer (``dsv4_ep_exchange_alloc``), sends its
+    CUDA IPC handle to the others through the process group (the only
+    collective, at set-up), and maps theirs; ``peer_bases`` is the device array
+    of all W buffers as seen from this GPU.  ``cap_tokens`` bounds the tokens
+    any rank passes per call.  Set-up is collective: every rank of ``group``
+    constructs its exchange in the same order."""
+
+    def __init__(self, moe, cap_tokens: int, group=None):
+        self.lib = _lib.load()
+        self.moe = moe
+        self.world, self.rank = moe.world, moe.rank
+        self.cap = int(cap_tokens)
+        self.dev = moe.expert_slot.device
+        H, k = moe.dim, moe.n_activated_experts
+        nbytes = int(self.lib.dsv4_ep_exchange_bytes(H, k, self.world, self.cap))
+        if nbytes <= 0:
+            raise RuntimeError("dsv4_ep_exchange_bytes: unsupported shape or capacity")
+        self.nbytes = nbytes
+        self._mapped: list[ctypes.c_void_p] = []
+        self.buf = ctypes.c_void_p()
+        check(self.lib.dsv4_ep_exchange_alloc(self.dev.index or 0, nbytes, ctypes.byref(self.buf)),
+              "dsv4_ep_exchange_alloc")
+        bases = [0] * self.world
+        bases[self.rank] = self.buf.value
+        if self.world > 1:
+            handle = (ctypes.c_uint8 * 64)()
+            check(self.lib.dsv4_ipc_handle(self.buf, handle), "dsv4_ipc_handle")
+            mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=self.dev)
+            every = torch.empty(self.world * 64, dtype=torch.uint8, device=self.dev)
+            dist.all_gather_into_tensor(every, mine, group=group)
+            every = every.cpu().numpy().tobytes()
+            for s in range(self.world):
+                if s == self.rank:
+                    continue
+                h = (ctypes.c_uint8 * 64).from_buffer_copy(every[64 * s:64 * (s + 1)])
+                p = ctypes.c_void_p()
+                check(self.lib.dsv4_ipc_open(self.dev.index or 0, h, ctypes.byref(p)), "dsv4_ipc_open")
+                self._mapped.append(p)
+                bases[s] = p.value
+            dist.barrier(group=group)  # every buffer is mapped everywhere before the first call
+        self.bases = bases
+        self.peer_bases = torch.tensor(bases, dtype=torch.int64, device=self.dev)
+        self.epoch = 0
+        self._ws = None
+
+    def close(self) -> None:
+        for p in self._mapped:
+            self.lib.dsv4_ipc_close(p)
+        self._mapped = []
+        if self.buf:
+            torch.cuda.synchronize(self.dev)
+            self.lib.dsv4_ep_exchange_free(self.buf)
+            self.buf = ctypes.c_void_p()
+
+    def workspace(self, T_own: int) -> torch.Tensor:
+        d = self.moe.layer_desc()
+        need = int(self.lib.dsv4_ep_p2p_expert_workspace_bytes(ctypes.byref(d), self.world, T_own, self.cap))
+        if need < 0:
+            raise RuntimeError("dsv4_ep_p2p_expert_workspace_bytes: invalid layer")
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(max(need, 1), dtype=torch.uint8, device=self.dev)
+        return self._ws
+
+
+def peer_dispatch(ex: PeerExchange, x, weights, indices, epoch: int):
+    """Step 1 over peer memory: this rank's rows into every owner's buffer."""
+    T, k = x.shape[0], ex.moe.n_activated_experts
+    if T > ex.cap:
+        raise RuntimeError(f"{T} tokens exceed the exchange capacity of {ex.cap}")
+    ret_pos = torch.empty((max(T, 1), k), dtype=torch.int32, device=x.device)
+    ws = torch.empty(max(int(ex.lib.dsv4_ep_p2p_dispatch_workspace_bytes(T, ex.world)), 1), dtype=torch.uint8,
+                     device=x.device)
+    weights = weights.to(torch.float32).contiguous()
+    indices = indices.to(torch.int64).contiguous()
+    check(ex.lib.dsv4_ep_dispatch_p2p(ptr(x), ptr(indices), ptr(weights), T, ex.moe.dim, k,
+                                      ex.moe.n_routed_experts, ex.world, ex.rank, ptr(ex.peer_bases), ex.cap,
+                                      epoch, ptr(ret_pos), ptr(ws), ws.numel(), stream_ptr()),
+          "dsv4_ep_dispatch_p2p")
+    return ret_pos, indices
+
+
+def peer_expert_forward(ex: PeerExchange, x, epoch: int):
+    """Step 3 over peer memory: wait for every source, compute, return rows."""
+    T = x.shape[0]
+    ws = ex.workspace(T)
+    d = ex.moe.layer_desc()
+    check(ex.lib.dsv4_ep_expert_forward_p2p(ctypes.byref(d), ex.rank, ex.world, ptr(x), T, ex.buf,
+                                            ptr(ex.peer_bases), ex.cap, epoch, ptr(ws), ws.numel(), stream_ptr()),
+          "dsv4_ep_expert_forward_p2p")
+    return ws
+
+
+def peer_combine(ex: PeerExchange, x, ret_pos, indices, ws, epoch: int):
+    """Step 5 over peer memory: wait for every owner's returns, combine."""
+    y = torch.empty_like(x)
+    d = ex.moe.layer_desc()
+    check(ex.lib.dsv4_ep_combine_p2p(ctypes.byref(d), ex.rank, ex.world, ex.buf, ptr(ret_pos), ptr(indices),
+                                     x.shape[0], ex.cap, epoch, ptr(ws), ws.numel(), ptr(y), stream_ptr()),
+          "dsv4_ep_combine_p2p")
+    return y
+
+
+def ep_forward_peer(ex: PeerExchange, x: torch.Tensor, routing=None) -> torch.Tensor:
+    """One expert-parallel layer call over peer memory: no host collective and
+    no host synchronisation.  Every rank must call it once per layer call."""
+    ex.epoch += 1
+    if routing is None:
+        weights, indices = ex.moe.gate(x)
+    else:
+        weights, indices = routing
+    ret_pos, indices = peer_dispatch(ex, x, weights, indices, ex.epoch)
+    ws = peer_expert_forward(ex, x, ex.epoch)
+    return peer_combine(ex, x, ret_pos, indices, ws, ex.epoch)
+
+
 def ep_moe_forward(moe, x: torch.Tensor, routing=None) -> torch.Tensor:
-    """``MoE.forward`` body for world > 1 (x [T, H] bf16 on this rank's GPU)."""
+    """``MoE.forward`` body for world > 1 (x [T, H] bf16 on this rank's GPU):
+    over peer memory once ``moe.enable_peer_exchange`` set it up, else through
+    host collectives."""
+    ex = getattr(moe, "peer_exchange", None)
+    if ex is not None:
+        return ep_forward_peer(ex, x, routing=routing)
     return ep_forward(CudaEPOps(moe), x, group=moe.group, routing=routing)

@@ -426,6 +426,19 @@ class MoE(nn.Module):
         self.shared_experts = Expert(args.dim, args.moe_inter_dim, swiglu_limit=args.swiglu_limit, device=device)
         self.register_load_state_dict_post_hook(lambda m, _keys: m.refresh_scale_atoms())
 
+    def enable_peer_exchange(self, cap_tokens: int) -> None:
+        """Expert parallelism over NVLink peer memory from now on (collective:
+        every rank of the group calls it with the same cap_tokens, the most
+        tokens any rank will pass per call)."""
+        if self.world == 1:
+            return
+        from .ep import PeerExchange
+
+        old = getattr(self, "peer_exchange", None)
+        if old is not None:
+            old.close()
+        self.peer_exchange = PeerExchange(self, cap_tokens, group=self.group)
+
     def refresh_scale_atoms(self) -> None:
         slots = self.expert_slot[self.experts_start_idx:self.experts_end_idx].contiguous()
         check(_lib.load().dsv4_build_scale_atoms(ptr(self.arena.buffer), self.arena.slot_stride, ptr(slots),

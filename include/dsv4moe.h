@@ -49,6 +49,7 @@ extern "C" {
 #define DSV4_DEVERR_BAD_INDEX 104
 #define DSV4_DEVERR_PLAN_OVERFLOW 105
 #define DSV4_DEVERR_MISALIGNED 106  /* a materializer source offset is not 16-byte aligned */
+#define DSV4_DEVERR_TIMEOUT_PEER 107  /* a peer rank's exchange flag did not arrive within 2 s */
 
 DSV4_API int dsv4_version(void);
 /* Number of kernels the library has enqueued in this process (every launch
@@ -297,6 +298,66 @@ DSV4_API int dsv4_ep_combine(const dsv4_moe_layer* L, int rank, int world, const
                              const int* ret_pos, const int64_t* indices, int T_own, int R,
                              const void* workspace, long long workspace_bytes, void* y,
                              void* stream);
+
+/* ------------------------------------------------------------------------
+ * Expert parallelism over peer memory (one process per GPU of one NVLink /
+ * NVSwitch node).  The same five steps as above, with the two exchanges done
+ * by the kernels themselves instead of host collectives and with no host
+ * synchronisation: the source's pack kernel quantizes each token once and
+ * stores its FP8 row straight into the owning rank's exchange buffer over
+ * NVLink, and the owner's return kernel stores every route's bf16 output row
+ * straight into the source's buffer.  Each side raises an epoch flag in the
+ * other's buffer after a system-scope fence; the waiting side spins on it for
+ * at most 2 s (DSV4_DEVERR_TIMEOUT_PEER on expiry, never a hang).  Plain
+ * peer loads and stores only: no multicast object, no NVLS.
+ *
+ * Set-up, once per rank: an exchange buffer of dsv4_ep_exchange_bytes(H,
+ * topk, W, cap_tokens) from dsv4_ep_exchange_alloc (zeroed), its IPC handle
+ * (dsv4_ipc_handle) sent to every other rank, their buffers mapped with
+ * dsv4_ipc_open, and a device array uint64 peer_bases[W] of every rank's
+ * buffer as seen from this GPU (this rank's own at index rank).  cap_tokens
+ * bounds the tokens any rank passes per call.  Per layer call, every rank
+ * uses the same epoch, a value that differs from the previous call's:
+ *
+ *   dsv4_ep_dispatch_p2p       (source)  rows into every owner's buffer, ret_pos
+ *   dsv4_ep_expert_forward_p2p (owner)   waits for all W sources, computes,
+ *                                        stores return rows into their buffers
+ *   dsv4_ep_combine_p2p        (source)  waits for all W owners, y [T_own][H]
+ *
+ * Buffers are reused across calls without further synchronisation: a source
+ * starts call e+1 only after its call-e combine has received every owner's
+ * returns, so no owner is still reading call e's rows.  The result is
+ * bit-identical to dsv4_moe_forward.  Replaces the same reference exchange as
+ * above (spark_runtime/lazy_official_runtime.py:999-1000).
+ * ---------------------------------------------------------------------- */
+#define DSV4_IPC_HANDLE_BYTES 64
+DSV4_API long long dsv4_ep_exchange_bytes(int hidden, int topk, int world, int cap_tokens);
+DSV4_API int dsv4_ep_exchange_alloc(int device, long long bytes, void** out);
+DSV4_API int dsv4_ep_exchange_free(void* buffer);
+/* 64-byte CUDA IPC handle of an allocation from dsv4_ep_exchange_alloc. */
+DSV4_API int dsv4_ipc_handle(const void* buffer, uint8_t* handle);
+/* Map another process's buffer into GPU `device`'s address space (peer access). */
+DSV4_API int dsv4_ipc_open(int device, const uint8_t* handle, void** out);
+DSV4_API int dsv4_ipc_close(void* mapped);
+DSV4_API long long dsv4_ep_p2p_dispatch_workspace_bytes(int T, int world);
+/* ret_pos: device int32 [T][topk], the row of this rank's return region that
+ * will hold each route (blocks in owner-rank order). */
+DSV4_API int dsv4_ep_dispatch_p2p(const void* x, const int64_t* indices, const float* weights,
+                                  int T, int hidden, int topk, int n_routed, int world, int rank,
+                                  const uint64_t* peer_bases, int cap_tokens, int epoch,
+                                  int* ret_pos, void* workspace, long long workspace_bytes,
+                                  void* stream);
+DSV4_API long long dsv4_ep_p2p_expert_workspace_bytes(const dsv4_moe_layer* L, int world,
+                                                      int T_own, int cap_tokens);
+/* exchange: this rank's own buffer. Steps 3 and 5 share one workspace. */
+DSV4_API int dsv4_ep_expert_forward_p2p(const dsv4_moe_layer* L, int rank, int world,
+                                        const void* x_own, int T_own, void* exchange,
+                                        const uint64_t* peer_bases, int cap_tokens, int epoch,
+                                        void* workspace, long long workspace_bytes, void* stream);
+DSV4_API int dsv4_ep_combine_p2p(const dsv4_moe_layer* L, int rank, int world,
+                                 const void* exchange, const int* ret_pos, const int64_t* indices,
+                                 int T_own, int cap_tokens, int epoch, const void* workspace,
+                                 long long workspace_bytes, void* y, void* stream);
 
 #ifdef __cplusplus
 }

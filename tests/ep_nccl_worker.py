@@ -1,5 +1,6 @@
 """One rank of the two-GPU expert-parallel check (launched by
-tests/test_gpu_ep.py::test_ep_nccl_two_gpus through torch.distributed.run).
+tests/test_gpu_ep.py::test_ep_two_gpus through torch.distributed.run;
+EP_MODE=peer exchanges over NVLink peer memory, else over NCCL).
 
 Every rank builds the same synthetic layer, keeps the experts it owns in its
 arena, routes its own tokens and runs ``MoE.forward`` over NCCL; the result
@@ -29,13 +30,20 @@ def main() -> int:
         full = build_moe(layer, device=dev, group=singles[rank])  # single-GPU layer, every expert
         ep = build_moe(layer, device=dev)  # expert-parallel over the world: own experts only
         assert ep.world == world and ep.n_local_experts == cfg.n_routed // world
-        n = (64, 37)[rank % 2]
-        g = torch.Generator().manual_seed(1000 + rank)
-        x = torch.randn(1, n, cfg.dim, generator=g).to(torch.bfloat16).to(dev)
-        y = ep(x)
-        y_ref = full(x)
-        torch.cuda.synchronize()
-        ok = torch.equal(y.view(torch.int16), y_ref.view(torch.int16))
+        if os.environ.get("EP_MODE", "nccl") == "peer":
+            ep.enable_peer_exchange(64)
+        ok = True
+        for step in range(2):  # the second call reuses the exchange buffers
+            n = ((64, 37), (5, 64))[step][rank % 2]
+            g = torch.Generator().manual_seed(1000 + 10 * step + rank)
+            x = torch.randn(1, n, cfg.dim, generator=g).to(torch.bfloat16).to(dev)
+            y = ep(x)
+            y_ref = full(x)
+            torch.cuda.synchronize()
+            ok = ok and torch.equal(y.view(torch.int16), y_ref.view(torch.int16))
+        from spark_b200 import _lib
+
+        _lib.raise_on_device_error()
         flag = torch.tensor([1 if ok else 0], device=dev)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
         if ok:
@@ -43,6 +51,9 @@ def main() -> int:
         else:
             diff = (y.float() - y_ref.float()).abs().max().item()
             print("EP_MISMATCH", rank, diff, flush=True)
+        if getattr(ep, "peer_exchange", None) is not None:
+            dist.barrier()  # no rank unmaps a buffer another may still store to
+            ep.peer_exchange.close()
         return 0 if int(flag.item()) == 1 else 1
     finally:
         dist.destroy_process_group()

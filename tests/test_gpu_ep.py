@@ -8,7 +8,9 @@ owning-rank forward and combine are checked without a second GPU:
 * the expert-parallel output equals ``dsv4_moe_forward`` on the same tokens
   bit for bit.
 
-The real multi-process run over NCCL is ``test_ep_nccl_two_gpus`` (needs 2 GPUs)."""
+The peer-memory form (``dsv4_ep_*_p2p``) is emulated the same way with W
+exchange buffers on the one GPU.  The real multi-process runs, over NCCL and
+over peer memory, are ``test_ep_two_gpus`` (needs 2 GPUs)."""
 
 import ctypes
 import os
@@ -130,18 +132,141 @@ def test_emulated_ep_is_bit_identical_to_single_gpu(cuda_device, name, W, tokens
         assert np.array_equal(send[:o_send.shape[0], :used].cpu().numpy(), o_send[:, :used])
 
 
+def _emulated_peer_ep(moe, xs, routings, W, epochs=(1, 2)):
+    """The peer-memory steps for W emulated ranks on one GPU: W exchange
+    buffers, peer_bases = those W buffers.  All of one step's launches (every
+    rank's dispatch, then every owner's forward, then every combine) precede
+    the next step's in one stream, so each flag a wait kernel polls was raised
+    by a kernel that already finished: nothing waits on a concurrent kernel."""
+    L = _lib()
+    lib = L.load()
+    E, H, k = moe.n_routed_experts, moe.dim, moe.n_activated_experts
+    d = moe.layer_desc()
+    cap = max(max(x.shape[0] for x in xs), 1)
+    nbytes = lib.dsv4_ep_exchange_bytes(H, k, W, cap)
+    assert nbytes > 0
+    bufs = []
+    for _ in range(W):
+        p = ctypes.c_void_p()
+        L.check(lib.dsv4_ep_exchange_alloc(torch.cuda.current_device(), nbytes, ctypes.byref(p)), "alloc")
+        bufs.append(p)
+    bases = torch.tensor([b.value for b in bufs], dtype=torch.int64, device="cuda")
+    out = []
+    try:
+        for epoch in epochs:
+            disp = []
+            for r, (x, (w, idx)) in enumerate(zip(xs, routings)):
+                T = x.shape[0]
+                ret_pos = torch.empty((max(T, 1), k), dtype=torch.int32, device="cuda")
+                ws = torch.empty(max(lib.dsv4_ep_p2p_dispatch_workspace_bytes(T, W), 1), dtype=torch.uint8,
+                                 device="cuda")
+                L.check(lib.dsv4_ep_dispatch_p2p(L.ptr(x), L.ptr(idx), L.ptr(w), T, H, k, E, W, r, L.ptr(bases),
+                                                 cap, epoch, L.ptr(ret_pos), L.ptr(ws), ws.numel(), L.stream_ptr()),
+                        "dsv4_ep_dispatch_p2p")
+                disp.append((ret_pos, ws))
+            wss = []
+            for r, x in enumerate(xs):
+                T = x.shape[0]
+                ws = torch.empty(max(lib.dsv4_ep_p2p_expert_workspace_bytes(ctypes.byref(d), W, T, cap), 1),
+                                 dtype=torch.uint8, device="cuda")
+                L.check(lib.dsv4_ep_expert_forward_p2p(ctypes.byref(d), r, W, L.ptr(x), T, bufs[r], L.ptr(bases),
+                                                       cap, epoch, L.ptr(ws), ws.numel(), L.stream_ptr()),
+                        "dsv4_ep_expert_forward_p2p")
+                wss.append(ws)
+            ys = []
+            for r, (x, (w, idx)) in enumerate(zip(xs, routings)):
+                y = torch.empty_like(x)
+                L.check(lib.dsv4_ep_combine_p2p(ctypes.byref(d), r, W, bufs[r], L.ptr(disp[r][0]), L.ptr(idx),
+                                                x.shape[0], cap, epoch, L.ptr(wss[r]), wss[r].numel(), L.ptr(y),
+                                                L.stream_ptr()), "dsv4_ep_combine_p2p")
+                ys.append(y)
+            torch.cuda.synchronize()
+            L.raise_on_device_error()
+            out.append(ys)
+    finally:
+        torch.cuda.synchronize()
+        for b in bufs:
+            lib.dsv4_ep_exchange_free(b)
+    return out
+
+
+@pytest.mark.parametrize("name,W,tokens", [("cpu_ref", 2, (9, 4)), ("cpu_ref", 4, (1, 0, 40, 300)),
+                                           ("decode", 8, (64, 64, 64, 64, 64, 64, 64, 64)),
+                                           ("decode", 2, (1100, 7))])
+def test_emulated_peer_ep_is_bit_identical_to_single_gpu(cuda_device, name, W, tokens):
+    """Dispatch rows stored into the owners' exchange buffers, return rows into
+    the sources', epoch flags in both directions: every rank's result equals
+    the single-GPU layer bit for bit, on two consecutive calls (buffer reuse)."""
+    from spark_b200.synthetic import CONFIGS, build_moe, make_layer
+
+    cfg = CONFIGS[name].with_tokens(max(tokens))
+    layer = make_layer(cfg, seed=2, device="cpu")
+    moe = build_moe(layer, device=cuda_device)
+    k, H = cfg.topk, cfg.dim
+    xs, routings = [], []
+    for r, n in enumerate(tokens):
+        g = torch.Generator().manual_seed(70 + r)
+        x = torch.randn(n, H, generator=g).to(torch.bfloat16).to(cuda_device)
+        w, idx = moe.gate(x) if n else (torch.empty(0, k, device=cuda_device),
+                                        torch.empty(0, k, dtype=torch.int64, device=cuda_device))
+        xs.append(x.contiguous())
+        routings.append((w.float().contiguous(), idx.to(torch.int64).contiguous()))
+    runs = _emulated_peer_ep(moe, xs, routings, W)
+    for ys in runs:
+        for r, (x, (w, idx)) in enumerate(zip(xs, routings)):
+            if x.shape[0] == 0:
+                continue
+            y_ref = moe.forward_tokens(x, routing=(w, idx))
+            torch.cuda.synchronize()
+            assert torch.equal(ys[r].view(torch.int16), y_ref.view(torch.int16)), r
+
+
+def test_peer_wait_times_out_with_an_error_not_a_hang(cuda_device):
+    """An owner whose sources never signal: the wait kernel gives up after its
+    bound, latches DSV4_DEVERR_TIMEOUT_PEER, and the context stays usable."""
+    from spark_b200.synthetic import CONFIGS, build_moe, make_layer
+
+    L = _lib()
+    lib = L.load()
+    cfg = CONFIGS["cpu_ref"].with_tokens(4)
+    moe = build_moe(make_layer(cfg, seed=2, device="cpu"), device=cuda_device)
+    d = moe.layer_desc()
+    W, cap = 2, 4
+    p = ctypes.c_void_p()
+    L.check(lib.dsv4_ep_exchange_alloc(torch.cuda.current_device(),
+                                       lib.dsv4_ep_exchange_bytes(cfg.dim, cfg.topk, W, cap), ctypes.byref(p)),
+            "alloc")
+    try:
+        bases = torch.tensor([p.value, p.value], dtype=torch.int64, device="cuda")
+        ws = torch.empty(lib.dsv4_ep_p2p_expert_workspace_bytes(ctypes.byref(d), W, 0, cap), dtype=torch.uint8,
+                         device="cuda")
+        L.check(lib.dsv4_ep_expert_forward_p2p(ctypes.byref(d), 0, W, None, 0, p, L.ptr(bases), cap, 7,
+                                               L.ptr(ws), ws.numel(), L.stream_ptr()), "forward")
+        torch.cuda.synchronize()
+        with pytest.raises(RuntimeError, match="exchange flag"):
+            L.raise_on_device_error()
+        x = torch.ones(8, device="cuda")
+        assert float((x * 2).sum()) == 16.0  # the context still works
+    finally:
+        torch.cuda.synchronize()
+        lib.dsv4_ep_exchange_free(p)
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
 
 
-def test_ep_nccl_two_gpus():
-    """Two processes, one GPU each, NCCL all-to-all: every rank's MoE.forward
-    equals the single-GPU layer on its tokens bit for bit."""
+@pytest.mark.parametrize("mode", ["nccl", "peer"])
+def test_ep_two_gpus(mode):
+    """Two processes, one GPU each, exchanging through NCCL all-to-all or
+    through NVLink peer memory: every rank's MoE.forward equals the single-GPU
+    layer on its tokens bit for bit."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=f"{REPO}:{REPO / 'deepseek-v4-flash-dgx-spark_b200'}")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", EP_MODE=mode,
+               PYTHONPATH=f"{REPO}:{REPO / 'deepseek-v4-flash-dgx-spark_b200'}")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
            str(REPO / "tests" / "ep_nccl_worker.py")]
