@@ -345,8 +345,13 @@ def run_ours_ep(args, world, rank, local):
     x = torch.randn(T, cfg.dim, generator=g, device=dev).to(torch.bfloat16)
     lib = _lib.load()
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
-    if args.exchange == "peer":
-        moe.enable_peer_exchange(T)  # collective: every rank, same capacity
+    exchange = args.exchange
+    exchange_note = ""
+    if exchange == "peer":
+        try:
+            moe.enable_peer_exchange(T)  # collective: every rank, same capacity, same outcome
+        except RuntimeError as exc:  # raised on every rank together: all fall back to NCCL
+            exchange, exchange_note = "nccl", f" (peer-memory set-up failed: {exc})"
 
     for _ in range(max(args.warmup, 3)):
         y = ep_moe_forward(moe, x)
@@ -451,7 +456,7 @@ def run_ours_ep(args, world, rank, local):
                    "parallelism": f"ep{world}", "exchange": (
                        "NVLink peer memory: the pack kernel stores FP8 rows into the owners' buffers, the "
                        "return kernel stores bf16 route rows into the sources' (epoch flags, no host sync)"
-                       if args.exchange == "peer" else "NCCL all-to-all") +
+                       if exchange == "peer" else "NCCL all-to-all" + exchange_note) +
                    f"; {rb} B per token and owning rank, {2 * H} B per route",
                    "cuda_graph": False},
         "stage_ms_rank0": dict(zip(["unpack", "plan", "scatter", "gemm1", "gemm2", "return_gather"],
@@ -461,7 +466,7 @@ def run_ours_ep(args, world, rank, local):
                 "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": y.numel() * 2,
                 "ms_per_step": round(e2e_ms, 5),
                 "path": "MoE.forward -> spark_b200.ep (C ABI, " +
-                        ("NVLink peer memory)" if args.exchange == "peer" else "NCCL)")},
+                        ("NVLink peer memory)" if exchange == "peer" else "NCCL)")},
         "clocks": clk,
         "gpu_launches": launches_per_step * args.steps,
     }

@@ -172,15 +172,25 @@ class PeerExchange:
             every = torch.empty(self.world * 64, dtype=torch.uint8, device=self.dev)
             dist.all_gather_into_tensor(every, mine, group=group)
             every = every.cpu().numpy().tobytes()
+            failed = None
             for s in range(self.world):
                 if s == self.rank:
                     continue
                 h = (ctypes.c_uint8 * 64).from_buffer_copy(every[64 * s:64 * (s + 1)])
                 p = ctypes.c_void_p()
-                check(self.lib.dsv4_ipc_open(self.dev.index or 0, h, ctypes.byref(p)), "dsv4_ipc_open")
+                rc = self.lib.dsv4_ipc_open(self.dev.index or 0, h, ctypes.byref(p))
+                if rc != _lib.OK:
+                    failed = f"dsv4_ipc_open of rank {s}'s buffer: status {rc}"
+                    break
                 self._mapped.append(p)
                 bases[s] = p.value
-            dist.barrier(group=group)  # every buffer is mapped everywhere before the first call
+            # every rank learns whether every buffer is mapped everywhere (and
+            # none starts before that): all succeed or all raise, together
+            ok = torch.tensor([0 if failed else 1], dtype=torch.int32, device=self.dev)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+            if int(ok.item()) != 1:
+                self.close()
+                raise RuntimeError(failed or "a peer rank could not map the exchange buffers")
         self.bases = bases
         self.peer_bases = torch.tensor(bases, dtype=torch.int64, device=self.dev)
         self.epoch = 0
