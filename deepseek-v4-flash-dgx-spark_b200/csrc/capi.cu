@@ -948,8 +948,7 @@ int dsv4_ep_expert_forward_p2p(const dsv4_moe_layer* L, int rank, int world, con
   uint8_t* exch = static_cast<uint8_t*>(exchange);
   stage_mark(0, st);
   // every source's rows and counts are in place
-  if ((rc = launch_ep_wait(reinterpret_cast<const int*>(exch), world, epoch,
-                           DSV4_DEVERR_TIMEOUT_PEER, st)))
+  if ((rc = launch_ep_wait(exch, 0, world, epoch, DSV4_DEVERR_TIMEOUT_PEER, st)))
     return rc;
   if ((rc = launch_ep_unpack_p2p(exch, cap_tokens, T_own, k, H, e_begin, e_count, world,
                                  idx_local, w_local, ret_dst, st)))
@@ -986,8 +985,7 @@ int dsv4_ep_combine_p2p(const dsv4_moe_layer* L, int rank, int world, const void
   bind_device(exchange);
   // every owner's return rows are in place (waited for even with no tokens, so
   // the flags of this epoch are consumed in order)
-  if ((rc = launch_ep_wait(reinterpret_cast<const int*>(exch + kEpRetFlagOff), world, epoch,
-                           DSV4_DEVERR_TIMEOUT_PEER, st)))
+  if ((rc = launch_ep_wait(exch, kEpRetFlagOff, world, epoch, DSV4_DEVERR_TIMEOUT_PEER, st)))
     return rc;
   if (T_own == 0) return DSV4_OK;
   if (!ret_pos || !indices || !y || !workspace) return DSV4_ERR_ARG;

@@ -45,12 +45,16 @@ constexpr int kEpMetaEntry = 12;
 //   [32, 64)       int32 ret_flag[8]: = epoch once owner r's return rows are in place
 //   [64, 192)      int32 info[8][4] per source s: rows, routes, offset of its
 //                  return block from this rank in s's return region, unused
+//   [192, 196)     int32 call counter: the epoch of this rank's current call
+//                  when the caller passes epoch 0 (device-side counting, so a
+//                  captured CUDA graph replays with a fresh epoch each time)
 //   [1024, ...)    receive region: source s's rows at s * cap_tokens rows
 //   then           return region: this rank's routes' bf16 output rows
 //                  (cap_tokens * topk rows of H), in owner-rank blocks
 constexpr int kEpHeaderBytes = 1024;
 constexpr int kEpRetFlagOff = 32;
 constexpr int kEpInfoOff = 64;
+constexpr int kEpEpochOff = 192;
 
 long long ep_row_bytes(int H, int k) { return ((long long)H + H / 128 + (long long)kEpMetaEntry * k + 15) / 16 * 16; }
 
@@ -371,13 +375,28 @@ __device__ __forceinline__ int ld_acquire_sys(const int* p) {
   return v;
 }
 
+// The call counter in this rank's own buffer.
+__device__ __forceinline__ int* ep_counter(const uint64_t* bases, int rank) {
+  return reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bases[rank]) + kEpEpochOff);
+}
+
 // Source: after its rows are in every owner's buffer (previous launch), tell
 // owner d how many rows / routes arrived and where their returns go, then
-// raise disp_flag[rank] there.  One lane per destination.
+// raise disp_flag[rank] there.  One lane per destination.  epoch <= 0: this
+// call's epoch is the own call counter plus one (stored back).
 __global__ void ep_signal_dispatch_kernel(const uint64_t* __restrict__ bases, int rank, int world,
                                           const int* __restrict__ send_counts,
                                           const int* __restrict__ dst_base, int epoch) {
   const int d = threadIdx.x;
+  if (epoch <= 0) {
+    int e = 0;
+    if (d == 0) {
+      int* ctr = ep_counter(bases, rank);
+      e = *ctr + 1;
+      *ctr = e;
+    }
+    epoch = __shfl_sync(0xffffffffu, e, 0);
+  }
   if (d >= world) return;
   uint8_t* b = reinterpret_cast<uint8_t*>(bases[d]);
   int* info = reinterpret_cast<int*>(b + kEpInfoOff) + 4 * rank;
@@ -394,17 +413,22 @@ __global__ void ep_signal_return_kernel(const uint64_t* __restrict__ bases, int 
                                         int epoch) {
   const int d = threadIdx.x;
   if (d >= world) return;
+  if (epoch <= 0) epoch = *ep_counter(bases, rank);
   __threadfence_system();
   st_release_sys(reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bases[d]) + kEpRetFlagOff) + rank,
                  epoch);
 }
 
-// Bounded wait until flags[0..world) all equal epoch (one lane per flag).  On
-// timeout the lane records err_code and returns: the kernels that follow then
-// read whatever the buffer holds, the host sees the error.
-__global__ void ep_wait_kernel(const int* __restrict__ flags, int world, int epoch, int err_code) {
+// Bounded wait until the flags at own + flag_off, one per rank, all equal
+// epoch (epoch <= 0: the own call counter).  On timeout the lane records
+// err_code and returns: the kernels that follow then read whatever the buffer
+// holds, the host sees the error.
+__global__ void ep_wait_kernel(const uint8_t* __restrict__ own, int flag_off, int world, int epoch,
+                               int err_code) {
   const int s = threadIdx.x;
   if (s >= world) return;
+  if (epoch <= 0) epoch = *reinterpret_cast<const int*>(own + kEpEpochOff);
+  const int* flags = reinterpret_cast<const int*>(own + flag_off);
   const uint64_t t0 = globaltimer();
   while (ld_acquire_sys(flags + s) != epoch) {
     if (globaltimer() - t0 > kWaitTimeoutNs) {
@@ -548,8 +572,9 @@ int launch_ep_signal_empty(const uint64_t* peer_bases, int rank, int world, int*
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
 
-int launch_ep_wait(const int* flags, int world, int epoch, int err_code, cudaStream_t st) {
-  launch_k(ep_wait_kernel, 1, 32, 0, st, flags, world, epoch, err_code);
+int launch_ep_wait(const uint8_t* own, int flag_off, int world, int epoch, int err_code,
+                   cudaStream_t st) {
+  launch_k(ep_wait_kernel, 1, 32, 0, st, own, flag_off, world, epoch, err_code);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
 

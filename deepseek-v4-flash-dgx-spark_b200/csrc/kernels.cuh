@@ -70,7 +70,8 @@ long long ep_exchange_bytes(int H, int k, int world, int cap);
 long long ep_return_region_off(int H, int k, int world, int cap);
 int launch_ep_signal_empty(const uint64_t* peer_bases, int rank, int world, int* send_counts,
                            uint8_t* ws, int epoch, cudaStream_t st);
-int launch_ep_wait(const int* flags, int world, int epoch, int err_code, cudaStream_t st);
+int launch_ep_wait(const uint8_t* own, int flag_off, int world, int epoch, int err_code,
+                   cudaStream_t st);
 int launch_ep_unpack_p2p(const uint8_t* exch, int cap, int T_own, int k, int H, int e_begin,
                          int e_count, int world, int64_t* idx_local, float* w_local, int* ret_dst,
                          cudaStream_t st);

@@ -193,7 +193,6 @@ class PeerExchange:
                 raise RuntimeError(failed or "a peer rank could not map the exchange buffers")
         self.bases = bases
         self.peer_bases = torch.tensor(bases, dtype=torch.int64, device=self.dev)
-        self.epoch = 0
         self._ws = None
 
     def close(self) -> None:
@@ -255,15 +254,16 @@ def peer_combine(ex: PeerExchange, x, ret_pos, indices, ws, epoch: int):
 
 def ep_forward_peer(ex: PeerExchange, x: torch.Tensor, routing=None) -> torch.Tensor:
     """One expert-parallel layer call over peer memory: no host collective and
-    no host synchronisation.  Every rank must call it once per layer call."""
-    ex.epoch += 1
+    no host synchronisation, so it can be captured in a CUDA graph.  Every
+    rank must call (or replay) it once per layer call; the epochs are counted
+    on the device (epoch 0)."""
     if routing is None:
         weights, indices = ex.moe.gate(x)
     else:
         weights, indices = routing
-    ret_pos, indices = peer_dispatch(ex, x, weights, indices, ex.epoch)
-    ws = peer_expert_forward(ex, x, ex.epoch)
-    return peer_combine(ex, x, ret_pos, indices, ws, ex.epoch)
+    ret_pos, indices = peer_dispatch(ex, x, weights, indices, 0)
+    ws = peer_expert_forward(ex, x, 0)
+    return peer_combine(ex, x, ret_pos, indices, ws, 0)
 
 
 def ep_moe_forward(moe, x: torch.Tensor, routing=None) -> torch.Tensor:

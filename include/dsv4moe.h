@@ -317,7 +317,11 @@ DSV4_API int dsv4_ep_combine(const dsv4_moe_layer* L, int rank, int world, const
  * dsv4_ipc_open, and a device array uint64 peer_bases[W] of every rank's
  * buffer as seen from this GPU (this rank's own at index rank).  cap_tokens
  * bounds the tokens any rank passes per call.  Per layer call, every rank
- * uses the same epoch, a value that differs from the previous call's:
+ * uses the same epoch, a positive value that differs from the previous
+ * call's; or every call of the buffer's life passes epoch 0, and the library
+ * counts calls in the buffer itself (dispatch increments, the other steps
+ * read), which is what a CUDA graph of the three steps needs (every rank
+ * replays it the same number of times):
  *
  *   dsv4_ep_dispatch_p2p       (source)  rows into every owner's buffer, ret_pos
  *   dsv4_ep_expert_forward_p2p (owner)   waits for all W sources, computes,

@@ -190,13 +190,16 @@ def _emulated_peer_ep(moe, xs, routings, W, epochs=(1, 2)):
     return out
 
 
-@pytest.mark.parametrize("name,W,tokens", [("cpu_ref", 2, (9, 4)), ("cpu_ref", 4, (1, 0, 40, 300)),
-                                           ("decode", 8, (64, 64, 64, 64, 64, 64, 64, 64)),
-                                           ("decode", 2, (1100, 7))])
-def test_emulated_peer_ep_is_bit_identical_to_single_gpu(cuda_device, name, W, tokens):
+@pytest.mark.parametrize("name,W,tokens,epochs", [("cpu_ref", 2, (9, 4), (1, 2)),
+                                                  ("cpu_ref", 4, (1, 0, 40, 300), (1, 2)),
+                                                  ("cpu_ref", 4, (1, 0, 40, 300), (0, 0, 0)),
+                                                  ("decode", 8, (64, 64, 64, 64, 64, 64, 64, 64), (0, 0)),
+                                                  ("decode", 2, (1100, 7), (1, 2))])
+def test_emulated_peer_ep_is_bit_identical_to_single_gpu(cuda_device, name, W, tokens, epochs):
     """Dispatch rows stored into the owners' exchange buffers, return rows into
-    the sources', epoch flags in both directions: every rank's result equals
-    the single-GPU layer bit for bit, on two consecutive calls (buffer reuse)."""
+    the sources', epoch flags in both directions (epochs given by the host, or
+    0: counted on the device): every rank's result equals the single-GPU layer
+    bit for bit, on consecutive calls (buffer reuse)."""
     from spark_b200.synthetic import CONFIGS, build_moe, make_layer
 
     cfg = CONFIGS[name].with_tokens(max(tokens))
@@ -211,7 +214,7 @@ def test_emulated_peer_ep_is_bit_identical_to_single_gpu(cuda_device, name, W, t
                                         torch.empty(0, k, dtype=torch.int64, device=cuda_device))
         xs.append(x.contiguous())
         routings.append((w.float().contiguous(), idx.to(torch.int64).contiguous()))
-    runs = _emulated_peer_ep(moe, xs, routings, W)
+    runs = _emulated_peer_ep(moe, xs, routings, W, epochs)
     for ys in runs:
         for r, (x, (w, idx)) in enumerate(zip(xs, routings)):
             if x.shape[0] == 0:
