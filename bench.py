@@ -49,7 +49,9 @@ def _parse():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--workload", default="decode", choices=["decode", "prefill"])
+    p.add_argument("--workload", default="decode", choices=["decode", "prefill", "stack"],
+                   help="stack: the full-depth MoE-only decode stack (--layers layers, bf16 residual)")
+    p.add_argument("--layers", type=int, default=43)
     p.add_argument("--tokens", type=int, default=None)
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -504,6 +506,152 @@ def run_ours_ep(args, world, rank, local):
     return result, cfg, layer, moe
 
 
+def run_stack(args, world, rank, local):
+    """Full-depth MoE-only decode stack: ``--layers`` distinct seeded layers
+    (seed = layer id; H=4096, 256 experts top-6 + shared, I=2048, FP4 routed /
+    FP8 shared), every expert of every layer resident in HBM (with N GPUs each
+    rank holds its E/N experts per layer and the layers run expert-parallel over
+    NVLink peer memory).  One step = T tokens per GPU through every layer,
+    x <- x + MoE_l(rms_norm(x)) in bf16, the whole step one CUDA graph per rank."""
+    import torch
+    import torch.distributed as dist
+
+    from spark_b200 import _lib
+    from spark_b200.moe import packed_block_bytes
+    from spark_b200.synthetic import CONFIGS, build_moe, make_layer
+
+    dev = torch.device("cuda", local)
+    T = args.tokens or 8
+    cfg = CONFIGS["decode"].with_tokens(T)
+    H, I, E = cfg.dim, cfg.inter, cfg.n_routed
+    block = packed_block_bytes(H, I)
+    shared_bytes = 3 * I * H + 3 * (I // 128) * (H // 128)
+    per_layer = (E // world) * (block + 3 * I * H // 32) + shared_bytes + E * H * 2
+    free, _total = torch.cuda.mem_get_info(dev)
+    if per_layer * args.layers * 1.03 + (4 << 30) > free:
+        raise RuntimeError(f"{args.layers} layers need {per_layer * args.layers / 2**30:.0f} GiB per GPU, "
+                           f"{free / 2**30:.0f} GiB free")
+    lib = _lib.load()
+    layers = []
+    for l in range(args.layers):
+        lay = make_layer(cfg, seed=l, device=dev)
+        moe = build_moe(lay, device=dev, layer_id=l)
+        del lay
+        if world > 1:
+            moe.enable_peer_exchange(T)
+        layers.append(moe)
+    torch.cuda.synchronize()
+    g = torch.Generator(device=dev).manual_seed(args.seed + 1000 * (rank + 1))
+    x0 = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    ws = torch.empty(max(layers[0].workspace_bytes(T), 1), dtype=torch.uint8, device=dev) if world == 1 else None
+
+    def layer_out(moe, x):
+        if world == 1:
+            return moe.forward_tokens(x, workspace=ws)
+        from spark_b200.ep import ep_moe_forward
+
+        return ep_moe_forward(moe, x)
+
+    def rms_norm(x):
+        # the block's pre-MoE normalisation without learned weights: keeps the
+        # residual stream from drifting into a few shared directions, so the
+        # routing stays as diverse as a real stack's
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
+
+    # eager pass: the experts each layer touches (all ranks' tokens), for the bytes count
+    touched = 0
+    x = x0.clone()
+    for moe in layers:
+        h = rms_norm(x)
+        idx = moe.gate(h)[1].to(torch.int64).reshape(-1)
+        if world > 1:
+            every = torch.empty(world * idx.numel(), dtype=torch.int64, device=dev)
+            dist.all_gather_into_tensor(every, idx)
+            idx = every[(every >= moe.experts_start_idx) & (every < moe.experts_end_idx)]
+        touched += int(torch.unique(idx).numel())
+        x = x + layer_out(moe, h)
+    torch.cuda.synchronize()
+    _lib.raise_on_device_error()
+
+    xs = x0.clone()
+
+    def step():
+        xs.copy_(x0)
+        for moe in layers:
+            xs.add_(layer_out(moe, rms_norm(xs)))
+
+    for _ in range(max(args.warmup, 2)):
+        step()
+    torch.cuda.synchronize()
+    s_cap = torch.cuda.Stream(device=dev)
+    s_cap.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    n0 = lib.dsv4_kernel_launches()
+    with torch.cuda.graph(graph, stream=s_cap):
+        step()
+    launches_per_step = lib.dsv4_kernel_launches() - n0
+    torch.cuda.current_stream().wait_stream(s_cap)
+    graph.replay()
+    torch.cuda.synchronize()
+    _lib.raise_on_device_error()
+
+    times = []
+    clocks = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    for _ in range(args.steps):
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    _lib.raise_on_device_error()
+    ms = sum(times) / len(times)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    peaks, peak_src = _peaks()
+    bytes_step = touched * block + args.layers * (shared_bytes + E * H * 2 + 4 * T * H)
+    achieved = bytes_step / (ms * 1e-3) / 1e9
+    del graph
+    for moe in layers:
+        if getattr(moe, "peer_exchange", None) is not None:
+            torch.cuda.synchronize()
+            dist.barrier()
+            moe.peer_exchange.close()
+            moe.peer_exchange = None
+    result = {
+        "metric": METRIC, "value": round(world * T / (ms * 1e-3), 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "e2m1/e4m3 x e4m3 -> f32 (bf16 out)",
+        "data": "synthetic (seeded per layer; random-init weights of the V4-Flash MoE shapes)",
+        "config": {"workload": f"moe_stack_{args.layers}_layers_decode", "tokens_per_gpu": T, "hidden": H,
+                   "inter": I, "routed_experts": E, "topk": cfg.topk, "shared_experts": 1,
+                   "layers": args.layers, "experts_resident_per_gpu": args.layers * (E // world),
+                   "rank0_experts_touched_per_step": touched, "residual": "bf16, x += MoE_l(rms_norm(x)) (weight-free pre-norm)",
+                   "l2": f"not flushed: a step streams {bytes_step / 1e9:.1f} GB, far above the 126 MB L2",
+                   "parallelism": "single" if world == 1 else f"ep{world} over NVLink peer memory",
+                   "cuda_graph": True},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                     "kernel": "whole step (rank 0): touched experts + shared + gate bytes of every layer",
+                     "algorithmic_bytes": bytes_step, "peak_source": peak_src},
+        "clocks": clk,
+        "gpu_launches": launches_per_step * args.steps,
+    }
+    return result
+
+
 def _sweep(args, local):
     """Other decode batch sizes and the prefill layer, short runs."""
     import torch
@@ -630,6 +778,9 @@ def cpu_layer_rate(cfg_name: str, sample_tokens: int, seed: int, threads: int | 
 def run_reference(args, world, rank):
     if rank != 0:
         return None
+    if args.workload == "stack":  # the oracle's per-layer rate already bounds it: layers x one layer
+        return {"impl": "reference", "unavailable": "the full-depth stack has no CPU arm of its own; "
+                "the per-layer CPU rate is the decode workload's reference line"}
     import torch
 
     threads = os.cpu_count() or 1
@@ -664,6 +815,16 @@ def main():
             print(json.dumps(res), flush=True)
         return
     world, rank, local = _dist_init(args.gpus)
+    if args.workload == "stack":
+        res = run_stack(args, world, rank, local)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     res, cfg, layer, moe = run_ours(args, world, rank, local)
     del moe, layer
     if rank == 0 and world == 1:
