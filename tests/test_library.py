@@ -73,3 +73,49 @@ def test_check_maps_codes_to_reference_messages():
     with pytest.raises(RuntimeError, match="source slice exceeds storage tensor"):
         _lib.check(_lib.ERR_BOUNDS)
     _lib.check(_lib.OK)
+
+
+def test_peer_exchange_sizes_and_argument_checks():
+    """Host-side checks of the peer-memory expert-parallel entry points (no GPU:
+    every case returns before a CUDA call)."""
+    from spark_b200 import _lib
+
+    lib = _lib.load()
+    H, k = 4096, 6
+    rb = lib.dsv4_ep_row_bytes(H, k)
+    for W, cap in ((2, 64), (8, 64), (8, 4096)):
+        n = lib.dsv4_ep_exchange_bytes(H, k, W, cap)
+        recv = (W * cap * rb + 255) // 256 * 256
+        ret = (cap * k * H * 2 + 255) // 256 * 256
+        assert n == 1024 + recv + ret
+    # unsupported shapes / capacities
+    assert lib.dsv4_ep_exchange_bytes(H, k, 9, 64) == -1          # more than 8 ranks
+    assert lib.dsv4_ep_exchange_bytes(1000, k, 2, 64) == -1       # hidden not a multiple of 512
+    assert lib.dsv4_ep_exchange_bytes(H, k, 2, 0) == -1           # no capacity
+    assert lib.dsv4_ep_exchange_bytes(H, k, 2, 1 << 22) == -1     # return rows beyond the 24-bit index
+    assert lib.dsv4_ep_p2p_dispatch_workspace_bytes(-1, 2) == -1
+    assert lib.dsv4_ep_p2p_dispatch_workspace_bytes(64, 2) > 0
+    p = ctypes.c_void_p()
+    assert lib.dsv4_ep_exchange_alloc(0, 0, ctypes.byref(p)) == _lib.ERR_ARG
+    assert lib.dsv4_ep_exchange_alloc(-1, 1024, ctypes.byref(p)) == _lib.ERR_ARG
+    assert lib.dsv4_ipc_handle(None, None) == _lib.ERR_ARG
+    assert lib.dsv4_ipc_open(0, None, ctypes.byref(p)) == _lib.ERR_ARG
+    assert lib.dsv4_ep_exchange_free(None) == _lib.OK and lib.dsv4_ipc_close(None) == _lib.OK
+    fake = ctypes.c_void_p(0x1000)
+    ws = ctypes.c_void_p(0x2000)
+    args = dict(x=fake, idx=fake, w=fake, T=4, H=H, k=k, E=256, W=2, rank=0, bases=fake, cap=4, epoch=1,
+                ret=fake, ws=ws, wsb=1 << 20, st=None)
+
+    def dispatch(**kw):
+        a = dict(args, **kw)
+        return lib.dsv4_ep_dispatch_p2p(a["x"], a["idx"], a["w"], a["T"], a["H"], a["k"], a["E"], a["W"],
+                                        a["rank"], a["bases"], a["cap"], a["epoch"], a["ret"], a["ws"],
+                                        a["wsb"], a["st"])
+
+    assert dispatch(rank=2) == _lib.ERR_ARG              # rank outside the world
+    assert dispatch(W=9) == _lib.ERR_ARG                 # more than 8 ranks
+    assert dispatch(T=5) == _lib.ERR_ARG                 # more tokens than the exchange holds
+    assert dispatch(E=255) == _lib.ERR_ARG               # experts do not divide over the ranks
+    assert dispatch(bases=None) == _lib.ERR_ARG          # no peer table
+    assert dispatch(wsb=16) == _lib.ERR_WORKSPACE        # workspace too small
+    assert dispatch(x=None) == _lib.ERR_ARG              # tokens but no input
