@@ -234,6 +234,9 @@ class ExpertArena:
         n = max(self.max_slots, 1)
         self.buffer = torch.zeros(n * self.slot_stride, dtype=torch.uint8, device=self.device)
         self.sf = torch.zeros(n * self.sf_stride, dtype=torch.uint8, device=self.device)
+        from .telemetry import expert_telemetry
+
+        expert_telemetry().register_resident(max_slots, self.buffer.numel() + self.sf.numel())
         self._free = list(range(self.max_slots - 1, -1, -1))
         self._experts: dict[int, Expert] = {}
         self._released: set[int] = set()
@@ -290,6 +293,9 @@ class ExpertArena:
                                            ptr(self.buffer), self.slot_stride, ptr(self.sf), self.sf_stride,
                                            ptr(bf16_out), bf16_stride, stream_ptr(stream)),
               "dsv4_materialize")
+        from .telemetry import expert_telemetry
+
+        expert_telemetry().record_materialize(n * self.block_bytes)
         return n * self.block_bytes
 
 
@@ -493,6 +499,18 @@ class MoE(nn.Module):
             x2 = x2.to(torch.bfloat16)
         x2 = x2.contiguous()
         routing = self.gate(x2, input_ids) if self.gate.hashed else None
+        from .telemetry import expert_telemetry
+
+        tel = expert_telemetry()
+        if tel.route_trace_path is not None:
+            # the reference's route trace needs this call's routing on the host;
+            # the layer then runs on exactly that routing
+            if routing is None:
+                routing = self.gate(x2, input_ids)
+            ids = input_ids if input_ids is not None else torch.empty(0, dtype=torch.int64)
+            tel.record_routing(layer_id=self.layer_id, input_ids=ids, expert_indices=routing[1])
+        else:
+            tel.count_routing(x2.shape[0], x2.shape[0] * self.n_activated_experts)
         if self.world == 1:
             y = self.forward_tokens(x2, routing=routing)
         else:

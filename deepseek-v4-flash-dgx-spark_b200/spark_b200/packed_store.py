@@ -215,7 +215,11 @@ class PackedExpertStore:
             got = self._native_module.read_into(self._fd(path), buf[o:o + size], size, offset)
             if got != size:
                 raise RuntimeError("short packed expert read")
-        return buf, offs, time.monotonic() - t0
+        dt = time.monotonic() - t0
+        from .telemetry import expert_telemetry
+
+        expert_telemetry().record_packed_read(len(experts), sum(e[2] for e in entries), dt)
+        return buf, offs, dt
 
     def upload_experts(self, layer_id: int, experts: list[int], arena: ExpertArena, slots: list[int], *,
                        bf16_out: torch.Tensor | None = None, stream=None) -> dict[str, float]:

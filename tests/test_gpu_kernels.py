@@ -524,3 +524,35 @@ def test_pair_gemm_bit_identical_to_single_cta_gemm(cuda_device, tmp_path, T):
     form runs in its own process."""
     a, b = _layer_bits_under_env(tmp_path, "cpu_ref", T, [{"DSV4_BLOCK_N": "256"}, {"DSV4_BLOCK_N": "128"}])
     assert np.array_equal(a, b)
+
+
+def test_moe_forward_writes_the_route_trace(cuda_device, tmp_path):
+    """With the reference's route-trace variable set, MoE.forward appends one
+    expert_route line per call holding the gate's routing, and its output is
+    bit-identical to the untraced call."""
+    import json
+
+    from spark_b200 import telemetry as tm
+    from spark_b200.synthetic import CONFIGS, build_moe, make_layer
+
+    cfg = CONFIGS["cpu_ref"].with_tokens(6)
+    layer = make_layer(cfg, seed=1)
+    moe = build_moe(layer, device=cuda_device)
+    x = layer["x"].view(2, 3, cfg.dim).to(cuda_device)
+    ids = torch.arange(6, device=cuda_device).view(2, 3)
+    tm.set_expert_telemetry(tm.ExpertTelemetry(None))
+    try:
+        y_plain = moe(x, ids)
+        tm.set_expert_telemetry(tm.ExpertTelemetry(tmp_path / "routes.jsonl"))
+        y = moe(x, ids)
+        torch.cuda.synchronize()
+        assert torch.equal(y.view(torch.int16), y_plain.view(torch.int16))
+        lines = (tmp_path / "routes.jsonl").read_text().splitlines()
+        assert len(lines) == 1
+        d = json.loads(lines[0])
+        _, idx = moe.gate(x.view(-1, cfg.dim), ids.view(-1))
+        assert d["event"] == "expert_route" and d["layer_id"] == moe.layer_id
+        assert d["token_ids"] == list(range(6)) and d["token_count"] == 6
+        assert d["expert_indices"] == idx.cpu().tolist() and d["activation_count"] == 6 * cfg.topk
+    finally:
+        tm.set_expert_telemetry(None)
