@@ -196,6 +196,10 @@ class PeerExchange:
         self._ws = None
 
     def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's.  Peers store into this
+        buffer during their calls, so every rank must have finished its last
+        layer call first: synchronise the device and pass a process-group
+        barrier on every rank before any rank closes."""
         for p in self._mapped:
             self.lib.dsv4_ipc_close(p)
         self._mapped = []
