@@ -55,6 +55,9 @@ def _parse():
     p.add_argument("--tokens", type=int, default=None)
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-parity", action="store_true", help="skip the output check against the oracle")
+    p.add_argument("--no-config4", action="store_true",
+                   help="N>1: skip the 4096-token/GPU expert-parallel measurements after the headline")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                    help="expert-parallel exchange (N>1): NVLink peer memory from the kernels, or NCCL all-to-all")
@@ -149,6 +152,31 @@ def _traffic_record(workload: str):
         return None
 
 
+def _parity_block(layer, x_rows, y_rows, w_rows, i_rows):
+    """Checker, outside every timed region: the layer outputs of a few tokens
+    against the oracle restatement on the device's own routing (tokens are
+    independent, so only the experts they touch are decoded).  The oracle
+    only checks here; nothing it computes is measured or returned as output."""
+    import numpy as np
+
+    from oracle import moe_oracle as O
+
+    cfg = layer["cfg"]
+    x_rows, y_rows = x_rows.float().cpu().numpy(), y_rows.float().cpu().numpy()
+    w_rows, i_rows = w_rows.float().cpu().numpy(), i_rows.cpu().numpy().astype(np.int64)
+    experts = sorted(set(int(e) for e in i_rows.reshape(-1).tolist()))
+    mw = O.MoEWeights(
+        gate_w=None, gate_bias=None,
+        experts={e: O.expert_from_block(layer["blocks"][e].cpu().numpy(), cfg.dim, cfg.inter) for e in experts},
+        shared=O.shared_from_tensors({k: v.cpu().numpy() for k, v in layer["shared"].items()}),
+        topk=cfg.topk, route_scale=cfg.route_scale, swiglu_limit=cfg.swiglu_limit)
+    ref = O.moe_forward(x_rows, mw, routing=(w_rows, i_rows), workers=min(16, os.cpu_count() or 1))[0]
+    err = float(np.max(np.abs(y_rows.astype(np.float64) - ref)) / (np.sqrt(np.mean(ref.astype(np.float64) ** 2))
+                                                                  + 1e-30))
+    return {"checked_tokens": int(x_rows.shape[0]), "experts": len(experts), "max_err_rms": round(err, 6),
+            "tol": 2e-2, "ok": bool(err <= 2e-2), "against": "oracle restatement on the device's routing"}
+
+
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
@@ -206,6 +234,15 @@ def run_ours(args, world, rank, local):
     graph_prof.replay()
     torch.cuda.synchronize()
     lib.dsv4_profile_enable(0)
+
+    # output parity of a sample of tokens (checker, before the timed region)
+    parity = None
+    if not args.no_parity:
+        y_chk = moe.forward_tokens(x, workspace=ws)
+        w_chk, i_chk = moe.gate(x)
+        torch.cuda.synchronize()
+        pick = torch.arange(0, T, max(1, T // 8), device=dev)[:8]
+        parity = _parity_block(layer, x[pick], y_chk[pick], w_chk[pick], i_chk[pick])
 
     # touched experts of this batch (for the algorithmic-bytes count)
     offs = (ctypes.c_longlong * 17)()
@@ -320,6 +357,8 @@ def run_ours(args, world, rank, local):
         "clocks": clk,
         "gpu_launches": launches_per_step * args.steps,
     }
+    if parity is not None:
+        result["parity"] = parity
     return result, cfg, layer, moe
 
 
@@ -359,6 +398,7 @@ def run_ours_ep(args, world, rank, local):
         y = ep_moe_forward(moe, x)
     torch.cuda.synchronize()
     _lib.raise_on_device_error()
+    parity = _ep_parity(args, moe, layer, x, world, rank, dev) if not args.no_parity else None
     n0 = lib.dsv4_kernel_launches()
     y = ep_moe_forward(moe, x)
     launches_per_step = lib.dsv4_kernel_launches() - n0
@@ -497,13 +537,149 @@ def run_ours_ep(args, world, rank, local):
         "clocks": clk,
         "gpu_launches": launches_per_step * args.steps,
     }
+    if parity is not None:
+        result["parity"] = parity
     del graph
     if getattr(moe, "peer_exchange", None) is not None:
         torch.cuda.synchronize()
         dist.barrier()  # no rank frees its buffer while a peer could still store into it
         moe.peer_exchange.close()
         moe.peer_exchange = None
+    if args.workload == "decode" and not args.no_config4:
+        del moe, layer
+        torch.cuda.empty_cache()
+        result["config4"] = _ep_config4(args, world, rank, local)
+        return result, cfg, None, None
     return result, cfg, layer, moe
+
+
+def _ep_parity(args, moe, layer, x, world, rank, dev):
+    """Checker, before the timed region: a few tokens of every rank (their
+    inputs, expert-parallel outputs and routing) gathered to rank 0 and
+    compared with the oracle there.  Every rank takes the same collective
+    steps; the other ranks wait at the barrier while rank 0 checks."""
+    import torch
+    import torch.distributed as dist
+
+    from spark_b200.ep import ep_moe_forward
+
+    T, H = x.shape
+    y = ep_moe_forward(moe, x)
+    w, idx = moe.gate(x)
+    n = min(T, 4 if world <= 2 else 2)
+    pick = torch.arange(0, T, max(1, T // n), device=dev)[:n]
+    parts = {"x": x[pick].contiguous(), "y": y[pick].contiguous(), "w": w[pick].float().contiguous(),
+             "i": idx[pick].to(torch.int64).contiguous()}
+    gathered = {}
+    for key, t in parts.items():
+        g = torch.empty((world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=dev)
+        dist.all_gather_into_tensor(g, t)
+        gathered[key] = g
+    torch.cuda.synchronize()
+    res = None
+    if rank == 0:
+        res = _parity_block(layer, gathered["x"], gathered["y"], gathered["w"], gathered["i"])
+        res["ranks"] = world
+    dist.barrier()
+    return res
+
+
+def _ep_config4(args, world, rank, local):
+    """The expert-parallel layer at 4096 tokens per GPU (256 experts split over
+    the ranks, top-6, FP4 routed experts, FP8 dispatch rows with per-128
+    scales, bf16 return rows), with uniform and Zipf(1.2) routing; measured
+    after the headline, outside its timed region.  Per routing: the layer time
+    (CUDA events, max over ranks), tokens/s, the bytes each GPU stores into
+    its peers (dispatch rows to remote owners + return rows to remote
+    sources) and the resulting NVLink GB/s per direction against the measured
+    770 GB/s peer copy, and the routed rows per GPU (max / mean: the load
+    imbalance the even expert split gives)."""
+    import torch
+    import torch.distributed as dist
+
+    from spark_b200 import _lib
+    from spark_b200.ep import ep_moe_forward
+    from spark_b200.synthetic import CONFIGS, build_moe, make_layer
+
+    dev = torch.device("cuda", local)
+    lib = _lib.load()
+    T = 4096
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    out = {"tokens_per_gpu": T, "nvlink_peer_copy_gbs": 770.0}
+    for routing, base in (("uniform", "decode"), ("zipf1.2", "prefill")):
+        cfg = CONFIGS[base].with_tokens(T)
+        layer = make_layer(cfg, seed=args.seed + 77, device=dev)
+        moe = build_moe(layer, device=dev)
+        del layer
+        g = torch.Generator(device=dev).manual_seed(args.seed + 5000 + rank)
+        x = torch.randn(T, cfg.dim, generator=g, device=dev).to(torch.bfloat16)
+        exchange = "peer"
+        try:
+            moe.enable_peer_exchange(T)
+        except RuntimeError:
+            exchange = "nccl"
+        for _ in range(3):
+            ep_moe_forward(moe, x)
+        torch.cuda.synchronize()
+        _lib.raise_on_device_error()
+        idx = moe.gate(x)[1].to(torch.int64).contiguous()
+        every = torch.empty(world * idx.numel(), dtype=torch.int64, device=dev)
+        dist.all_gather_into_tensor(every, idx.view(-1))
+        graph = None
+        if exchange == "peer":
+            s_cap = torch.cuda.Stream(device=dev)
+            s_cap.wait_stream(torch.cuda.current_stream())
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s_cap):
+                ep_moe_forward(moe, x)
+            torch.cuda.current_stream().wait_stream(s_cap)
+            graph.replay()
+            torch.cuda.synchronize()
+        times = []
+        for _ in range(10):
+            flush.fill_(1)
+            dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            if graph is not None:
+                graph.replay()
+            else:
+                ep_moe_forward(moe, x)
+            e1.record()
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        _lib.raise_on_device_error()
+        t = torch.tensor([statistics.median(times)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        # traffic and load from every rank's routing (host arithmetic)
+        e_per = cfg.n_routed // world
+        own = (every.view(world, T, cfg.topk) // e_per).cpu()
+        row_b = int(lib.dsv4_ep_row_bytes(cfg.dim, cfg.topk))
+        out_b, routes = [], []
+        for r in range(world):
+            rows_out = sum(int((own[r] == d).any(dim=1).sum()) for d in range(world) if d != r)
+            ret_out = int(((own == r).sum(dim=2)[[s for s in range(world) if s != r]]).sum())
+            out_b.append(rows_out * row_b + ret_out * 2 * cfg.dim)
+            routes.append(int((own == r).sum()))
+        max_out = max(out_b)
+        del graph
+        if getattr(moe, "peer_exchange", None) is not None:
+            torch.cuda.synchronize()
+            dist.barrier()
+            moe.peer_exchange.close()
+            moe.peer_exchange = None
+        del moe, x
+        torch.cuda.empty_cache()
+        out[routing] = {
+            "ms": round(ms, 4), "tokens_per_s": round(world * T / (ms * 1e-3), 1), "exchange": exchange,
+            "bytes_out_per_gpu_max": max_out, "nvlink_gbs_per_direction": round(max_out / (ms * 1e-3) / 1e9, 1),
+            "nvlink_frac_of_peer_copy": round(max_out / (ms * 1e-3) / 1e9 / 770.0, 4),
+            "routed_rows_per_gpu_max": max(routes), "routed_rows_per_gpu_mean": round(sum(routes) / world, 1),
+            "imbalance_max_over_mean": round(max(routes) * world / max(sum(routes), 1), 3),
+            "expert_tflops_per_gpu_max": round((max(routes) + T) * 6.0 * cfg.dim * cfg.inter / (ms * 1e-3) / 1e12, 1),
+        }
+    return out
 
 
 def run_stack(args, world, rank, local):
@@ -682,11 +858,96 @@ def _sweep(args, local):
             e1.synchronize()
             ts.append(e0.elapsed_time(e1))
         ms = statistics.median(ts)
-        out[f"{wl}_T{T}"] = {"ms": round(ms, 4), "tokens_per_s": round(T / (ms * 1e-3), 1)}
+        entry = {"ms": round(ms, 4), "tokens_per_s": round(T / (ms * 1e-3), 1)}
+        if wl == "prefill":
+            entry["roofline"] = _prefill_roofline(moe, layer, ws, y, flush, cfg, T)
+        out[f"{wl}_T{T}"] = entry
         del moe, layer, ws, y
         torch.cuda.empty_cache()
     out.update(_materializer(args, dev, flush))
+    out["upload_32_experts"] = _upload_rate(args, dev)
     return out
+
+
+def _upload_rate(args, dev):
+    """The slab upload path (packed_store.upload_experts): 32 packed expert
+    blocks of the decode shapes (428 MB) written in the reference's layout to a
+    temporary directory, then pread in chunks of 8 into reused pinned staging,
+    copied to the device on a copy stream and materialized into a 32-slot arena,
+    the three stages overlapped.  The file was just written, so it is read
+    from the page cache: the figure is the host-memory -> HBM pipeline, not a
+    disk.  Beside it, one plain pinned -> device copy of the same bytes (the
+    PCIe ceiling of this host)."""
+    import tempfile
+
+    import torch
+
+    from spark_b200.moe import ExpertArena
+    from spark_b200.packed_store import PackedExpertStore, write_packed_layout
+    from spark_b200.synthetic import routed_blocks
+
+    H, I, n = 4096, 2048, 32
+    blocks = routed_blocks(n, H, I, args.seed + 17)
+    with tempfile.TemporaryDirectory() as tmp:
+        write_packed_layout(Path(tmp), {0: {e: blocks[e].numpy() for e in range(n)}}, H, I)
+        store = PackedExpertStore(Path(tmp) / "layout.json")
+        arena = ExpertArena(n, H, I, device=dev)
+        store.upload_experts(0, list(range(n)), arena, list(range(n)))  # warm: staging, rings, page cache
+        runs = [store.upload_experts(0, list(range(n)), arena, list(range(n))) for _ in range(3)]
+        store.close()
+    best = max(runs, key=lambda r: r["upload_gbs"])
+    host = blocks.reshape(-1).pin_memory()
+    devbuf = torch.empty_like(host, device=dev)
+    ts = []
+    for _ in range(3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        devbuf.copy_(host, non_blocking=True)
+        e1.record()
+        e1.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    h2d = host.numel() / (min(ts) * 1e-3) / 1e9
+    del arena, devbuf
+    torch.cuda.empty_cache()
+    return {"bytes": int(best["packed_read_bytes"]), "upload_gbs": round(best["upload_gbs"], 2),
+            "pread_seconds": round(best["packed_read_seconds"], 4), "wall_seconds": round(best["upload_seconds"], 4),
+            "plain_pinned_h2d_gbs": round(h2d, 2), "frac_of_h2d": round(best["upload_gbs"] / h2d, 3),
+            "source": "page-cache resident file, chunks of 8 experts"}
+
+
+def _prefill_roofline(moe, layer, ws, y, flush, cfg, T):
+    """Tensor roofline of the prefill layer's expert GEMMs: their algorithmic
+    FLOPs (T*(k+1)*3*2*H*I) over the GEMM1 + GEMM2 time taken by the library's
+    stage events on the launching stream (median of 5, L2 flushed between),
+    against the dense FP8 rate (what kind::mxf8f6f4 with e4m3 activations
+    runs at) and the dense FP4 rate, both scaled from the measured bf16 peak
+    by the nominal dense ratios (FP8 = 2x, FP4 = 4x bf16)."""
+    import torch
+
+    from spark_b200 import _lib
+    from spark_b200.synthetic import algorithmic_flops
+
+    lib = _lib.load()
+    lib.dsv4_profile_enable(1)
+    buf = (ctypes.c_float * 6)()
+    gemm = []
+    for _ in range(5):
+        flush.fill_(1)
+        moe.forward_tokens(layer["x"], workspace=ws, out=y)
+        torch.cuda.synchronize()
+        lib.dsv4_profile_read(buf, 6)
+        gemm.append(buf[3] + buf[4])
+    lib.dsv4_profile_enable(0)
+    gemm_ms = statistics.median(gemm)
+    flops = algorithmic_flops(cfg, T) - 2.0 * T * cfg.dim * cfg.n_routed
+    achieved = flops / (gemm_ms * 1e-3) / 1e12
+    peaks, src = _peaks()
+    bf16 = peaks.get("bf16_tflops", 1590.0)
+    return {"bound": "tensor", "achieved": round(achieved, 1), "unit": "TFLOP/s", "algorithmic_flops": flops,
+            "kernel_ms": round(gemm_ms, 4), "peak_fp8": round(2 * bf16, 1), "frac_fp8": round(achieved / (2 * bf16), 4),
+            "peak_fp4": round(4 * bf16, 1), "frac_fp4": round(achieved / (4 * bf16), 4),
+            "kernel": "expert_gemm_kernel (GEMM1 + GEMM2), kind::mxf8f6f4 (e4m3 x e2m1, FP8 rate)",
+            "peak_source": f"{src} bf16 x2 (FP8) / x4 (FP4), nominal dense ratios"}
 
 
 def _materializer(args, dev, flush):

@@ -421,6 +421,14 @@ int dsv4_device_error(int clear, int* code) {
   return DSV4_OK;
 }
 
+int dsv4_device_error_async(int* dst, void* stream) {
+  if (!dst) return DSV4_ERR_ARG;
+  return cudaMemcpyFromSymbolAsync(dst, g_dsv4_device_error, sizeof(int), 0, cudaMemcpyDefault,
+                                   static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? DSV4_OK
+             : DSV4_ERR_CUDA;
+}
+
 int dsv4_profile_enable(int enable) {
   // The events are created once and never destroyed: a CUDA graph captured
   // with profiling on keeps recording them whenever it is replayed, so they

@@ -510,14 +510,9 @@ static int launch_one(const CUtensorMap& a0, const CUtensorMap& a1, const CUtens
                       const CUtensorMap& s1, const CUtensorMap& b, const GemmArgs& args, int grid,
                       cudaStream_t st) {
   using C = GemmCfg<BM, GATED>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(expert_gemm_kernel<BM, GATED>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)C::SMEM_BYTES) != cudaSuccess)
-      return DSV4_ERR_CUDA;
-    attr_set = true;
-  }
+  if (ensure_smem_attr(reinterpret_cast<const void*>(expert_gemm_kernel<BM, GATED>),
+                       (int)C::SMEM_BYTES))
+    return DSV4_ERR_CUDA;
   launch_k(expert_gemm_kernel<BM, GATED>, grid, 192, C::SMEM_BYTES, st,
            a0, a1, s0, s1, b, args);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;

@@ -399,16 +399,14 @@ int pair_clusters_resident(bool gated) {
   int n = 0;
   if (gated) {
     cfg.dynamicSmemBytes = PairCfg<true>::SMEM_BYTES;
-    if (cudaFuncSetAttribute(expert_gemm_pair_kernel<true>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)PairCfg<true>::SMEM_BYTES) != cudaSuccess ||
+    if (ensure_smem_attr(reinterpret_cast<const void*>(expert_gemm_pair_kernel<true>),
+                         (int)PairCfg<true>::SMEM_BYTES) ||
         cudaOccupancyMaxActiveClusters(&n, expert_gemm_pair_kernel<true>, &cfg) != cudaSuccess)
       n = 0;
   } else {
     cfg.dynamicSmemBytes = PairCfg<false>::SMEM_BYTES;
-    if (cudaFuncSetAttribute(expert_gemm_pair_kernel<false>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)PairCfg<false>::SMEM_BYTES) != cudaSuccess ||
+    if (ensure_smem_attr(reinterpret_cast<const void*>(expert_gemm_pair_kernel<false>),
+                         (int)PairCfg<false>::SMEM_BYTES) ||
         cudaOccupancyMaxActiveClusters(&n, expert_gemm_pair_kernel<false>, &cfg) != cudaSuccess)
       n = 0;
   }

@@ -257,14 +257,14 @@ int launch_gate_logits(const void* x, const void* w, int w_is_fp32, int T, int H
   const int grid = (E + kGateEPC - 1) / kGateEPC;
   const size_t smem = (size_t)kGateEPC * H * sizeof(float);
   if (w_is_fp32) {
-    cudaFuncSetAttribute(gate_logits_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
+    if (ensure_smem_attr(reinterpret_cast<const void*>(gate_logits_kernel<true>), (int)smem))
+      return DSV4_ERR_CUDA;
     launch_k(gate_logits_kernel<true>, grid, kGateThreads, smem, st,
              static_cast<const __nv_bfloat16*>(x), w, T,
                                                       H, E, logits);
   } else {
-    cudaFuncSetAttribute(gate_logits_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
+    if (ensure_smem_attr(reinterpret_cast<const void*>(gate_logits_kernel<false>), (int)smem))
+      return DSV4_ERR_CUDA;
     launch_k(gate_logits_kernel<false>, grid, kGateThreads, smem, st,
              static_cast<const __nv_bfloat16*>(x), w,
                                                        T, H, E, logits);

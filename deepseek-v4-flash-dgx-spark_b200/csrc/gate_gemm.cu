@@ -276,14 +276,9 @@ static int launch_gate_gemm_cfg(const void* x, const void* w, int T, int H, int 
   int rc;
   if ((rc = make_tmap_bf16(&tx, x, H, T, BM))) return rc;
   if ((rc = make_tmap_bf16(&tw, w, H, E, NE))) return rc;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(gate_gemm_kernel<BM, NE, FUSED>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)C::SMEM_BYTES) != cudaSuccess)
-      return DSV4_ERR_CUDA;
-    attr = true;
-  }
+  if (ensure_smem_attr(reinterpret_cast<const void*>(gate_gemm_kernel<BM, NE, FUSED>),
+                       (int)C::SMEM_BYTES))
+    return DSV4_ERR_CUDA;
   const int items = (T + BM - 1) / BM * (E / NE) * ksplit;
   const int grid = items < num_sms ? items : num_sms;
   launch_k(gate_gemm_kernel<BM, NE, FUSED>, grid, 192, C::SMEM_BYTES, st,

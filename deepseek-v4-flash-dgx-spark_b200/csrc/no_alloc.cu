@@ -36,7 +36,10 @@ static void* g_static_scratch_ptr[kMaxDevices];
 static std::mutex g_static_scratch_mu;
 
 // Device address of the scratch on the current device, looked up once per
-// device (the first call on a device does the lookup).
+// device (the first call on a device does the lookup).  The address belongs
+// to the device's primary context: after cudaDeviceReset the module is loaded
+// again and the cached address is stale, so the entry point must not be used
+// in a process that resets a device it has already called it on.
 static int static_scratch_address(void** out) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return DSV4_ERR_CUDA;
@@ -68,16 +71,17 @@ extern "C" int dsv4_expert_forward_static(const dsv4_moe_layer* L, int expert, c
   if (need < 0) return DSV4_ERR_ARG;
   if (need > static_cast<long long>(kStaticScratchBytes)) return DSV4_ERR_WORKSPACE;
   if (T == 0) return DSV4_OK;
-  // run on the device that owns the output buffer
+  // Run on the device that owns the output when it is plain device memory;
+  // managed or host-registered outputs run on the current device, as in
+  // dsv4_expert_forward.
   cudaPointerAttributes a;
-  if (cudaPointerGetAttributes(&a, y) != cudaSuccess || a.type != cudaMemoryTypeDevice) {
-    cudaGetLastError();
-    return DSV4_ERR_ARG;
+  if (cudaPointerGetAttributes(&a, y) == cudaSuccess && a.type == cudaMemoryTypeDevice) {
+    int cur = -1;
+    if (cudaGetDevice(&cur) != cudaSuccess || cur != a.device) {
+      if (cudaSetDevice(a.device) != cudaSuccess) return DSV4_ERR_CUDA;
+    }
   }
-  int cur = -1;
-  if (cudaGetDevice(&cur) != cudaSuccess || cur != a.device) {
-    if (cudaSetDevice(a.device) != cudaSuccess) return DSV4_ERR_CUDA;
-  }
+  cudaGetLastError();
   void* scratch = nullptr;
   int rc = static_scratch_address(&scratch);
   if (rc) return rc;

@@ -146,7 +146,17 @@ class PeerExchange:
     collective, at set-up), and maps theirs; ``peer_bases`` is the device array
     of all W buffers as seen from this GPU.  ``cap_tokens`` bounds the tokens
     any rank passes per call.  Set-up is collective: every rank of ``group``
-    constructs its exchange in the same order."""
+    constructs its exchange in the same order.
+
+    A wait for a peer's flag that runs out (2 s, a rank that died or fell
+    behind) latches ``DSV4_DEVERR_TIMEOUT_PEER``; the kernels after it run on
+    whatever the buffer holds and the device epoch counter still advances, so
+    a late peer's stores for one call can land while this rank reads the next.
+    After such a timeout the exchange is poisoned: every eager call checks,
+    without synchronising, the error word its predecessor copied back and
+    raises ``RuntimeError`` once it is set, and every later call raises too.
+    Recover by synchronising the device, passing a process-group barrier on
+    every rank, ``close()``-ing the exchange and creating a new one."""
 
     def __init__(self, moe, cap_tokens: int, group=None):
         self.lib = _lib.load()
@@ -194,6 +204,30 @@ class PeerExchange:
         self.bases = bases
         self.peer_bases = torch.tensor(bases, dtype=torch.int64, device=self.dev)
         self._ws = None
+        # the device error word, copied back after every eager call
+        self.poisoned: str | None = None
+        self._err_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self._err_event: torch.cuda.Event | None = None
+
+    def check_poisoned(self) -> None:
+        """Raise if an earlier call's peer wait ran out (non-blocking: reads
+        the error word the last finished call copied back)."""
+        if self.poisoned is None and self._err_event is not None and self._err_event.query():
+            code = int(self._err_host[0])
+            if code == 107:  # DSV4_DEVERR_TIMEOUT_PEER
+                self.poisoned = _lib.DEVERR_NAMES[code]
+        if self.poisoned is not None:
+            raise RuntimeError(f"expert-parallel peer exchange is poisoned ({self.poisoned}): synchronise, "
+                               "pass a barrier on every rank, close() it and create a new one")
+
+    def note_call_end(self) -> None:
+        """Enqueue the copy of the device error word after an eager call."""
+        if torch.cuda.is_current_stream_capturing():
+            return
+        check(self.lib.dsv4_device_error_async(ptr(self._err_host), stream_ptr()), "dsv4_device_error_async")
+        if self._err_event is None:
+            self._err_event = torch.cuda.Event()
+        self._err_event.record()
 
     def close(self) -> None:
         """Unmap the peers' buffers and free this rank's.  Peers store into this
@@ -260,14 +294,18 @@ def ep_forward_peer(ex: PeerExchange, x: torch.Tensor, routing=None) -> torch.Te
     """One expert-parallel layer call over peer memory: no host collective and
     no host synchronisation, so it can be captured in a CUDA graph.  Every
     rank must call (or replay) it once per layer call; the epochs are counted
-    on the device (epoch 0)."""
+    on the device (epoch 0).  Raises ``RuntimeError`` once an earlier call's
+    peer wait ran out (see ``PeerExchange``)."""
+    ex.check_poisoned()
     if routing is None:
         weights, indices = ex.moe.gate(x)
     else:
         weights, indices = routing
     ret_pos, indices = peer_dispatch(ex, x, weights, indices, 0)
     ws = peer_expert_forward(ex, x, 0)
-    return peer_combine(ex, x, ret_pos, indices, ws, 0)
+    y = peer_combine(ex, x, ret_pos, indices, ws, 0)
+    ex.note_call_end()
+    return y
 
 
 def ep_moe_forward(moe, x: torch.Tensor, routing=None) -> torch.Tensor:

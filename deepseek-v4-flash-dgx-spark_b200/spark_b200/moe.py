@@ -508,7 +508,8 @@ class MoE(nn.Module):
             if routing is None:
                 routing = self.gate(x2, input_ids)
             ids = input_ids if input_ids is not None else torch.empty(0, dtype=torch.int64)
-            tel.record_routing(layer_id=self.layer_id, input_ids=ids, expert_indices=routing[1])
+            tel.record_routing(layer_id=self.layer_id, input_ids=ids, expert_indices=routing[1],
+                               tokens=x2.shape[0])
         else:
             tel.count_routing(x2.shape[0], x2.shape[0] * self.n_activated_experts)
         if self.world == 1:

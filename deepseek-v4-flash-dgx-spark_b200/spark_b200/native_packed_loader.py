@@ -10,7 +10,8 @@ spark_runtime/native/native_packed_loader.cpp (pybind module at :325-359):
   ``.copy_storage_to_tensors_cuda``, ``.read_into_and_copy``,
   ``.read_into_and_copy_cuda`` (:199-321)
 
-The work is done by libdsv4moe.so (``dsv4_read_into``, ``dsv4_copy_slices``,
+A failed ``pread`` raises ``RuntimeError("pread failed: <strerror>")``, as the
+reference's ``std::system_error`` does through pybind11.  The work is done by libdsv4moe.so (``dsv4_read_into``, ``dsv4_copy_slices``,
 ``dsv4_read_into_and_copy``); ctypes releases the GIL around every call, as
 the reference's ``py::gil_scoped_release`` does.  Device targets get one
 ``cudaMemcpyAsync`` each on the current stream.  On B200 the bulk path is
@@ -66,7 +67,7 @@ def read_into(fd: int, destination: torch.Tensor, size: int, offset: int) -> int
     rc = _lib.load().dsv4_read_into(int(fd), destination.data_ptr(), destination.numel(), int(size), int(offset),
                                     ctypes.byref(got), ctypes.byref(err))
     if rc == ERR_IO:
-        raise OSError(err.value, f"pread failed: {os.strerror(err.value or errno.EIO)}")
+        raise RuntimeError(f"pread failed: {os.strerror(err.value or errno.EIO)}")
     _lib.check(rc, "read_into")
     return int(got.value)
 
@@ -178,7 +179,7 @@ class ExpertCopyPlan:
                                                  stream, ctypes.byref(rb), ctypes.byref(cb), ctypes.byref(rs),
                                                  ctypes.byref(cs), ctypes.byref(err))
         if rc == ERR_IO:
-            raise OSError(err.value, f"pread failed: {os.strerror(err.value or errno.EIO)}")
+            raise RuntimeError(f"pread failed: {os.strerror(err.value or errno.EIO)}")
         if rc == ERR_SHORT_READ:
             raise RuntimeError("short packed expert read")
         _raise_copy(rc)

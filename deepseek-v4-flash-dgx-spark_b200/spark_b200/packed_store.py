@@ -8,13 +8,19 @@ layers: {L: {path, bytes, experts: {E: {offset, bytes, tensors: {name:
 {offset, bytes, source_dtype, source_shape, transform}}}}}}}`` written
 atomically (tmp + rename).
 
-``PackedExpertStore`` keeps the reference's constructor, ``from_env``,
-``tensors_for_expert``, ``native_plan_for_expert``, ``read_and_copy_with_plan``,
-``copy_storage_to_tensors``, ``copy_storage_with_plan`` and ``close``
-(spark_runtime/lazy_official_runtime.py:49-338), and adds the B200 bulk path
-``upload_experts``: one pread per expert into a single pinned buffer, one
-host-to-device copy of all blocks, then the device materializer fills the
-arena slots (``ExpertArena.materialize``).
+``PackedExpertStore`` answers the reference's interface (constructor,
+``from_env``, ``tensors_for_expert``, ``native_plan_for_expert``,
+``read_and_copy_with_plan``, ``copy_storage_to_tensors``,
+``copy_storage_with_plan``, ``close``; spark_runtime/lazy_official_runtime.py:
+49-338).  Inside, the layout is parsed once into a flat index (``SlabIndex``:
+one row per expert with its file, offset and size, and the sub-offsets of its
+tensors); every lookup, read and copy plan is derived from that index.
+
+The B200 path is ``upload_experts``: experts move to the device in chunks
+through two reused pinned staging buffers and two device slab buffers, so the
+pread of chunk i+1 (host), the host-to-device copy of chunk i (a copy stream,
+one ``cudaMemcpyAsync`` per chunk) and the device materializer of chunk i-1
+(the caller's stream) overlap.
 """
 
 from __future__ import annotations
@@ -33,15 +39,31 @@ import torch
 from . import native_packed_loader as _native
 from .moe import PACKED_ORDER, ExpertArena
 
-_TRUE = {"1", "true", "yes"}
+# environment switches the reference's store reads (values "1", "true", "yes")
+_ENV_PINNED = "DEEPSEEK_SPARK_PACKED_NATIVE_PINNED_STAGING"
+_ENV_CUDA_MEMCPY = "DEEPSEEK_SPARK_NATIVE_CUDA_MEMCPY"
+_ENV_LAYOUT = "DEEPSEEK_SPARK_PACKED_EXPERT_LAYOUT"
+
+# source_dtype names of the layout -> torch dtypes (lazy_official_runtime.py:341-353)
+_DTYPES = {"BF16": torch.bfloat16, "F32": torch.float32, "F8_E8M0": torch.float8_e8m0fnu, "I8": torch.int8,
+           "I32": torch.int32, "I64": torch.int64}
 
 
-def _flag(name: str) -> bool:
-    return os.getenv(name, "0") in _TRUE
+def _env_on(name: str) -> bool:
+    return os.environ.get(name, "0").strip().lower() in ("1", "true", "yes")
+
+
+def _torch_dtype(name: str) -> torch.dtype:
+    dt = _DTYPES.get(name)
+    if dt is None:
+        raise ValueError(f"unsupported packed source dtype: {name}")
+    return dt
 
 
 @dataclass(frozen=True)
 class PackedExpertBatch:
+    """One expert block read into host memory: tensor views into ``_storage``."""
+
     tensors: dict[str, torch.Tensor]
     tensor_infos: dict[str, dict[str, Any]]
     read_seconds: float
@@ -51,25 +73,67 @@ class PackedExpertBatch:
 
 @dataclass(frozen=True)
 class NativeExpertCopyPlan:
+    """Copy plan of one expert's parameters: the loader plan over the
+    parameters found in the block, and the indices of those found / missing."""
+
     plan: Any
     parameter_indices: tuple[int, ...]
     fallback_indices: tuple[int, ...]
 
 
-def _source_dtype_to_torch(dtype_name: str) -> torch.dtype:
-    """lazy_official_runtime.py:341-353."""
-    mapping = {
-        "BF16": torch.bfloat16,
-        "F32": torch.float32,
-        "F8_E8M0": torch.float8_e8m0fnu,
-        "I8": torch.int8,
-        "I32": torch.int32,
-        "I64": torch.int64,
-    }
-    try:
-        return mapping[dtype_name]
-    except KeyError as exc:
-        raise ValueError(f"unsupported packed source dtype: {dtype_name}") from exc
+class SlabIndex:
+    """layout.json flattened: row r of the index is one (layer, expert) block,
+    at ``offset[r]`` of file ``files[file_id[r]]``, ``nbytes[r]`` long, with its
+    tensors' layout entries in ``tensors[r]`` (name -> info, offsets relative
+    to the block)."""
+
+    def __init__(self, layout: dict, base_dir: Path):
+        self.files: list[Path] = []
+        self.rows: dict[tuple[int, int], int] = {}
+        file_id, offset, nbytes = [], [], []
+        self.tensors: list[dict[str, dict[str, Any]]] = []
+        for lkey in sorted(layout.get("layers", {}), key=int):
+            lentry = layout["layers"][lkey]
+            path = Path(lentry["path"])
+            self.files.append(path if path.is_absolute() else base_dir / path)
+            fid = len(self.files) - 1
+            for ekey in sorted(lentry.get("experts", {}), key=int):
+                e = lentry["experts"][ekey]
+                self.rows[(int(lkey), int(ekey))] = len(offset)
+                file_id.append(fid)
+                offset.append(int(e["offset"]))
+                nbytes.append(int(e["bytes"]))
+                self.tensors.append(e["tensors"])
+        self.file_id = np.asarray(file_id, dtype=np.int32)
+        self.offset = np.asarray(offset, dtype=np.int64)
+        self.nbytes = np.asarray(nbytes, dtype=np.int64)
+
+    def row(self, layer_id: int, expert_id: int) -> int | None:
+        return self.rows.get((int(layer_id), int(expert_id)))
+
+    def rows_for(self, layer_id: int, experts: list[int]) -> np.ndarray:
+        rows = [self.row(layer_id, e) for e in experts]
+        missing = [e for e, r in zip(experts, rows) if r is None]
+        if missing:
+            raise KeyError(f"experts missing from the packed layout: layer={layer_id} experts={missing}")
+        return np.asarray(rows, dtype=np.int64)
+
+
+class _Staging:
+    """Per-thread host staging buffer, grown to the largest request and
+    reused; pinned when requested and CUDA is present."""
+
+    def __init__(self, pinned: bool):
+        self.pinned = pinned and torch.cuda.is_available()
+        self._local = threading.local()
+
+    def get(self, size: int) -> torch.Tensor:
+        buf = getattr(self._local, "buf", None)
+        if buf is None or buf.numel() < size:
+            cap = max(size, 1 << 20)
+            buf = torch.empty(cap, dtype=torch.uint8, pin_memory=self.pinned)
+            self._local.buf = buf
+        return buf[:size]
 
 
 class PackedExpertStore:
@@ -78,116 +142,103 @@ class PackedExpertStore:
         self.base_dir = self.layout_path.parent
         self.layout = json.loads(self.layout_path.read_text())
         self.layers: dict[str, Any] = self.layout.get("layers", {})
-        self.native_pinned_staging = _flag("DEEPSEEK_SPARK_PACKED_NATIVE_PINNED_STAGING")
-        self.native_cuda_memcpy = _flag("DEEPSEEK_SPARK_NATIVE_CUDA_MEMCPY")
+        self.index = SlabIndex(self.layout, self.base_dir)
+        # the native loader and its copy plans are always on here; the two
+        # switches below keep their reference meaning
+        self.native_pinned_staging = _env_on(_ENV_PINNED)
+        self.native_cuda_memcpy = _env_on(_ENV_CUDA_MEMCPY)
         self.native_copy_plan = True
         self.native_fused_materializer = True
         self._native_module = _native.load_native_packed_loader()
-        self._fds: dict[Path, int] = {}
-        self._lock = threading.Lock()
-        self._thread_local = threading.local()
-        self._copy_plans: dict[tuple[int, int, tuple[str, ...]], NativeExpertCopyPlan] = {}
+        self._staging = _Staging(self.native_pinned_staging)
+        self._fd_lock = threading.Lock()
+        self._fd_of_file: list[int | None] = [None] * len(self.index.files)
+        self._plans: dict[tuple[int, tuple[str, ...]], NativeExpertCopyPlan] = {}
+        self._upload: dict[tuple[str, int], dict[str, Any]] = {}  # per device: pinned + device rings
 
     @classmethod
     def from_env(cls) -> "PackedExpertStore | None":
-        value = os.getenv("DEEPSEEK_SPARK_PACKED_EXPERT_LAYOUT")
-        return cls(Path(value)) if value else None
+        path = os.environ.get(_ENV_LAYOUT)
+        return cls(Path(path)) if path else None
 
     def close(self) -> None:
-        with self._lock:
-            for fd in self._fds.values():
-                os.close(fd)
-            self._fds.clear()
+        with self._fd_lock:
+            for i, fd in enumerate(self._fd_of_file):
+                if fd is not None:
+                    os.close(fd)
+                    self._fd_of_file[i] = None
+        self._upload.clear()
 
-    def _fd(self, path: Path) -> int:
-        with self._lock:
-            fd = self._fds.get(path)
+    # ------------------------------------------------------------------ lookups
+    def _descriptor(self, file_id: int) -> int:
+        with self._fd_lock:
+            fd = self._fd_of_file[file_id]
             if fd is None:
-                fd = os.open(path, os.O_RDONLY)
-                self._fds[path] = fd
+                fd = os.open(self.index.files[file_id], os.O_RDONLY)
+                self._fd_of_file[file_id] = fd
             return fd
 
-    def _expert_entry(self, layer_id: int, expert_id: int):
-        layer = self.layers.get(str(layer_id))
-        if layer is None:
+    def _block(self, layer_id: int, expert_id: int) -> tuple[int, int, int, dict] | None:
+        """(descriptor, file offset, bytes, tensor infos) of one block, or None."""
+        r = self.index.row(layer_id, expert_id)
+        if r is None:
             return None
-        expert = layer.get("experts", {}).get(str(expert_id))
-        if expert is None:
-            return None
-        path = Path(layer["path"])
-        if not path.is_absolute():
-            path = self.base_dir / path
-        return path, int(expert["offset"]), int(expert["bytes"]), expert["tensors"]
+        return (self._descriptor(int(self.index.file_id[r])), int(self.index.offset[r]), int(self.index.nbytes[r]),
+                self.index.tensors[r])
 
-    def _native_staging(self, size: int) -> torch.Tensor:
-        staging = getattr(self._thread_local, "staging", None)
-        pinned = self.native_pinned_staging and torch.cuda.is_available()
-        if staging is None or staging.numel() < size or getattr(self._thread_local, "pinned", False) != pinned:
-            staging = torch.empty(size, dtype=torch.uint8, device="cpu", pin_memory=pinned)
-            self._thread_local.staging = staging
-            self._thread_local.pinned = pinned
-        return staging[:size]
-
-    @staticmethod
-    def _tensor_from_storage(storage: torch.Tensor, tensor_info: dict[str, Any]) -> torch.Tensor:
-        offset = int(tensor_info["offset"])
-        size = int(tensor_info["bytes"])
-        dtype = _source_dtype_to_torch(tensor_info["source_dtype"])
-        shape = [int(d) for d in tensor_info["source_shape"]]
-        return storage[offset:offset + size].view(dtype).reshape(shape)
-
+    # ---------------------------------------------------------- reference API
     def tensors_for_expert(self, layer_id: int, expert_id: int) -> PackedExpertBatch | None:
-        entry = self._expert_entry(layer_id, expert_id)
-        if entry is None:
+        blk = self._block(layer_id, expert_id)
+        if blk is None:
             return None
-        path, offset, size, tensor_infos = entry
-        fd = self._fd(path)
-        start = time.monotonic()
-        view = self._native_staging(size)
-        got = self._native_module.read_into(fd, view, size, offset)
-        read_seconds = time.monotonic() - start
+        fd, off, size, infos = blk
+        storage = self._staging.get(size)
+        t0 = time.monotonic()
+        got = self._native_module.read_into(fd, storage, size, off)
+        seconds = time.monotonic() - t0
         if got != size:
             raise OSError(f"short packed expert read: layer={layer_id} expert={expert_id}")
-        tensors = {name: self._tensor_from_storage(view, info) for name, info in tensor_infos.items()}
-        return PackedExpertBatch(tensors, tensor_infos, read_seconds, size, view)
+        views = {}
+        for name, info in infos.items():
+            o, n = int(info["offset"]), int(info["bytes"])
+            views[name] = storage[o:o + n].view(_torch_dtype(info["source_dtype"])).reshape(
+                [int(d) for d in info["source_shape"]])
+        return PackedExpertBatch(views, infos, seconds, size, storage)
 
     def native_plan_for_expert(self, layer_id: int, expert_id: int, prefix: str,
                                parameters: list[tuple[str, torch.nn.Parameter]]) -> NativeExpertCopyPlan | None:
-        entry = self._expert_entry(layer_id, expert_id)
-        if entry is None:
+        r = self.index.row(layer_id, expert_id)
+        if r is None:
             return None
-        _, _, _, tensor_infos = entry
-        key = (layer_id, expert_id, tuple(name for name, _ in parameters))
-        plan = self._copy_plans.get(key)
-        if plan is not None:
-            return plan
-        offsets, sizes, idx, fallback = [], [], [], []
-        for index, (name, param) in enumerate(parameters):
-            info = tensor_infos.get(f"{prefix}.{name}")
-            if info is None:
-                fallback.append(index)
-                continue
-            offsets.append(int(info["offset"]))
-            sizes.append(param.numel() * param.element_size())
-            idx.append(index)
-        native = self._native_module.ExpertCopyPlan(offsets, sizes) if offsets else None
-        plan = NativeExpertCopyPlan(native, tuple(idx), tuple(fallback))
-        self._copy_plans[key] = plan
-        return plan
+        key = (r, tuple(name for name, _ in parameters))
+        cached = self._plans.get(key)
+        if cached is not None:
+            return cached
+        infos = self.index.tensors[r]
+        found = [(i, infos.get(f"{prefix}.{name}")) for i, (name, _) in enumerate(parameters)]
+        have = [(i, info) for i, info in found if info is not None]
+        plan = None
+        if have:
+            plan = self._native_module.ExpertCopyPlan(
+                [int(info["offset"]) for _, info in have],
+                [parameters[i][1].numel() * parameters[i][1].element_size() for i, _ in have])
+        made = NativeExpertCopyPlan(plan, tuple(i for i, _ in have),
+                                    tuple(i for i, info in found if info is None))
+        self._plans[key] = made
+        return made
 
     def read_and_copy_with_plan(self, layer_id: int, expert_id: int, plan, targets: list[torch.Tensor], *,
                                 non_blocking: bool):
-        entry = self._expert_entry(layer_id, expert_id)
-        if entry is None:
+        blk = self._block(layer_id, expert_id)
+        if blk is None:
             return None
-        path, offset, size, _ = entry
-        fd = self._fd(path)
-        staging = self._native_staging(size)
+        fd, off, size, _ = blk
+        staging = self._staging.get(size)
         if self.native_cuda_memcpy:
-            res = plan.read_into_and_copy_cuda(fd, staging, size, offset, targets)
+            rb, cb, rs, cs = plan.read_into_and_copy_cuda(fd, staging, size, off, targets)
         else:
-            res = plan.read_into_and_copy(fd, staging, size, offset, targets, non_blocking)
-        return int(res[0]), int(res[1]), float(res[2]), float(res[3])
+            rb, cb, rs, cs = plan.read_into_and_copy(fd, staging, size, off, targets, non_blocking)
+        return int(rb), int(cb), float(rs), float(cs)
 
     def copy_storage_to_tensors(self, storage, targets, offsets, *, non_blocking: bool) -> int:
         return int(self._native_module.copy_storage_to_tensors(storage, targets, offsets, non_blocking))
@@ -197,43 +248,106 @@ class PackedExpertStore:
             return int(plan.copy_storage_to_tensors_cuda(storage, targets))
         return int(plan.copy_storage_to_tensors(storage, targets, non_blocking))
 
-    # -------------------------------------------------------------- B200 bulk path
+    # --------------------------------------------------------- B200 bulk path
+    def _pread_rows(self, rows: np.ndarray, dst: torch.Tensor, dst_off: np.ndarray) -> int:
+        """pread the blocks of index ``rows`` into ``dst`` at ``dst_off``; raises
+        on a short read.  Returns the bytes read."""
+        total = 0
+        for r, o in zip(rows.tolist(), dst_off.tolist()):
+            size = int(self.index.nbytes[r])
+            fd = self._descriptor(int(self.index.file_id[r]))
+            got = self._native_module.read_into(fd, dst[o:o + size], size, int(self.index.offset[r]))
+            if got != size:
+                raise RuntimeError("short packed expert read")
+            total += size
+        return total
+
     def read_blocks(self, layer_id: int, experts: list[int]) -> tuple[torch.Tensor, list[int], float]:
         """All blocks of ``experts`` in one (pinned when CUDA is present) host
         buffer: returns (buffer, byte offset of each block, read seconds)."""
-        entries = [self._expert_entry(layer_id, e) for e in experts]
-        if any(e is None for e in entries):
-            missing = [x for x, e in zip(experts, entries) if e is None]
-            raise KeyError(f"experts missing from the packed layout: layer={layer_id} experts={missing}")
-        offs, total = [], 0
-        for _, _, size, _ in entries:
-            offs.append(total)
-            total += (size + 255) // 256 * 256
-        buf = torch.empty(max(total, 1), dtype=torch.uint8, pin_memory=torch.cuda.is_available())
+        rows = self.index.rows_for(layer_id, experts)
+        sizes = self.index.nbytes[rows]
+        offs = np.concatenate([[0], np.cumsum((sizes + 255) // 256 * 256)])
+        buf = torch.empty(max(int(offs[-1]), 1), dtype=torch.uint8, pin_memory=torch.cuda.is_available())
         t0 = time.monotonic()
-        for (path, offset, size, _), o in zip(entries, offs):
-            got = self._native_module.read_into(self._fd(path), buf[o:o + size], size, offset)
-            if got != size:
-                raise RuntimeError("short packed expert read")
+        nbytes = self._pread_rows(rows, buf, offs[:-1])
         dt = time.monotonic() - t0
         from .telemetry import expert_telemetry
 
-        expert_telemetry().record_packed_read(len(experts), sum(e[2] for e in entries), dt)
-        return buf, offs, dt
+        expert_telemetry().record_packed_read(len(experts), nbytes, dt)
+        return buf, [int(o) for o in offs[:-1]], dt
+
+    def _rings(self, device: torch.device, chunk_bytes: int) -> dict[str, Any]:
+        key = (str(device), chunk_bytes)
+        ring = self._upload.get(key)
+        if ring is None:
+            ring = {"host": [torch.empty(chunk_bytes, dtype=torch.uint8, pin_memory=True) for _ in range(2)],
+                    "dev": [torch.empty(chunk_bytes, dtype=torch.uint8, device=device) for _ in range(2)],
+                    "copy_stream": torch.cuda.Stream(device=device),
+                    "h2d_done": [torch.cuda.Event() for _ in range(2)],
+                    "mat_done": [torch.cuda.Event() for _ in range(2)]}
+            self._upload[key] = ring  # kept: an unsynchronised upload may still be using an older ring
+        return ring
 
     def upload_experts(self, layer_id: int, experts: list[int], arena: ExpertArena, slots: list[int], *,
-                       bf16_out: torch.Tensor | None = None, stream=None) -> dict[str, float]:
-        """Fill arena ``slots`` with ``experts`` of ``layer_id``: pread into one
-        pinned buffer, one host-to-device copy, device materializer (bit-exact
-        bytes + scale atoms).  Returns the reference's stats keys."""
-        buf, offs, read_s = self.read_blocks(layer_id, experts)
-        t0 = time.monotonic()
-        dev_slab = buf.to(arena.device, non_blocking=True)
-        copied = arena.materialize(dev_slab, offs, slots, bf16_out=bf16_out, stream=stream)
-        torch.cuda.current_stream(arena.device).synchronize()
-        return {"packed_loads": len(experts), "packed_read_bytes": int(sum(
-            self._expert_entry(layer_id, e)[2] for e in experts)), "packed_read_seconds": read_s,
-            "materialize_seconds": time.monotonic() - t0, "copied_bytes": copied}
+                       bf16_out: torch.Tensor | None = None, stream=None, chunk_experts: int = 8,
+                       synchronize: bool = True) -> dict[str, float]:
+        """Fill arena ``slots`` with ``experts`` of ``layer_id`` (bit-exact bytes
+        plus scale atoms, and optionally the exact bf16 decode).
+
+        Pipelined in chunks of ``chunk_experts`` blocks: while the host preads
+        chunk i+1 into one pinned buffer, the copy stream moves chunk i to one
+        device buffer (one ``cudaMemcpyAsync``) and ``stream`` runs the device
+        materializer over chunk i-1 from the other.  A buffer is refilled only
+        after the work that reads it has finished (events), and the
+        materializer of a chunk waits for its copy.  Returns the reference's
+        stats keys plus the upload's wall time and rate."""
+        if len(experts) != len(slots):
+            raise RuntimeError("targets and offsets length mismatch")
+        if not experts:
+            return {"packed_loads": 0, "packed_read_bytes": 0, "packed_read_seconds": 0.0,
+                    "materialize_seconds": 0.0, "copied_bytes": 0, "upload_seconds": 0.0, "upload_gbs": 0.0}
+        dev = arena.device
+        rows = self.index.rows_for(layer_id, experts)
+        sizes = self.index.nbytes[rows]
+        stride = int(((sizes.max() + 255) // 256) * 256)
+        per = max(1, min(int(chunk_experts), len(experts)))
+        ring = self._rings(dev, stride * per)
+        compute = stream if stream is not None else torch.cuda.current_stream(dev)
+        copy_stream = ring["copy_stream"]
+        read_s = 0.0
+        copied = 0
+        t_start = time.monotonic()
+        for c, first in enumerate(range(0, len(experts), per)):
+            b = c % 2
+            chunk_rows = rows[first:first + per]
+            n = len(chunk_rows)
+            host, dbuf = ring["host"][b], ring["dev"][b]
+            if c >= 2:
+                ring["h2d_done"][b].synchronize()  # the copy out of this pinned buffer has finished
+            t0 = time.monotonic()
+            self._pread_rows(chunk_rows, host, np.arange(n, dtype=np.int64) * stride)
+            read_s += time.monotonic() - t0
+            with torch.cuda.stream(copy_stream):
+                if c >= 2:
+                    copy_stream.wait_event(ring["mat_done"][b])  # the materializer read this device buffer
+                dbuf[:n * stride].copy_(host[:n * stride], non_blocking=True)
+                ring["h2d_done"][b].record(copy_stream)
+            compute.wait_event(ring["h2d_done"][b])
+            with torch.cuda.stream(compute):
+                copied += arena.materialize(dbuf, [i * stride for i in range(n)], slots[first:first + n],
+                                            bf16_out=bf16_out, stream=compute)
+                ring["mat_done"][b].record(compute)
+        if synchronize:
+            compute.synchronize()
+        total_s = time.monotonic() - t_start
+        nbytes = int(sizes.sum())
+        from .telemetry import expert_telemetry
+
+        expert_telemetry().record_packed_read(len(experts), nbytes, read_s)
+        return {"packed_loads": len(experts), "packed_read_bytes": nbytes, "packed_read_seconds": read_s,
+                "materialize_seconds": total_s - read_s, "copied_bytes": copied, "upload_seconds": total_s,
+                "upload_gbs": nbytes / max(total_s, 1e-9) / 1e9}
 
 
 def _tensor_meta(name: str, dim: int, inter: int) -> tuple[str, list[int], str]:

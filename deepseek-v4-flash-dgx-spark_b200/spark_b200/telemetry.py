@@ -78,10 +78,16 @@ class ExpertTelemetry:
             self.routed_activations += int(activations)
 
     def record_routing(self, *, layer_id: int, input_ids: torch.Tensor,
-                       expert_indices: torch.Tensor) -> None:
-        """Counters plus, when tracing, the reference's ``expert_route`` line."""
+                       expert_indices: torch.Tensor, tokens: int | None = None) -> None:
+        """Counters plus, when tracing, the reference's ``expert_route`` line.
+
+        ``tokens`` is the number of routed tokens when ``input_ids`` does not
+        hold one id per token (a caller without token ids passes an empty
+        tensor); by default it is ``input_ids.numel()``, the reference's count.
+        The line's ``token_ids`` / ``token_count`` always describe
+        ``input_ids`` as given."""
         flat = expert_indices.flatten()
-        self.count_routing(input_ids.numel(), flat.numel())
+        self.count_routing(input_ids.numel() if tokens is None else tokens, flat.numel())
         if self.route_trace_path is None:
             return
         ids = flat.detach().cpu().tolist()

@@ -61,6 +61,12 @@ DSV4_API const char* dsv4_status_string(int status);
 /* Synchronises the device, returns the first device-side error code (0 if
  * none) in *code, and clears it when clear != 0. */
 DSV4_API int dsv4_device_error(int clear, int* code);
+/* Enqueues on `stream` a copy of the device-side error word of the current
+ * device into *dst (pinned host or device memory) and returns at once; the
+ * value is valid once the stream has reached that point.  Lets a caller check
+ * for a latched error (for example a peer wait that ran out) without
+ * synchronising the device.  No counterpart in the reference. */
+DSV4_API int dsv4_device_error_async(int* dst, void* stream);
 
 /* ---- MoE layer description ---------------------------------------------
  * Routed experts live in an expert arena: one device buffer of n_slots slots
@@ -146,9 +152,12 @@ DSV4_API int dsv4_profile_read(float* stage_ms, int n);
  * library holds on every GPU it runs on until the process exits.  Calls whose
  * dsv4_expert_workspace_bytes(L, T) exceeds it return DSV4_ERR_WORKSPACE
  * (up to 640 tokens at H=4096, I=2048).  The first call on a device looks up
- * the array's device address; make it before any stream capture.  All calls
- * share the array: calls that may overlap on the GPU race and must not be
- * issued.  Nothing is allocated, freed or cleared. */
+ * the array's device address; make it before any stream capture.  The
+ * address is cached for the life of the process, so the entry point is not
+ * valid after cudaDeviceReset on a device it was called on.  All calls share
+ * the array: calls that may overlap on the GPU race and must not be issued.
+ * Nothing is allocated, freed or cleared.  y may be device, managed or
+ * host-registered memory, as for dsv4_expert_forward. */
 DSV4_API long long dsv4_expert_static_scratch_bytes(void);
 DSV4_API int dsv4_expert_forward_static(const dsv4_moe_layer* L, int expert, const void* x, int T,
                                         const float* row_weights, void* y, void* stream);

@@ -119,20 +119,29 @@ def decode_e4m3(codes: np.ndarray) -> np.ndarray:
     return E4M3_VALUES[np.asarray(codes, dtype=np.uint8)]
 
 
+# byte -> (low nibble value, high nibble value): one lookup per packed byte
+_E2M1_PAIRS = np.stack([E2M1_VALUES[np.arange(256) & 0xF], E2M1_VALUES[np.arange(256) >> 4]], axis=1)
+
+
 def unpack_e2m1(packed: np.ndarray) -> np.ndarray:
     """[..., K/2] bytes -> [..., K] fp32, low nibble first."""
     packed = np.asarray(packed, dtype=np.uint8)
-    lo = E2M1_VALUES[packed & 0xF]
-    hi = E2M1_VALUES[packed >> 4]
-    return np.stack([lo, hi], axis=-1).reshape(*packed.shape[:-1], packed.shape[-1] * 2)
+    return _E2M1_PAIRS[packed].reshape(*packed.shape[:-1], packed.shape[-1] * 2)
 
 
 def dequant_fp4_weight(packed: np.ndarray, scale: np.ndarray, block: int = 32) -> np.ndarray:
     """FP4 e2m1 [N, K/2] bytes with ue8m0 scales [N, K/block] -> fp32 [N, K].
-    Exact: every product is representable in fp32 (and in bf16)."""
-    w = unpack_e2m1(packed)
-    s = e8m0_to_f32(scale)
-    return (w * np.repeat(s, block, axis=1)).astype(np.float32)
+    Exact: every product is representable in fp32 (and in bf16), so the
+    multi-threaded torch CPU lookup and multiply below give the same bits as
+    the element-wise definition (unpack_e2m1 x 2^(scale-127))."""
+    import torch
+
+    packed = np.ascontiguousarray(packed, dtype=np.uint8)
+    n = packed.shape[0]
+    w = torch.from_numpy(_E2M1_PAIRS)[torch.from_numpy(packed).long()].reshape(n, -1)
+    s = torch.from_numpy(np.ascontiguousarray(e8m0_to_f32(scale), dtype=np.float32))
+    k = w.shape[1]
+    return (w.view(n, k // block, block) * s[:, :, None]).view(n, k).numpy()
 
 
 def dequant_fp8_weight(codes: np.ndarray, scale: np.ndarray, block: int = 128) -> np.ndarray:
@@ -247,6 +256,31 @@ def route_from_logits(logits: np.ndarray, bias: np.ndarray | None, topk: int,
     return wts, idx.astype(np.int64)
 
 
+def routing_flips(device_indices: np.ndarray, logits_ref: np.ndarray, bias: np.ndarray | None,
+                  topk: int) -> list[tuple[int, float]]:
+    """Tokens whose device top-k set differs from the top-k the oracle selects
+    on its own (float64-accumulated) logits, with the score gap of each flip:
+    (token, gap relative to the boundary score), where the gap is how far the
+    oracle's best rejected-by-the-device expert beats the device's worst
+    choice that the oracle rejected, in selection score (sigmoid + bias).  A
+    flip is legitimate only when that gap is within the logits' accumulation
+    error (a near tie)."""
+    scores = sigmoid_canonical(np.asarray(logits_ref, np.float32))
+    sel = scores if bias is None else (scores + np.asarray(bias, np.float32)).astype(np.float32)
+    order = np.argsort(-sel, axis=-1, kind="stable")[:, :topk]
+    out = []
+    for t in range(device_indices.shape[0]):
+        d, r = set(device_indices[t].tolist()), set(order[t].tolist())
+        if d == r:
+            continue
+        only_r = sorted(r - d)
+        only_d = sorted(d - r)
+        gap = float(max(sel[t, e] for e in only_r) - min(sel[t, e] for e in only_d))
+        boundary = float(abs(sel[t, order[t, topk - 1]])) or 1e-30
+        out.append((t, gap / boundary))
+    return out
+
+
 def hash_route(logits: np.ndarray, tid2eid: np.ndarray, input_ids: np.ndarray, route_scale: float):
     """Hash-routed layers (gate.tid2eid [vocab, k], weight-manifest.csv:3; the
     official Gate's hash mode is absent here, so this is the restated choice):
@@ -309,8 +343,16 @@ def quantized_linear(x_bf16: np.ndarray, w_dense: np.ndarray) -> np.ndarray:
 
 def dequant_linear(a: np.ndarray, w_dense: np.ndarray) -> np.ndarray:
     """The GEMM of ``quantized_linear`` on already quantized-and-dequantized
-    activations ``a``."""
-    return round_bf16((a.astype(np.float64) @ w_dense.astype(np.float64).T).astype(np.float32))
+    activations ``a``.  Every product of an e4m3 activation and an e2m1 / e4m3
+    weight (with power-of-two scales) has at most 5 significant bits and the
+    exponents of one dot product span far fewer than float64's 53 bits, so the
+    float64 sum is exact whatever the summation order; the multi-threaded torch
+    CPU product therefore gives the bits of a sequential float64 sum."""
+    import torch
+
+    a64 = torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).double()
+    w64 = torch.from_numpy(np.ascontiguousarray(w_dense, dtype=np.float32)).double()
+    return round_bf16((a64 @ w64.T).numpy().astype(np.float32))
 
 
 def silu(x: np.ndarray) -> np.ndarray:
@@ -375,22 +417,33 @@ def combine(T: int, H: int, indices: np.ndarray, expert_out: dict, shared_out: n
     return round_bf16(y)
 
 
-def moe_forward(x_bf16: np.ndarray, mw: MoEWeights, routing=None, dense_cache=None):
+def moe_forward(x_bf16: np.ndarray, mw: MoEWeights, routing=None, dense_cache=None, workers: int = 1):
     """Full layer.  ``routing`` = (weights, indices) overrides the gate (used to
     check the expert math on the device's own routing).  Returns
-    (y bf16-as-fp32 [T,H], weights, indices, per-route outputs dict)."""
+    (y bf16-as-fp32 [T,H], weights, indices, per-route outputs dict).
+
+    ``workers`` > 1 evaluates the experts in a thread pool (the weight decode
+    and the float64 products release the GIL); each expert's output is the
+    same either way and the combine always sums in ascending expert id."""
     T, H = x_bf16.shape
     if routing is None:
         wts, idx, _ = gate_forward(x_bf16, mw.gate_w, mw.gate_bias, mw.topk, mw.route_scale)
     else:
         wts, idx = routing
-    outs = {}
-    for e in np.unique(idx):
-        e = int(e)
+
+    def one(e):
         rows, top = np.nonzero(idx == e)  # torch.where order: row-major
         dense = dense_cache(e) if dense_cache is not None else None
-        o = expert_forward(x_bf16[rows], mw.experts[e], wts[rows, top], mw.swiglu_limit, dense)
-        outs[e] = (rows, o)
+        return e, (rows, expert_forward(x_bf16[rows], mw.experts[e], wts[rows, top], mw.swiglu_limit, dense))
+
+    active = [int(e) for e in np.unique(idx)]
+    if workers > 1 and len(active) > 1:
+        from concurrent.futures import ThreadPoolExecutor
+
+        with ThreadPoolExecutor(workers) as pool:
+            outs = dict(pool.map(one, active))
+    else:
+        outs = dict(one(e) for e in active)
     shared_dense = dense_cache("shared") if dense_cache is not None else None
     sh = expert_forward(x_bf16, mw.shared, None, mw.swiglu_limit, shared_dense)
     y = combine(T, H, idx, outs, sh)

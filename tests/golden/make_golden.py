@@ -1,7 +1,7 @@
 """Generate the golden fixtures of the MoE hot path from the reference itself.
 
-    make -C oracle                      # the reference loader, built from its source
-    python tests/golden/make_golden.py  # needs the reference sources (default /root/reference)
+    make -C oracle REFERENCE_DIR=<checkout>   # the reference loader, built from its source
+    python tests/golden/make_golden.py  --reference <checkout of the reference> (or $REFERENCE_DIR)
 
 Runs, on the CPU of the build container, the reference's own code for the
 layer configuration "4 tokens, H=1024, 16 routed experts top-4 + 1 shared,
@@ -155,7 +155,7 @@ def official_stub(cfg):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("REFERENCE_DIR"), required="REFERENCE_DIR" not in os.environ)
     args = ap.parse_args()
     ref = Path(args.reference)
     sys.path.insert(0, str(ref))

@@ -1,6 +1,6 @@
 """Golden route-trace lines and routing counters from the reference itself.
 
-    python tests/golden/make_route_trace_golden.py  # needs the reference sources (default /root/reference)
+    python tests/golden/make_route_trace_golden.py  --reference <checkout of the reference> (or $REFERENCE_DIR)
 
 Runs the reference's ``ExpertCacheManager.record_routing``
 (spark_runtime/lazy_official_runtime.py:550-603, the call LazyMoE.forward
@@ -34,7 +34,7 @@ CALLS = [
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("REFERENCE_DIR"), required="REFERENCE_DIR" not in os.environ)
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference)))
     with tempfile.TemporaryDirectory() as tmp:

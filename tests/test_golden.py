@@ -137,6 +137,21 @@ def _ref_loader():
     return mod
 
 
+def test_pread_failure_raises_like_the_reference_loader():
+    """A failed pread (a bad descriptor) raises RuntimeError with the same
+    message in the drop-in loader and in the reference loader compiled from
+    its own source."""
+    from spark_b200 import native_packed_loader as npl
+
+    ref = _ref_loader()
+    msgs = []
+    for mod in (ref, npl):
+        with pytest.raises(RuntimeError) as info:
+            mod.read_into(987654, torch.zeros(16, dtype=torch.uint8), 8, 0)
+        msgs.append(str(info.value))
+    assert msgs[0] == msgs[1] == "pread failed: Bad file descriptor"
+
+
 def test_loader_mirror_agrees_with_compiled_reference_loader():
     """Same return values and copies as the reference C++ loader compiled from
     its own source (oracle/_ref), on a random block and plan."""

@@ -245,7 +245,19 @@ def test_peer_wait_times_out_with_an_error_not_a_hang(cuda_device):
                          device="cuda")
         L.check(lib.dsv4_ep_expert_forward_p2p(ctypes.byref(d), 0, W, None, 0, p, L.ptr(bases), cap, 7,
                                                L.ptr(ws), ws.numel(), L.stream_ptr()), "forward")
+        # the exchange learns of the latched timeout without synchronising:
+        # the word is copied back after the call and read by the next call
+        from spark_b200.ep import PeerExchange
+
+        ex = PeerExchange.__new__(PeerExchange)
+        ex.lib, ex.poisoned, ex._err_event = lib, None, None
+        ex._err_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        ex.check_poisoned()  # nothing recorded yet: no error
+        ex.note_call_end()
         torch.cuda.synchronize()
+        for _ in range(2):  # poisoned for good, not just once
+            with pytest.raises(RuntimeError, match="poisoned"):
+                ex.check_poisoned()
         with pytest.raises(RuntimeError, match="exchange flag"):
             L.raise_on_device_error()
         x = torch.ones(8, device="cuda")
