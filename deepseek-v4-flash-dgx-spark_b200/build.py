@@ -2,8 +2,10 @@
 
     python deepseek-v4-flash-dgx-spark_b200/build.py [--force]
 
-The shared library lands in deepseek-v4-flash-dgx-spark_b200/lib/ and is
-loaded by spark_b200._lib through ctypes.  nvcc cross-compiles for sm_100a on
+The shared libraries land in deepseek-v4-flash-dgx-spark_b200/lib/:
+libdsv4moe.so (the C ABI, loaded by spark_b200._lib through ctypes) and
+libdsv4moe_torch.so (the TORCH_LIBRARY(dsv4moe) op layer over it, loaded by
+spark_b200.ops with torch.ops.load_library).  nvcc cross-compiles for sm_100a on
 a machine without a GPU.
 """
 
@@ -20,6 +22,7 @@ REPO = PKG_DIR.parent
 CSRC = PKG_DIR / "csrc"
 LIB_DIR = PKG_DIR / "lib"
 LIB = LIB_DIR / "libdsv4moe.so"
+TORCH_OPS_LIB = LIB_DIR / "libdsv4moe_torch.so"
 INCLUDE = REPO / "include"
 
 SOURCES = ["dsv4moe.cu", "loader.cpp"]
@@ -79,6 +82,39 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     return LIB
 
 
+def _torch_flags() -> tuple[list[str], list[str]]:
+    import torch
+    import torch.utils.cpp_extension as ext
+
+    inc = [f"-I{p}" for p in ext.include_paths()] + [f"-I{Path(nvcc()).parent.parent / 'include'}"]
+    libs = [f"-L{p}" for p in ext.library_paths()] + [f"-Wl,-rpath,{p}" for p in ext.library_paths()]
+    abi = int(torch.compiled_with_cxx11_abi())
+    return inc + [f"-D_GLIBCXX_USE_CXX11_ABI={abi}"], libs + ["-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu",
+                                                              "-ltorch_cuda"]
+
+
+def build_torch_ops(force: bool = False) -> Path:
+    """libdsv4moe_torch.so: the TORCH_LIBRARY(dsv4moe) op layer (csrc/torch_ops.cpp)
+    over libdsv4moe.so, compiled with g++ against the installed torch headers
+    (no CUDA code of its own) and loaded with torch.ops.load_library."""
+    src = CSRC / "torch_ops.cpp"
+    lib = build(force)
+    if not force and TORCH_OPS_LIB.exists() and TORCH_OPS_LIB.stat().st_mtime > max(
+            src.stat().st_mtime, lib.stat().st_mtime, (INCLUDE / "dsv4moe.h").stat().st_mtime,
+            Path(__file__).stat().st_mtime):
+        return TORCH_OPS_LIB
+    cflags, ldflags = _torch_flags()
+    tmp = TORCH_OPS_LIB.with_suffix(".so.tmp")
+    cmd = ["g++", "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden", *cflags, f"-I{INCLUDE}",
+           str(src), "-o", str(tmp), f"-L{LIB_DIR}", "-ldsv4moe", "-Wl,-rpath,$ORIGIN", *ldflags]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"g++ failed on torch_ops.cpp:\n{r.stdout}\n{r.stderr}")
+    os.replace(tmp, TORCH_OPS_LIB)
+    return TORCH_OPS_LIB
+
+
 if __name__ == "__main__":
     path = build(force="--force" in sys.argv, verbose="-v" in sys.argv)
     print(path)
+    print(build_torch_ops(force="--force" in sys.argv))

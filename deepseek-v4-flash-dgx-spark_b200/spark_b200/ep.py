@@ -35,7 +35,7 @@ import ctypes
 import torch
 import torch.distributed as dist
 
-from . import _lib
+from . import _lib, ops
 from ._lib import check, ptr, stream_ptr
 
 
@@ -61,40 +61,15 @@ class CudaEPOps:
         return self.moe.gate(x)
 
     def dispatch(self, x, weights, indices):
-        T, W, k = x.shape[0], self.world, self.topk
-        send = torch.empty((max(T * min(W, k), 1), self.row_bytes), dtype=torch.uint8, device=x.device)
-        counts = torch.empty((W, 2), dtype=torch.int32, device=x.device)
-        ret_pos = torch.empty((max(T, 1), k), dtype=torch.int32, device=x.device)
-        ws = torch.empty(max(int(self.lib.dsv4_ep_dispatch_workspace_bytes(T, W)), 1), dtype=torch.uint8,
-                         device=x.device)
-        weights = weights.to(torch.float32).contiguous()
-        indices = indices.to(torch.int64).contiguous()
-        check(self.lib.dsv4_ep_dispatch(ptr(x), ptr(indices), ptr(weights), T, self.hidden, k, self.n_routed, W,
-                                        ptr(send), send.shape[0], ptr(counts), ptr(ret_pos), ptr(ws), ws.numel(),
-                                        stream_ptr()), "dsv4_ep_dispatch")
-        return send, counts, ret_pos
+        return ops.load().ep_dispatch(x, indices, weights, self.n_routed, self.world)
 
     def expert_forward(self, x, recv, recv_counts, n_ret):
-        T, R = x.shape[0], recv.shape[0]
-        self._desc = self.moe.layer_desc()
-        need = int(self.lib.dsv4_ep_expert_workspace_bytes(ctypes.byref(self._desc), self.world, T, R))
-        if need < 0:
-            raise RuntimeError("dsv4_ep_expert_workspace_bytes: invalid layer")
-        ws = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device)
-        ret_send = torch.empty((n_ret, self.hidden), dtype=torch.bfloat16, device=x.device)
-        check(self.lib.dsv4_ep_expert_forward(ctypes.byref(self._desc), self.rank, self.world, ptr(x), T,
-                                              ptr(recv), R, ptr(recv_counts), ptr(ret_send), n_ret, ptr(ws),
-                                              ws.numel(), stream_ptr()), "dsv4_ep_expert_forward")
-        return ret_send, ws
+        return ops.load().ep_expert_forward(*self.moe.layer_args(), self.rank, self.world, x, recv, recv_counts,
+                                            n_ret)
 
     def combine(self, ret_recv, ret_pos, indices, x, R, state):
-        ws = state
-        y = torch.empty_like(x)
-        indices = indices.to(torch.int64).contiguous()
-        check(self.lib.dsv4_ep_combine(ctypes.byref(self._desc), self.rank, self.world, ptr(ret_recv), ptr(ret_pos),
-                                       ptr(indices), x.shape[0], R, ptr(ws), ws.numel(), ptr(y), stream_ptr()),
-              "dsv4_ep_combine")
-        return y
+        return ops.load().ep_combine(*self.moe.layer_args(), self.rank, self.world, ret_recv, ret_pos, indices, x,
+                                     R, state)
 
 
 def _a2a_rows(out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits, group) -> None:
@@ -254,40 +229,27 @@ class PeerExchange:
 
 def peer_dispatch(ex: PeerExchange, x, weights, indices, epoch: int):
     """Step 1 over peer memory: this rank's rows into every owner's buffer."""
-    T, k = x.shape[0], ex.moe.n_activated_experts
+    T = x.shape[0]
     if T > ex.cap:
         raise RuntimeError(f"{T} tokens exceed the exchange capacity of {ex.cap}")
-    ret_pos = torch.empty((max(T, 1), k), dtype=torch.int32, device=x.device)
-    ws = torch.empty(max(int(ex.lib.dsv4_ep_p2p_dispatch_workspace_bytes(T, ex.world)), 1), dtype=torch.uint8,
-                     device=x.device)
-    weights = weights.to(torch.float32).contiguous()
     indices = indices.to(torch.int64).contiguous()
-    check(ex.lib.dsv4_ep_dispatch_p2p(ptr(x), ptr(indices), ptr(weights), T, ex.moe.dim, k,
-                                      ex.moe.n_routed_experts, ex.world, ex.rank, ptr(ex.peer_bases), ex.cap,
-                                      epoch, ptr(ret_pos), ptr(ws), ws.numel(), stream_ptr()),
-          "dsv4_ep_dispatch_p2p")
+    ret_pos = ops.load().ep_dispatch_p2p(x, indices, weights, ex.moe.n_routed_experts, ex.world, ex.rank,
+                                         ex.peer_bases, ex.cap, epoch)
     return ret_pos, indices
 
 
 def peer_expert_forward(ex: PeerExchange, x, epoch: int):
     """Step 3 over peer memory: wait for every source, compute, return rows."""
-    T = x.shape[0]
-    ws = ex.workspace(T)
-    d = ex.moe.layer_desc()
-    check(ex.lib.dsv4_ep_expert_forward_p2p(ctypes.byref(d), ex.rank, ex.world, ptr(x), T, ex.buf,
-                                            ptr(ex.peer_bases), ex.cap, epoch, ptr(ws), ws.numel(), stream_ptr()),
-          "dsv4_ep_expert_forward_p2p")
+    ws = ex.workspace(x.shape[0])
+    ops.load().ep_expert_forward_p2p(*ex.moe.layer_args(), ex.rank, ex.world, x, ex.buf.value, ex.peer_bases,
+                                     ex.cap, epoch, ws)
     return ws
 
 
 def peer_combine(ex: PeerExchange, x, ret_pos, indices, ws, epoch: int):
     """Step 5 over peer memory: wait for every owner's returns, combine."""
-    y = torch.empty_like(x)
-    d = ex.moe.layer_desc()
-    check(ex.lib.dsv4_ep_combine_p2p(ctypes.byref(d), ex.rank, ex.world, ex.buf, ptr(ret_pos), ptr(indices),
-                                     x.shape[0], ex.cap, epoch, ptr(ws), ws.numel(), ptr(y), stream_ptr()),
-          "dsv4_ep_combine_p2p")
-    return y
+    return ops.load().ep_combine_p2p(*ex.moe.layer_args(), ex.rank, ex.world, ex.buf.value, ret_pos, indices, x,
+                                     ex.cap, epoch, ws)
 
 
 def ep_forward_peer(ex: PeerExchange, x: torch.Tensor, routing=None) -> torch.Tensor:

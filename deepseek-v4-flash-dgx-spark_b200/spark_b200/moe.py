@@ -27,8 +27,10 @@ import torch
 import torch.distributed as dist
 from torch import nn
 
-from . import _lib
-from ._lib import MoELayerDesc, check, ptr, stream_ptr
+from contextlib import nullcontext as _nullcontext
+
+from . import _lib, ops
+from ._lib import MoELayerDesc, ptr
 
 FP4 = torch.float4_e2m1fn_x2
 E8M0 = torch.float8_e8m0fnu
@@ -151,17 +153,14 @@ class Expert(nn.Module):
         self.register_load_state_dict_post_hook(lambda m, _keys: m.refresh_scale_atoms())
 
     def refresh_scale_atoms(self, stream=None) -> None:
-        lib = _lib.load()
-        if self.fp4:
-            check(lib.dsv4_build_scale_atoms(ptr(self.block), self.block.numel(), ptr(self._slot0), 1,
-                                             self.dim, self.inter_dim, ptr(self.scale_atoms),
-                                             self.scale_atoms.numel(), stream_ptr(stream)),
-                  "dsv4_build_scale_atoms")
-        else:
-            check(lib.dsv4_build_shared_scale_atoms(ptr(self.w1.scale), ptr(self.w2.scale), ptr(self.w3.scale),
-                                                    self.dim, self.inter_dim, ptr(self.scale_atoms),
-                                                    stream_ptr(stream)),
-                  "dsv4_build_shared_scale_atoms")
+        dsv4 = ops.load()
+        with torch.cuda.stream(stream) if stream is not None else _nullcontext():
+            if self.fp4:
+                dsv4.build_scale_atoms(self.block, self.block.numel(), self._slot0, self.dim, self.inter_dim,
+                                       self.scale_atoms, self.scale_atoms.numel())
+            else:
+                dsv4.build_shared_scale_atoms(self.w1.scale, self.w2.scale, self.w3.scale, self.dim, self.inter_dim,
+                                              self.scale_atoms)
 
     def _desc(self) -> MoELayerDesc:
         d = MoELayerDesc()
@@ -182,25 +181,27 @@ class Expert(nn.Module):
             d.shared_sf = ptr(self.scale_atoms)
         return d
 
+    def layer_args(self) -> tuple[list, list[int], list[float]]:
+        """The op layer's (layer, dims, scalars) lists for this expert."""
+        if self.fp4:
+            tensors = [None, None, self.block, self.scale_atoms, self._slot0, None, None, None, None]
+        else:
+            tensors = [None, None, None, None, None, self.w1.weight, self.w2.weight, self.w3.weight,
+                       self.scale_atoms]
+        return ops.layer_args(self._desc(), tensors)
+
     def forward(self, x: torch.Tensor, weights: torch.Tensor | None = None) -> torch.Tensor:
         shape = x.shape
         x2 = x.reshape(-1, self.dim)
         if x2.dtype != torch.bfloat16:
             x2 = x2.to(torch.bfloat16)
         x2 = x2.contiguous()
-        T = x2.shape[0]
-        y = torch.empty(T, self.dim, dtype=torch.bfloat16, device=x2.device)
         w = None
         if weights is not None:
             w = weights.reshape(-1).to(torch.float32).contiguous()
-            if w.numel() != T:
+            if w.numel() != x2.shape[0]:
                 raise RuntimeError("routing weights must have one entry per row")
-        d = self._desc()
-        lib = _lib.load()
-        ws_bytes = lib.dsv4_expert_workspace_bytes(ctypes.byref(d), T)
-        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x2.device)
-        check(lib.dsv4_expert_forward(ctypes.byref(d), 0 if self.fp4 else -1, ptr(x2), T, ptr(w), ptr(y),
-                                      ptr(ws), ws_bytes, stream_ptr()), "dsv4_expert_forward")
+        y = ops.load().expert_forward(x2, 0 if self.fp4 else -1, w, *self.layer_args())
         return y.view(*shape[:-1], self.dim).to(x.dtype)
 
 
@@ -289,10 +290,9 @@ class ExpertArena:
         bf16_stride = 0
         if bf16_out is not None:
             bf16_stride = bf16_out.shape[-1] if bf16_out.dim() > 1 else bf16_out.numel() // max(self.max_slots, 1)
-        check(_lib.load().dsv4_materialize(ptr(slab), ptr(off), ptr(sl), n, self.dim, self.inter,
-                                           ptr(self.buffer), self.slot_stride, ptr(self.sf), self.sf_stride,
-                                           ptr(bf16_out), bf16_stride, stream_ptr(stream)),
-              "dsv4_materialize")
+        with torch.cuda.stream(stream) if stream is not None else _nullcontext():
+            ops.load().materialize(slab, off, sl, self.buffer, self.slot_stride, self.sf, self.sf_stride, bf16_out,
+                                   bf16_stride, self.dim, self.inter)
         from .telemetry import expert_telemetry
 
         expert_telemetry().record_materialize(n * self.block_bytes)
@@ -334,49 +334,23 @@ class Gate(nn.Module):
 
     def logits(self, x: torch.Tensor) -> torch.Tensor:
         x = x.reshape(-1, self.dim).to(torch.bfloat16).contiguous()
-        out = torch.empty(x.shape[0], self.n_experts, dtype=torch.float32, device=x.device)
-        check(_lib.load().dsv4_gate_logits(ptr(x), ptr(self.weight), int(self.weight.dtype == torch.float32),
-                                           x.shape[0], self.dim, self.n_experts, ptr(out), stream_ptr()),
-              "dsv4_gate_logits")
-        return out
+        return ops.load().gate_logits(x, self.weight)
 
     def route(self, logits: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        logits = logits.to(torch.float32).contiguous()
-        T = logits.shape[0]
-        w = torch.empty(T, self.topk, dtype=torch.float32, device=logits.device)
-        idx = torch.empty(T, self.topk, dtype=torch.int64, device=logits.device)
-        check(_lib.load().dsv4_gate_topk(ptr(logits), ptr(self.bias), T, self.n_experts, self.topk,
-                                         self.route_scale, ptr(w), ptr(idx), stream_ptr()),
-              "dsv4_gate_topk")
-        return w, idx
+        return ops.load().gate_topk(logits.to(torch.float32).contiguous(), self.bias, self.topk, self.route_scale)
 
     def forward(self, x: torch.Tensor, input_ids: torch.Tensor | None = None):
         x = x.reshape(-1, self.dim).to(torch.bfloat16).contiguous()
-        T = x.shape[0]
-        logits = torch.empty(T, self.n_experts, dtype=torch.float32, device=x.device)
-        w = torch.empty(T, self.topk, dtype=torch.float32, device=x.device)
-        idx = torch.empty(T, self.topk, dtype=torch.int64, device=x.device)
-        lib = _lib.load()
-        fp32 = int(self.weight.dtype == torch.float32)
+        dsv4 = ops.load()
         if self.hashed:
             if input_ids is None:
                 raise RuntimeError(f"layer {self.layer_id} routes by token id: input_ids is required")
             ids = input_ids.reshape(-1).to(device=x.device, dtype=torch.int64).contiguous()
-            if ids.numel() != T:
+            if ids.numel() != x.shape[0]:
                 raise RuntimeError("input_ids must hold one id per token")
-            need = lib.dsv4_gate_hash_workspace_bytes(ptr(self.weight), fp32, T, self.dim, self.n_experts)
-            ws = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device) if need > 0 else None
-            check(lib.dsv4_gate_route_hash(ptr(x), ptr(self.weight), fp32, ptr(self.tid2eid), self.tid2eid.shape[0],
-                                           ptr(ids), T, self.dim, self.n_experts, self.topk, self.route_scale,
-                                           ptr(logits), ptr(w), ptr(idx), ptr(ws), max(need, 0), stream_ptr()),
-                  "dsv4_gate_route_hash")
-            self.last_logits = logits
-            return w, idx
-        need = lib.dsv4_gate_workspace_bytes(ptr(self.weight), fp32, T, self.dim, self.n_experts)
-        ws = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device) if need > 0 else None
-        check(lib.dsv4_gate_route(ptr(x), ptr(self.weight), fp32, ptr(self.bias), T, self.dim, self.n_experts,
-                                  self.topk, self.route_scale, ptr(logits), ptr(w), ptr(idx), ptr(ws),
-                                  max(need, 0), stream_ptr()), "dsv4_gate_route")
+            w, idx, logits = dsv4.gate_route(x, self.weight, None, self.topk, self.route_scale, self.tid2eid, ids)
+        else:
+            w, idx, logits = dsv4.gate_route(x, self.weight, self.bias, self.topk, self.route_scale)
         self.last_logits = logits
         return w, idx
 
@@ -447,10 +421,8 @@ class MoE(nn.Module):
 
     def refresh_scale_atoms(self) -> None:
         slots = self.expert_slot[self.experts_start_idx:self.experts_end_idx].contiguous()
-        check(_lib.load().dsv4_build_scale_atoms(ptr(self.arena.buffer), self.arena.slot_stride, ptr(slots),
-                                                 slots.numel(), self.dim, self.args.moe_inter_dim,
-                                                 ptr(self.arena.sf), self.arena.sf_stride, stream_ptr()),
-              "dsv4_build_scale_atoms")
+        ops.load().build_scale_atoms(self.arena.buffer, self.arena.slot_stride, slots, self.dim,
+                                     self.args.moe_inter_dim, self.arena.sf, self.arena.sf_stride)
         self.shared_experts.refresh_scale_atoms()
 
     def layer_desc(self) -> MoELayerDesc:
@@ -470,27 +442,30 @@ class MoE(nn.Module):
         d.shared_sf = ptr(sh.scale_atoms)
         return d
 
+    def layer_args(self) -> tuple[list, list[int], list[float]]:
+        """The op layer's (layer, dims, scalars) lists for this layer."""
+        sh = self.shared_experts
+        tensors = [self.gate.weight, self.gate.bias, self.arena.buffer, self.arena.sf, self.expert_slot,
+                   sh.w1.weight, sh.w2.weight, sh.w3.weight, sh.scale_atoms]
+        return ops.layer_args(self.layer_desc(), tensors)
+
     def workspace_bytes(self, T: int) -> int:
         d = self.layer_desc()
         return int(_lib.load().dsv4_moe_workspace_bytes(ctypes.byref(d), T))
 
     def forward_tokens(self, x: torch.Tensor, *, routing: tuple[torch.Tensor, torch.Tensor] | None = None,
                        workspace: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
-        """Single-rank layer over x [T,H] bf16 -> [T,H] bf16 (no host sync)."""
-        T = x.shape[0]
-        d = self.layer_desc()
-        lib = _lib.load()
-        need = lib.dsv4_moe_workspace_bytes(ctypes.byref(d), T)
-        if workspace is None or workspace.numel() < need:
-            workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device)
-        y = out if out is not None else torch.empty_like(x)
+        """Single-rank layer over x [T,H] bf16 -> [T,H] bf16 (no host sync), one
+        ``torch.ops.dsv4moe.moe_forward`` call."""
         rw = ri = None
         if routing is not None:
             rw = routing[0].to(torch.float32).contiguous()
             ri = routing[1].to(torch.int64).contiguous()
-        check(lib.dsv4_moe_forward(ctypes.byref(d), ptr(x), T, ptr(y), ptr(rw), ptr(ri), ptr(workspace),
-                                   workspace.numel(), stream_ptr()), "dsv4_moe_forward")
-        return y
+        dsv4 = ops.load()
+        if out is None:
+            return dsv4.moe_forward(x, *self.layer_args(), rw, ri, workspace)
+        dsv4.moe_forward_out(x, *self.layer_args(), rw, ri, workspace, out)
+        return out
 
     def forward(self, x: torch.Tensor, input_ids: torch.Tensor | None = None) -> torch.Tensor:
         shape = x.size()
