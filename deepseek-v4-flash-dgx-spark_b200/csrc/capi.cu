@@ -109,7 +109,9 @@ static int gate_route(const void* x, const void* w, int w_fp32, const float* bia
 // ---------------------------------------------------------------------------
 struct Plan {
   int T, E, k, H, I, S, block_n, max_rows, max_tiles;
-  long long off[19];
+  int split1, split2;  // split-K slices of GEMM1 / GEMM2 (1 = none)
+  int part_rows;       // compact rows of the split-K partial sums
+  long long off[21];
   long long total;
 };
 
@@ -130,6 +132,26 @@ static int choose_block_n(int T, int k, int E) {
   if (avg <= 48) return 64;
   if (avg <= 2048) return 128;
   return 256;
+}
+
+// Split-K slices for the decode-size GEMMs: with few tokens the layer has few
+// (segment tile, weight block) items, each a long serial stream of k tiles, so
+// most SMs would idle.  Cut each item's k range into S slices (S divides the
+// K/512 scale groups) until there are >= 16 units per SM.
+// DSV4_KSPLIT forces S (tuning).
+static int choose_k_split(int T, int k, int E, int block_n, int nb, int kt, int nsm) {
+  const int groups = kt / 4;
+  static const int forced = env_int("DSV4_KSPLIT", 0, 0, 64);
+  if (block_n > 64 || groups < 2) return 1;
+  int s = 1;
+  if (forced) {
+    while (s * 2 <= forced && s * 2 <= groups) s *= 2;
+  } else {
+    const long long tiles = (long long)((long long)T * k < E ? (long long)T * k : E) + 1;
+    while (s * 2 <= groups && tiles * nb * s < 16LL * nsm) s *= 2;
+  }
+  while (groups % s) s >>= 1;
+  return s;
 }
 
 static int validate(const dsv4_moe_layer* L) {
@@ -173,7 +195,14 @@ static Plan make_plan(const dsv4_moe_layer* L, int T, int E_local = -1) {
   p.max_tiles = (int)(((long long)T * p.k + (long long)T * p.S) / p.block_n + p.E + 2);
   const long long atom_groups = p.max_rows / 32 + 4;
   const long long nchunks = T > 0 ? (T + route_chunk_tokens(T) - 1) / route_chunk_tokens(T) : 0;
-  long long sz[19] = {
+  const int nsm = num_sms();
+  const int nb1 = p.I / 128, nb2 = p.H / 256;
+  p.split1 = choose_k_split(T, p.k, p.E, p.block_n, nb1, p.H / 128, nsm);
+  p.split2 = choose_k_split(T, p.k, p.E, p.block_n, nb2, p.I / 128, nsm);
+  p.part_rows = T * p.k + T * p.S;
+  const int smax = p.split1 > p.split2 ? p.split1 : p.split2;
+  const long long part_ld = (long long)(nb1 * 256 > nb2 * 256 ? nb1 * 256 : nb2 * 256);
+  long long sz[21] = {
       (long long)T * (p.E > p.k ? p.E : p.k) * 4,  // logits (expert parallel: return rows)
       (long long)T * p.k * 4,                 // weights
       (long long)T * p.k * 8,                 // indices
@@ -189,15 +218,17 @@ static Plan make_plan(const dsv4_moe_layer* L, int T, int E_local = -1) {
       (long long)p.max_rows * p.I,            // hq
       atom_groups * (p.I / 512) * 512,        // hsf
       (long long)p.max_rows * p.H * 2,        // O
-      E_local < 0 ? gate_partials_bytes(T, p.H, p.E, num_sms(),
+      E_local < 0 ? gate_partials_bytes(T, p.H, p.E, nsm,
                                         L->gate_w && !L->gate_w_fp32 && p.E == 256)
                   : 0,                        // gate partial logits
       (long long)p.E * nchunks * 4,           // per-chunk expert counts
       (long long)p.E * nchunks * 4,           // per-chunk segment offsets
       16,                                     // plan control words
+      smax > 1 ? (long long)smax * p.part_rows * part_ld * 4 : 0,  // split-K partial sums
+      smax > 1 ? (long long)p.max_tiles * (nb1 + nb2) * 4 : 0,     // split-K item counters
   };
   long long o = 0;
-  for (int i = 0; i < 19; ++i) {
+  for (int i = 0; i < 21; ++i) {
     p.off[i] = o;
     o += align256(sz[i]);
   }
@@ -225,11 +256,36 @@ static int make_pair_sf_maps(const dsv4_moe_layer* L, PairMaps* pm, const uint8_
 
 // GEMM1 (w1|w3 + SwiGLU + re-quant) then GEMM2 (w2) over a routing plan.
 // out_bf16 receives the expert rows [max_rows, H] (row = plan slot).
+// Split-K buffers of one layer call (see choose_k_split); split1/split2 = 1: none.
+struct SplitK {
+  int split1 = 1, split2 = 1;
+  float* partial = nullptr;
+  int part_rows = 0;
+  int* done1 = nullptr;  // [max_tiles * I/128] GEMM1 item counters
+  int* done2 = nullptr;  // [max_tiles * H/256] GEMM2 item counters
+};
+
+static SplitK plan_split(const Plan& p, uint8_t* ws) {
+  SplitK k;
+  if (p.split1 == 1 && p.split2 == 1) return k;
+  k.split1 = p.split1;
+  k.split2 = p.split2;
+  k.partial = reinterpret_cast<float*>(ws + p.off[19]);
+  k.part_rows = p.part_rows;
+  k.done1 = reinterpret_cast<int*>(ws + p.off[20]);
+  k.done2 = k.done1 + (size_t)p.max_tiles * (p.I / 128);
+  return k;
+}
+
+static int split_counters(const Plan& p) {
+  return (p.split1 > 1 || p.split2 > 1) ? p.max_tiles * (p.I / 128 + p.H / 256) : 0;
+}
+
 static int run_expert_gemms(const dsv4_moe_layer* L, const int4* tiles, const int* n_tiles,
                             const float* slot_weight, const uint8_t* xq, const uint8_t* xsf,
                             uint8_t* hq, uint8_t* hsf, __nv_bfloat16* out_bf16, int out_ld,
                             int max_rows, int max_tiles, int block_n, const int* expert_slot,
-                            int n_routed, int nsm, cudaStream_t st) {
+                            int n_routed, int nsm, cudaStream_t st, const SplitK& sk = SplitK()) {
   const int H = L->hidden, I = L->inter;
   const bool has_shared = L->shared_w1 != nullptr;
   const bool has_routed = L->arena != nullptr;
@@ -279,6 +335,11 @@ static int run_expert_gemms(const dsv4_moe_layer* L, const int4* tiles, const in
   g1.out_sf = hsf;
   g1.out_ld = I;
   g1.swiglu_limit = L->swiglu_limit;
+  g1.k_split = pair ? 1 : sk.split1;
+  g1.partial = sk.partial;
+  g1.part_rows = sk.part_rows;
+  g1.part_ld = g1.nb_count * 256;
+  g1.item_done = sk.done1;
   // CTA-pair form: maps of the three scale-atom buffers as 256-byte rows
   PairMaps pm;
   int clusters = 0;
@@ -298,7 +359,7 @@ static int run_expert_gemms(const dsv4_moe_layer* L, const int4* tiles, const in
     if ((rc = launch_expert_gemm_pair(true, pm, g1, 0, sc >> 8, 0, sc >> 8, clusters, st)))
       return rc;
   } else {
-    const long long work1 = (long long)max_tiles * g1.nb_count;
+    const long long work1 = (long long)max_tiles * g1.nb_count * g1.k_split;
     const int grid1 = (int)(work1 < nsm ? work1 : nsm);
     if ((rc = launch_expert_gemm(true, block_n, a0, a1, s0, s1, b, g1, grid1, st))) return rc;
   }
@@ -327,6 +388,9 @@ static int run_expert_gemms(const dsv4_moe_layer* L, const int4* tiles, const in
   g2.out_sf = nullptr;
   g2.out_bf16 = out_bf16;
   g2.out_ld = out_ld;
+  g2.k_split = pair ? 1 : sk.split2;
+  g2.part_ld = g2.nb_count * 256;
+  g2.item_done = sk.done2;
   if (pair) {
     int clusters2 = pair_clusters_resident(false);
     if (clusters2 <= 0) return DSV4_ERR_UNSUPPORTED;
@@ -341,7 +405,7 @@ static int run_expert_gemms(const dsv4_moe_layer* L, const int4* tiles, const in
     rc = launch_expert_gemm_pair(false, pm, g2, (2 * sc) >> 8, (2 * sc) >> 8, (2 * sc) >> 8,
                                  (2 * sc) >> 8, clusters2, st);
   } else {
-    const long long work2 = (long long)max_tiles * g2.nb_count;
+    const long long work2 = (long long)max_tiles * g2.nb_count * g2.k_split;
     const int grid2 = (int)(work2 < nsm ? work2 : nsm);
     rc = launch_expert_gemm(false, block_n, a0, a0, s0, s0, b, g2, grid2, st);
   }
@@ -469,6 +533,10 @@ int dsv4_moe_workspace_layout(const dsv4_moe_layer* L, int T, long long* out, in
   out[15] = p.max_rows;
   out[16] = p.block_n;
   if (n_out > 17) out[17] = p.off[15];
+  if (n_out > 19) {
+    out[18] = p.split1;
+    out[19] = p.split2;
+  }
   return DSV4_OK;
 }
 
@@ -585,9 +653,10 @@ int dsv4_moe_forward(const dsv4_moe_layer* L, const void* x, int T, void* y,
   int* chunk_cnt = reinterpret_cast<int*>(ws + p.off[16]);
   int* chunk_base = reinterpret_cast<int*>(ws + p.off[17]);
   int* ctrl = reinterpret_cast<int*>(ws + p.off[18]);
+  const SplitK sk = plan_split(p, ws);
   if ((rc = launch_route_plan(ri, T, k, E, 0, p.S ? T : 0, p.block_n, p.max_rows, p.max_tiles,
                               chunk_cnt, chunk_base, ctrl, counts, seg_start, tiles, n_tiles,
-                              slot_token, slot_weight, st)))
+                              slot_token, slot_weight, st, sk.done1, split_counters(p))))
     return rc;
   stage_mark(2, st);
   if ((rc = launch_route_scatter(x, T, nullptr, 0, ri, rw, T, k, E, H, p.S ? T : 0, seg_start,
@@ -597,7 +666,7 @@ int dsv4_moe_forward(const dsv4_moe_layer* L, const void* x, int T, void* y,
   stage_mark(3, st);
 
   if ((rc = run_expert_gemms(L, tiles, n_tiles, slot_weight, xq, xsf, hq, hsf, O, H, p.max_rows,
-                             p.max_tiles, p.block_n, L->expert_slot, L->n_routed, nsm, st)))
+                             p.max_tiles, p.block_n, L->expert_slot, L->n_routed, nsm, st, sk)))
     return rc;
   rc = launch_combine(O, H, route_slot, ri, T, k, p.S ? seg_start + E : nullptr, y, st);
   stage_mark(6, st);
@@ -796,9 +865,10 @@ int dsv4_ep_expert_forward(const dsv4_moe_layer* L, int rank, int world, const v
                              idx_local, w_local, ret_dst, st)))
     return rc;
   stage_mark(1, st);
+  const SplitK sk = plan_split(p, ws);
   if ((rc = launch_route_plan(idx_local, T, k, e_count, 1, shared_rows, p.block_n, p.max_rows,
                               p.max_tiles, chunk_cnt, chunk_base, ctrl, counts, seg_start, tiles,
-                              n_tiles, slot_token, slot_weight, st)))
+                              n_tiles, slot_token, slot_weight, st, sk.done1, split_counters(p))))
     return rc;
   stage_mark(2, st);
   if ((rc = launch_route_scatter(x_own, T_own, rows_in, ep_row_bytes(H, k), idx_local, w_local, T,
@@ -807,7 +877,7 @@ int dsv4_ep_expert_forward(const dsv4_moe_layer* L, int rank, int world, const v
     return rc;
   stage_mark(3, st);
   if ((rc = run_expert_gemms(L, tiles, n_tiles, slot_weight, xq, xsf, hq, hsf, O, H, p.max_rows,
-                             p.max_tiles, p.block_n, L->expert_slot + e_begin, e_count, nsm, st)))
+                             p.max_tiles, p.block_n, L->expert_slot + e_begin, e_count, nsm, st, sk)))
     return rc;
   rc = launch_ep_return_gather(O, H, route_slot, ret_dst, T * k, ret_rows, ret_send, nsm, st);
   stage_mark(6, st);
@@ -962,9 +1032,10 @@ int dsv4_ep_expert_forward_p2p(const dsv4_moe_layer* L, int rank, int world, con
                                  idx_local, w_local, ret_dst, st)))
     return rc;
   stage_mark(1, st);
+  const SplitK sk = plan_split(p, ws);
   if ((rc = launch_route_plan(idx_local, T, k, e_count, 1, shared_rows, p.block_n, p.max_rows,
                               p.max_tiles, chunk_cnt, chunk_base, ctrl, counts, seg_start, tiles,
-                              n_tiles, slot_token, slot_weight, st)))
+                              n_tiles, slot_token, slot_weight, st, sk.done1, split_counters(p))))
     return rc;
   stage_mark(2, st);
   if ((rc = launch_route_scatter(x_own, T_own, exch + kEpHeaderBytes, ep_row_bytes(H, k), idx_local,
@@ -973,7 +1044,7 @@ int dsv4_ep_expert_forward_p2p(const dsv4_moe_layer* L, int rank, int world, con
     return rc;
   stage_mark(3, st);
   if ((rc = run_expert_gemms(L, tiles, n_tiles, slot_weight, xq, xsf, hq, hsf, O, H, p.max_rows,
-                             p.max_tiles, p.block_n, L->expert_slot + e_begin, e_count, nsm, st)))
+                             p.max_tiles, p.block_n, L->expert_slot + e_begin, e_count, nsm, st, sk)))
     return rc;
   rc = launch_ep_return_p2p(O, H, k, route_slot, ret_dst, T * k, peer_bases, rank, world,
                             cap_tokens, epoch, nsm, st);

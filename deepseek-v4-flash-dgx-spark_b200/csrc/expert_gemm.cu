@@ -136,17 +136,21 @@ __device__ __forceinline__ void gemm_produce(const CUtensorMap* tmW0p, const CUt
   int stage = 0;
   uint32_t phase = 0;
   int sf_slot = 1;  // ring slot of the current k-tile group (flips at each group)
+  const int S = args.k_split, KTS = KT / S;  // k-range slices per item, k tiles per slice
   ItemInfo cur, nxt;
-  if ((int)blockIdx.x < total) cur = decode_item<GATED>(args, blockIdx.x, NB, KT);
+  if ((int)blockIdx.x < total) cur = decode_item<GATED>(args, blockIdx.x / S, NB, KT);
+  // work units are (item, slice); slices start on a group of four k tiles, so
+  // the scale-atom ring flips at the same k tiles as without a split
   for (int w = blockIdx.x; w < total && !*abort_flag; w += step) {
-    // the next item's descriptor loads are issued now and used one item
-    // later, so their latency hides behind this item's k loop
-    if (w + step < total) nxt = decode_item<GATED>(args, w + step, NB, KT);
+    // the next unit's descriptor loads are issued now and used one unit
+    // later, so their latency hides behind this unit's k loop
+    if (w + step < total) nxt = decode_item<GATED>(args, (w + step) / S, NB, KT);
     const size_t g0 = (size_t)(cur.row0 >> 5);
     // transaction bytes count what the TMA reads from global memory: an e2m1
     // box is 8 KB there even though it spreads to 16 KB (16U4_ALIGN16B) in smem
     const uint32_t tx_base = C::A_BYTES + 2u * (cur.shared ? C::B_HALF : C::B_HALF / 2);
-    for (int kt = 0; kt < KT; ++kt) {
+    const int kt0 = (w % S) * KTS;
+    for (int kt = kt0; kt < kt0 + KTS; ++kt) {
       if (!mbar_wait(&empty[stage], phase ^ 1, DSV4_DEVERR_TIMEOUT_PRODUCER)) {
         *abort_flag = 1;
         break;
@@ -187,6 +191,109 @@ __device__ __forceinline__ void gemm_produce(const CUtensorMap* tmW0p, const CUt
   }
 }
 
+// Split-K epilogue of one (item, slice) unit.  Every thread drains its row's
+// 256 fp32 accumulator columns and stores those of valid rows to the slice's
+// partial rows; then the CTA counts the slice as finished.  The CTA whose
+// slice is the item's last adds the item's S partial rows in slice order
+// (the same sum whichever CTA is last) and applies the single-pass epilogue
+// arithmetic: four warps take rows in turn, each lane 8 of the 256 columns.
+template <bool GATED>
+__device__ __forceinline__ void split_epilogue(const GemmArgs& args, uint32_t taddr, bool warp_rows,
+                                               int r, int q, int lane, int item, int slice,
+                                               const int4& tl, int jb, uint64_t* acc_empty,
+                                               volatile int* split_last) {
+  const int S = args.k_split, nrows = tl.z;
+  if (warp_rows) {
+    float* prow = args.partial + ((size_t)slice * args.part_rows + tl.w + r) * args.part_ld + jb * 256;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t a[32], b[32];
+      tmem_ld32_issue(taddr + 64 * c, a);
+      tmem_ld32_issue(taddr + 64 * c + 32, b);
+      tmem_wait_ld2(a, b);
+      if (r < nrows) {
+        float4* d = reinterpret_cast<float4*>(prow + 64 * c);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          d[i] = make_float4(__uint_as_float(a[4 * i]), __uint_as_float(a[4 * i + 1]),
+                             __uint_as_float(a[4 * i + 2]), __uint_as_float(a[4 * i + 3]));
+          d[8 + i] = make_float4(__uint_as_float(b[4 * i]), __uint_as_float(b[4 * i + 1]),
+                                 __uint_as_float(b[4 * i + 2]), __uint_as_float(b[4 * i + 3]));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  mbar_arrive(acc_empty);
+  __threadfence();  // this thread's partial stores, before the count
+  epi_bar();
+  if (threadIdx.x == 64) *split_last = atomicAdd(args.item_done + item, 1) == S - 1;
+  epi_bar();
+  const bool last = *split_last != 0;
+  epi_bar();  // everyone read the flag before the next unit may overwrite it
+  if (!last) return;
+  __threadfence();
+  for (int rr = q; rr < nrows; rr += 4) {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    for (int sl = 0; sl < S; ++sl) {
+      const float4* p = reinterpret_cast<const float4*>(
+          args.partial + ((size_t)sl * args.part_rows + tl.w + rr) * args.part_ld + jb * 256 + 8 * lane);
+      const float4 x0 = __ldcg(p), x1 = __ldcg(p + 1);
+      v[0] += x0.x; v[1] += x0.y; v[2] += x0.z; v[3] += x0.w;
+      v[4] += x1.x; v[5] += x1.y; v[6] += x1.z; v[7] += x1.w;
+    }
+    const int row = tl.y + rr;
+    if (GATED) {
+      // lanes 0..15 hold g columns 8*lane.., lanes 16..31 the u columns of the same units
+      float gb[8], ub[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        gb[i] = bf16_round(v[i]);
+        ub[i] = __shfl_down_sync(0xffffffffu, gb[i], 16);
+      }
+      const float lim = args.swiglu_limit;
+      const float wr = args.slot_weight[row];
+      float hv[8], amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float g = gb[i], u = ub[i];
+        if (lim > 0.f) {
+          u = fminf(fmaxf(u, -lim), lim);
+          g = fminf(g, lim);
+        }
+        const float sg = __fdividef(g, 1.0f + __expf(-g));
+        hv[i] = bf16_round((sg * u) * wr);
+        amax = fmaxf(amax, fabsf(hv[i]));
+      }
+      if (lane >= 16) amax = 0.f;
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      amax = __shfl_sync(0xffffffffu, amax, 0);
+      const int e = act_scale_exp(amax);
+      const float inv = exp2i(-e);
+      if (lane < 16) {
+        uint8_t* dst = args.out_q + (size_t)row * args.out_ld + jb * 128 + 8 * lane;
+        *reinterpret_cast<uint2*>(dst) =
+            make_uint2(e4m3x4(hv[0] * inv, hv[1] * inv, hv[2] * inv, hv[3] * inv),
+                       e4m3x4(hv[4] * inv, hv[5] * inv, hv[6] * inv, hv[7] * inv));
+      }
+      if (lane == 0)
+        write_row_scale(args.out_sf, row, jb, (args.out_ld >> 7) >> 2, static_cast<uint8_t>(e + 127));
+    } else {
+      uint32_t pk[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+        pk[i] = *reinterpret_cast<const uint32_t*>(&b2);
+      }
+      *reinterpret_cast<uint4*>(args.out_bf16 + (size_t)row * args.out_ld + jb * 256 + 8 * lane) =
+          make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+  }
+}
+
 template <int BM, bool GATED>
 __global__ void __launch_bounds__(192, 1)
     expert_gemm_kernel(const __grid_constant__ CUtensorMap tmW0,
@@ -209,6 +316,7 @@ __global__ void __launch_bounds__(192, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* epi_abort = abort_flag + 1;
+  volatile int* split_last = epi_abort + 1;  // this CTA finished the item's last slice
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -239,7 +347,9 @@ __global__ void __launch_bounds__(192, 1)
   const int NB = args.nb_count;
   const int KT = args.kt_count;
   const int KT4 = KT >> 2;
-  const int total = *args.n_tiles * NB;
+  const int S = args.k_split;
+  const int KTS = KT / S;
+  const int total = *args.n_tiles * NB * S;
   const int step = (int)gridDim.x;
 
   if (warp == 0) {
@@ -257,10 +367,11 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t sfa_t = tmem + C::SFA_COL;
       const uint32_t sfb_t = tmem + C::SFB_COL;
       int4 tl_next = make_int4(0, 0, 0, 0);
-      if ((int)blockIdx.x < total) tl_next = args.tiles[blockIdx.x / NB];
+      if ((int)blockIdx.x < total) tl_next = args.tiles[blockIdx.x / S / NB];
       for (int w = blockIdx.x; w < total && !*abort_flag; w += step) {
         const int4 tl = tl_next;
-        if (w + step < total) tl_next = args.tiles[(w + step) / NB];
+        if (w + step < total) tl_next = args.tiles[(w + step) / S / NB];
+        const int kt0 = (w % S) * KTS;
         const uint32_t b_fmt = tl.x >= args.n_routed ? 0u : 5u;  // e4m3 shared, e2m1 routed
         if (!mbar_wait(acc_empty, aphase ^ 1, DSV4_DEVERR_TIMEOUT_MMA)) {
           *abort_flag = 1;
@@ -268,7 +379,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         tc_fence_after();
         bool ok = true;
-        for (int kt = 0; kt < KT; ++kt) {
+        for (int kt = kt0; kt < kt0 + KTS; ++kt) {
           if (!mbar_wait(&full[stage], phase, DSV4_DEVERR_TIMEOUT_MMA)) {
             ok = false;
             break;
@@ -296,7 +407,7 @@ __global__ void __launch_bounds__(192, 1)
           for (int kk = 0; kk < 4; ++kk) {
             const uint32_t idesc = idesc_mxf8f6f4(0u, b_fmt, 256, kt & 3, kk);
             tc_mma_mxf8f6f4(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, sfa_k, sfb_k,
-                            (kt > 0 || kk > 0) ? 1u : 0u);
+                            (kt > kt0 || kk > 0) ? 1u : 0u);
           }
           tc_commit(&empty[stage]);
           if (++stage == C::STAGES) {
@@ -327,8 +438,9 @@ __global__ void __launch_bounds__(192, 1)
     const float lim = args.swiglu_limit;
     const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
     for (int w = blockIdx.x; w < total; w += step) {
-      const int4 tl = args.tiles[w / NB];
-      const int jb = w % NB;
+      const int item = w / S;
+      const int4 tl = args.tiles[item / NB];
+      const int jb = item % NB;
       const int row0 = tl.y, nrows = tl.z;
       // epi_abort is written only by epilogue warps and read between two
       // barriers, so all four see the same value.
@@ -343,6 +455,11 @@ __global__ void __launch_bounds__(192, 1)
       aphase ^= 1;
       tc_fence_after();
       const bool warp_rows = q * 32 < nrows;  // TMEM lanes of this quarter hold real rows
+      if (S > 1) {
+        split_epilogue<GATED>(args, taddr, warp_rows, r, q, lane, item, w % S, tl, jb, acc_empty,
+                              split_last);
+        continue;
+      }
       uint32_t pk[128];                       // packed bf16 pairs out of TMEM
       if (warp_rows) {
         // 64 columns in flight per wait: the accumulator goes back to the MMA

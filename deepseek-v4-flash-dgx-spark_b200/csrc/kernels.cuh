@@ -7,7 +7,7 @@ namespace dsv4 {
 
 // Arguments of the grouped expert GEMM kernel (see expert_gemm.cu).
 struct GemmArgs {
-  const int4* tiles;      // [n_tiles] {segment, row0, nrows, 0}
+  const int4* tiles;      // [n_tiles] {segment, row0, nrows, compact index of row0}
   const int* n_tiles;     // device scalar written by the route plan
   const int* expert_slot; // [n_routed] routed expert -> arena slot
   int n_routed;           // segment id n_routed is the shared expert
@@ -25,6 +25,15 @@ struct GemmArgs {
   __nv_bfloat16* out_bf16;     // GEMM2: O [rows][out_ld]
   int out_ld;
   float swiglu_limit;
+  // split-K (k_split > 1): every item's k tiles are cut into k_split slices
+  // of whole scale groups; a slice stores its fp32 sums of the item's valid
+  // rows in partial[slice][compact row][part_ld], and the CTA that finishes
+  // the item's last slice adds the slices in order and runs the epilogue.
+  int k_split;
+  float* partial;
+  int part_rows;          // compact rows per slice (>= every valid route row)
+  int part_ld;            // floats per compact row: nb_count * 256
+  int* item_done;         // [n_tiles * nb_count] slices finished, zeroed by the route plan
 };
 
 int launch_gate_logits(const void* x, const void* w, int w_is_fp32, int T, int H, int E,
@@ -44,7 +53,8 @@ int route_chunk_tokens(int T);
 int launch_route_plan(const int64_t* indices, int T, int k, int E, int allow_skip,
                       int shared_rows, int block_n, int max_rows, int max_tiles, int* chunk_cnt,
                       int* chunk_base, int* ctrl, int* counts, int* seg_start, int4* tiles,
-                      int* n_tiles, int* slot_token, float* slot_weight, cudaStream_t st);
+                      int* n_tiles, int* slot_token, float* slot_weight, cudaStream_t st,
+                      int* zero_ptr = nullptr, int n_zero = 0);
 int launch_route_scatter(const void* x, int n_x_rows, const uint8_t* rows_in,
                          long long rows_in_stride, const int64_t* indices, const float* weights,
                          int T, int k, int E, int H, int shared_rows, const int* seg_start,

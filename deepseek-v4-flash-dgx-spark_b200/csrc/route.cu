@@ -61,7 +61,8 @@ __device__ void plan_layout(int* s_cnt, int* s_start, int* s_tbase, int NS, int 
                             int max_rows, int max_tiles, int bad, int* __restrict__ counts,
                             int* __restrict__ seg_start, int4* __restrict__ tiles,
                             int* __restrict__ n_tiles, int* __restrict__ slot_token,
-                            float* __restrict__ slot_weight, int* __restrict__ ctrl) {
+                            float* __restrict__ slot_weight, int* __restrict__ ctrl,
+                            int* __restrict__ zero_ptr, int n_zero) {
   __shared__ int s_fail;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
   __syncthreads();
@@ -106,10 +107,19 @@ __device__ void plan_layout(int* s_cnt, int* s_start, int* s_tbase, int NS, int 
     seg_start[s] = s_start[s];
     if (s < NS) counts[s] = s_cnt[s];
   }
+  // split-K item counters of the GEMMs start at zero on every call
+  for (int i = tid; i < n_zero; i += nthr) zero_ptr[i] = 0;
   for (int s = warp; s < NS; s += nthr / 32) {
     const int c = s_cnt[s], base = s_start[s], nt = s_tbase[s + 1] - s_tbase[s];
+    // compact row of the segment's first route: valid rows of earlier segments
+    int vb = 0;
+    for (int j = lane; j < s; j += 32) vb += s_cnt[j];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) vb += __shfl_xor_sync(0xffffffffu, vb, o);
+    // tile = {segment, first plan row, valid rows, compact index of the first row}
     for (int m = lane; m < nt; m += 32)
-      tiles[s_tbase[s] + m] = make_int4(s, base + m * block_n, min(block_n, c - m * block_n), 0);
+      tiles[s_tbase[s] + m] =
+          make_int4(s, base + m * block_n, min(block_n, c - m * block_n), vb + m * block_n);
     for (int r = base + c + lane; r < s_start[s + 1]; r += 32) {
       slot_token[r] = -1;
       slot_weight[r] = 0.f;
@@ -128,7 +138,7 @@ __global__ void __launch_bounds__(1024) route_plan_small_kernel(
     int chunk, int nchunks, int block_n, int max_rows, int max_tiles,
     int* __restrict__ chunk_base, int* __restrict__ counts, int* __restrict__ seg_start,
     int4* __restrict__ tiles, int* __restrict__ n_tiles, int* __restrict__ slot_token,
-    float* __restrict__ slot_weight, int* __restrict__ ctrl) {
+    float* __restrict__ slot_weight, int* __restrict__ ctrl, int* __restrict__ zero_ptr, int n_zero) {
   __shared__ int cnt[kSmallPlanInts];
   __shared__ int s_cnt[kMaxSegments], s_start[kMaxSegments + 1], s_tbase[kMaxSegments + 1];
   __shared__ int s_bad;
@@ -152,14 +162,15 @@ __global__ void __launch_bounds__(1024) route_plan_small_kernel(
   }
   if (tid == 0) s_cnt[E] = shared_rows;
   plan_layout(s_cnt, s_start, s_tbase, E + 1, block_n, max_rows, max_tiles, s_bad, counts,
-              seg_start, tiles, n_tiles, slot_token, slot_weight, ctrl);
+              seg_start, tiles, n_tiles, slot_token, slot_weight, ctrl, zero_ptr, n_zero);
 }
 
 __global__ void __launch_bounds__(kScanThreads) route_scan_kernel(
     const int* __restrict__ chunk_cnt, int nchunks, int E, int shared_rows, int block_n,
     int max_rows, int max_tiles, int* __restrict__ chunk_base, int* __restrict__ counts,
     int* __restrict__ seg_start, int4* __restrict__ tiles, int* __restrict__ n_tiles,
-    int* __restrict__ slot_token, float* __restrict__ slot_weight, int* __restrict__ ctrl) {
+    int* __restrict__ slot_token, float* __restrict__ slot_weight, int* __restrict__ ctrl,
+    int* __restrict__ zero_ptr, int n_zero) {
   __shared__ int s_cnt[kMaxSegments], s_start[kMaxSegments + 1], s_tbase[kMaxSegments + 1];
   __shared__ int s_last;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -194,7 +205,7 @@ __global__ void __launch_bounds__(kScanThreads) route_scan_kernel(
   for (int s = tid; s < E; s += kScanThreads) s_cnt[s] = __ldcg(counts + s);
   if (tid == 0) s_cnt[E] = shared_rows;
   plan_layout(s_cnt, s_start, s_tbase, E + 1, block_n, max_rows, max_tiles, __ldcg(ctrl + 1), counts,
-              seg_start, tiles, n_tiles, slot_token, slot_weight, ctrl);
+              seg_start, tiles, n_tiles, slot_token, slot_weight, ctrl, zero_ptr, n_zero);
 }
 
 // Per-128 act_quant of one token row by one warp, the codes and scales written
@@ -500,7 +511,7 @@ __global__ void single_segment_plan_kernel(int T, int seg, int block_n, int rows
   for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows_pad; r += gridDim.x * blockDim.x) {
     slot_token[r] = r < T ? r : -1;
     slot_weight[r] = r < T ? (w ? w[r] : 1.0f) : 0.f;
-    if (r < nt) tiles[r] = make_int4(seg, r * block_n, min(block_n, T - r * block_n), 0);
+    if (r < nt) tiles[r] = make_int4(seg, r * block_n, min(block_n, T - r * block_n), r * block_n);
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     *n_tiles = nt;
@@ -516,7 +527,8 @@ int route_chunk_tokens(int T) { return T <= 1024 ? 8 : kMaxChunk; }
 int launch_route_plan(const int64_t* indices, int T, int k, int E, int allow_skip,
                       int shared_rows, int block_n, int max_rows, int max_tiles, int* chunk_cnt,
                       int* chunk_base, int* ctrl, int* counts, int* seg_start, int4* tiles,
-                      int* n_tiles, int* slot_token, float* slot_weight, cudaStream_t st) {
+                      int* n_tiles, int* slot_token, float* slot_weight, cudaStream_t st,
+                      int* zero_ptr, int n_zero) {
   if (T <= 0 || k > kMaxK || E + 1 > kMaxSegments) return DSV4_ERR_ARG;
   const int chunk = route_chunk_tokens(T);
   const int nchunks = (T + chunk - 1) / chunk;
@@ -525,7 +537,7 @@ int launch_route_plan(const int64_t* indices, int T, int k, int E, int allow_ski
              indices, T, k, E, allow_skip, shared_rows, chunk,
                                                 nchunks, block_n, max_rows, max_tiles, chunk_base,
                                                 counts, seg_start, tiles, n_tiles, slot_token,
-                                                slot_weight, ctrl);
+                                                slot_weight, ctrl, zero_ptr, n_zero);
     return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
   }
   if (cudaMemsetAsync(ctrl, 0, 4 * sizeof(int), st) != cudaSuccess) return DSV4_ERR_CUDA;
@@ -535,7 +547,8 @@ int launch_route_plan(const int64_t* indices, int T, int k, int E, int allow_ski
   launch_k(route_scan_kernel, (E + kScanThreads / 32 - 1) / (kScanThreads / 32), kScanThreads, 0, st,
            chunk_cnt, nchunks, E, shared_rows, block_n,
                                                 max_rows, max_tiles, chunk_base, counts, seg_start,
-                                                tiles, n_tiles, slot_token, slot_weight, ctrl);
+                                                tiles, n_tiles, slot_token, slot_weight, ctrl, zero_ptr,
+                                                n_zero);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
 

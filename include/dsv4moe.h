@@ -107,7 +107,10 @@ DSV4_API long long dsv4_moe_workspace_bytes(const dsv4_moe_layer* L, int T);
 /* Byte offsets inside the workspace of the intermediate buffers, for
  * inspection: out[0..] = logits, weights, indices, counts, seg_start,
  * n_tiles, route_slot, slot_token, slot_weight, tiles, xq, xsf, hq, hsf, O.
- * Also returns max_rows in out[15] and block_n in out[16]. n_out >= 17. */
+ * Also returns max_rows in out[15] and block_n in out[16]. n_out >= 17.
+ * With n_out > 17: out[17] = gate partial logits; with n_out > 19: out[18],
+ * out[19] = split-K slices of the two expert GEMMs (1 = no split; small
+ * batches split each GEMM item's k range so that every SM streams weights). */
 DSV4_API int dsv4_moe_workspace_layout(const dsv4_moe_layer* L, int T, long long* out, int n_out);
 
 /* LazyMoE.forward(x, input_ids) (spark_runtime/lazy_official_runtime.py:980-1002)

@@ -577,6 +577,25 @@ def test_pair_gemm_bit_identical_to_single_cta_gemm(cuda_device, tmp_path, T):
     assert np.array_equal(a, b)
 
 
+@pytest.mark.parametrize("T", [1, 8])
+def test_split_k_gemm_matches_unsplit_gemm(cuda_device, tmp_path, T):
+    """Small decode batches split every GEMM item's k range over several CTAs
+    (fp32 partial sums added in slice order by the CTA that finishes the item
+    last).  Against the unsplit GEMM only the fp32 summation order differs, so
+    the layer outputs agree to bf16 rounding: at most one bf16 ulp apart
+    (after the SwiGLU and the FP8 re-quantization a flipped rounding can move
+    an element a little further, so the bound is 2% of the output RMS and at
+    most 1% of elements may differ).  Two runs of the split form are
+    bit-identical (the order of the partial sums does not depend on which CTA
+    finishes last).  DSV4_KSPLIT=1 turns the split off at library load."""
+    split, split2, unsplit = _layer_bits_under_env(tmp_path, "decode", T, [{}, {}, {"DSV4_KSPLIT": "1"}])
+    assert np.array_equal(split, split2)
+    a = torch.from_numpy(split).view(torch.bfloat16).float().numpy()
+    b = torch.from_numpy(unsplit).view(torch.bfloat16).float().numpy()
+    assert _rel_err(a, b) <= TOL
+    assert np.mean(split != unsplit) <= 0.01
+
+
 def test_moe_forward_writes_the_route_trace(cuda_device, tmp_path):
     """With the reference's route-trace variable set, MoE.forward appends one
     expert_route line per call holding the gate's routing, and its output is
