@@ -848,19 +848,30 @@ def _sweep(args, local):
         for _ in range(3):
             moe.forward_tokens(layer["x"], workspace=ws, out=y)
         torch.cuda.synchronize()
+        # the layer as a replayed CUDA graph, as the headline times it (eager
+        # calls at these sizes would time the host's launch path instead)
+        s_cap = torch.cuda.Stream(device=dev)
+        s_cap.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s_cap):
+            moe.forward_tokens(layer["x"], workspace=ws, out=y)
+        torch.cuda.current_stream().wait_stream(s_cap)
         ts = []
         for _ in range(10):
             flush.fill_(1)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
-            moe.forward_tokens(layer["x"], workspace=ws, out=y)
+            graph.replay()
             e1.record()
             e1.synchronize()
             ts.append(e0.elapsed_time(e1))
         ms = statistics.median(ts)
-        entry = {"ms": round(ms, 4), "tokens_per_s": round(T / (ms * 1e-3), 1)}
+        del graph
+        entry = {"ms": round(ms, 4), "tokens_per_s": round(T / (ms * 1e-3), 1), "cuda_graph": True}
         if wl == "prefill":
             entry["roofline"] = _prefill_roofline(moe, layer, ws, y, flush, cfg, T)
+        else:
+            entry.update(_decode_roofline(moe, layer, ws, y, flush, cfg, T, ms))
         out[f"{wl}_T{T}"] = entry
         del moe, layer, ws, y
         torch.cuda.empty_cache()
@@ -913,6 +924,41 @@ def _upload_rate(args, dev):
             "pread_seconds": round(best["packed_read_seconds"], 4), "wall_seconds": round(best["upload_seconds"], 4),
             "plain_pinned_h2d_gbs": round(h2d, 2), "frac_of_h2d": round(best["upload_gbs"] / h2d, 3),
             "source": "page-cache resident file, chunks of 8 experts"}
+
+
+def _decode_roofline(moe, layer, ws, y, flush, cfg, T, layer_ms):
+    """HBM roofline of a decode layer: the algorithmic bytes (touched experts'
+    blocks + shared expert + gate + activations) over the graph-replayed layer
+    time, and the expert GEMMs' weight bytes over their stage-event time."""
+    import torch
+
+    from spark_b200 import _lib
+    from spark_b200.synthetic import algorithmic_decode_bytes
+
+    lib = _lib.load()
+    offs = (ctypes.c_longlong * 20)()
+    d = moe.layer_desc()
+    lib.dsv4_moe_workspace_layout(ctypes.byref(d), T, offs, 20)
+    counts = ws[offs[3]:offs[3] + (cfg.n_routed + 1) * 4].view(torch.int32)[: cfg.n_routed]
+    touched = int((counts > 0).sum())
+    alg = algorithmic_decode_bytes(cfg, touched, T)
+    gemm_bytes = alg - cfg.n_routed * cfg.dim * 2 - cfg.n_routed * 4 - 4 * T * cfg.dim
+    lib.dsv4_profile_enable(1)
+    buf = (ctypes.c_float * 6)()
+    gemm = []
+    for _ in range(5):
+        flush.fill_(1)
+        moe.forward_tokens(layer["x"], workspace=ws, out=y)
+        torch.cuda.synchronize()
+        lib.dsv4_profile_read(buf, 6)
+        gemm.append(buf[3] + buf[4])
+    lib.dsv4_profile_enable(0)
+    gemm_ms = statistics.median(gemm)
+    hbm = _peaks()[0]["hbm_gbs"]
+    return {"experts_touched": touched, "split_k": [int(offs[18]), int(offs[19])],
+            "layer_frac_of_measured_hbm": round(alg / (layer_ms * 1e-3) / 1e9 / hbm, 4),
+            "gemm_ms": round(gemm_ms, 4),
+            "gemm_frac_of_measured_hbm": round(gemm_bytes / (gemm_ms * 1e-3) / 1e9 / hbm, 4)}
 
 
 def _prefill_roofline(moe, layer, ws, y, flush, cfg, T):

@@ -137,11 +137,23 @@ static int choose_block_n(int T, int k, int E) {
 // Split-K slices for the decode-size GEMMs: with few tokens the layer has few
 // (segment tile, weight block) items, each a long serial stream of k tiles, so
 // most SMs would idle.  Cut each item's k range into S slices (S divides the
-// K/512 scale groups) until there are >= 16 units per SM.
-// DSV4_KSPLIT forces S (tuning).
+// K/512 scale groups) until there are >= 16 units per SM.  The setting
+// (dsv4_set_k_split; initially DSV4_KSPLIT, default 0) forces S when > 0;
+// 1 turns the split off.
+static std::atomic<int> g_k_split_setting{-1};
+
+static int k_split_setting() {
+  int v = g_k_split_setting.load(std::memory_order_relaxed);
+  if (v < 0) {
+    v = env_int("DSV4_KSPLIT", 0, 0, 64);
+    g_k_split_setting.store(v, std::memory_order_relaxed);
+  }
+  return v;
+}
+
 static int choose_k_split(int T, int k, int E, int block_n, int nb, int kt, int nsm) {
   const int groups = kt / 4;
-  static const int forced = env_int("DSV4_KSPLIT", 0, 0, 64);
+  const int forced = k_split_setting();
   if (block_n > 64 || groups < 2) return 1;
   int s = 1;
   if (forced) {
@@ -452,6 +464,12 @@ using namespace dsv4;
 extern "C" {
 
 int dsv4_version(void) { return 1; }
+
+int dsv4_set_k_split(int slices) {
+  if (slices < 0 || slices > 64) return DSV4_ERR_ARG;
+  g_k_split_setting.store(slices, std::memory_order_relaxed);
+  return DSV4_OK;
+}
 
 long long dsv4_kernel_launches(void) { return g_kernel_launches.load(std::memory_order_relaxed); }
 

@@ -41,21 +41,22 @@ inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
   kernel<<<grid, block, smem, st>>>(std::forward<Args>(args)...);
 }
 
-// Raise a kernel's dynamic shared-memory limit to `bytes` on the current
-// device, once per (kernel, device): the attribute belongs to the device, so a
-// process that drives several GPUs must set it on each of them.
+// Raise a kernel's dynamic shared-memory limit to at least `bytes` on the
+// current device.  The attribute belongs to the device, so a process that
+// drives several GPUs must set it on each of them; the largest size set so
+// far is remembered per (kernel, device), and a larger request sets it again.
 inline int ensure_smem_attr(const void* kernel, int bytes) {
   constexpr int kMaxDev = 64, kMaxKernels = 64;
   static std::mutex mu;
   static const void* fns[kMaxKernels];
-  static uint64_t set_on[kMaxKernels];  // bit d: set on device d
+  static int set_to[kMaxKernels][kMaxDev];  // bytes set on each device (0: never)
   static int n_fns = 0;
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return DSV4_ERR_CUDA;
   std::lock_guard<std::mutex> lock(mu);
   int i = 0;
   while (i < n_fns && fns[i] != kernel) ++i;
-  if (i < n_fns && (set_on[i] >> dev & 1)) return DSV4_OK;
+  if (i < n_fns && set_to[i][dev] >= bytes) return DSV4_OK;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
       cudaSuccess) {
     cudaGetLastError();
@@ -63,10 +64,9 @@ inline int ensure_smem_attr(const void* kernel, int bytes) {
   }
   if (i == n_fns) {
     if (n_fns == kMaxKernels) return DSV4_OK;  // set, just not remembered
-    fns[n_fns] = kernel;
-    set_on[n_fns++] = 0;
+    fns[n_fns++] = kernel;
   }
-  set_on[i] |= 1ull << dev;
+  set_to[i][dev] = bytes;
   return DSV4_OK;
 }
 

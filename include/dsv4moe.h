@@ -58,6 +58,14 @@ DSV4_API int dsv4_version(void);
  * the reference: it backs the launch count a benchmark reports. */
 DSV4_API long long dsv4_kernel_launches(void);
 DSV4_API const char* dsv4_status_string(int status);
+/* Split-K control of the expert GEMMs (no counterpart in the reference; a
+ * tuning and testing control).  0 (the default, or the DSV4_KSPLIT environment
+ * variable at the first call) lets small decode batches split each GEMM
+ * item's k range over several CTAs; 1 turns the split off; n > 1 forces up to
+ * n slices.  The split changes only the fp32 summation order of the expert
+ * GEMMs.  It also changes dsv4_moe_workspace_bytes and the EP workspace
+ * sizes: set it before sizing workspaces, not while calls are in flight. */
+DSV4_API int dsv4_set_k_split(int slices);
 /* Synchronises the device, returns the first device-side error code (0 if
  * none) in *code, and clears it when clear != 0. */
 DSV4_API int dsv4_device_error(int clear, int* code);

@@ -577,22 +577,42 @@ def test_pair_gemm_bit_identical_to_single_cta_gemm(cuda_device, tmp_path, T):
     assert np.array_equal(a, b)
 
 
-@pytest.mark.parametrize("T", [1, 8])
-def test_split_k_gemm_matches_unsplit_gemm(cuda_device, tmp_path, T):
+@pytest.mark.parametrize("T", [1, 8, 37])
+def test_split_k_gemm_matches_unsplit_gemm(cuda_device, T):
     """Small decode batches split every GEMM item's k range over several CTAs
     (fp32 partial sums added in slice order by the CTA that finishes the item
     last).  Against the unsplit GEMM only the fp32 summation order differs, so
-    the layer outputs agree to bf16 rounding: at most one bf16 ulp apart
-    (after the SwiGLU and the FP8 re-quantization a flipped rounding can move
-    an element a little further, so the bound is 2% of the output RMS and at
-    most 1% of elements may differ).  Two runs of the split form are
-    bit-identical (the order of the partial sums does not depend on which CTA
-    finishes last).  DSV4_KSPLIT=1 turns the split off at library load."""
-    split, split2, unsplit = _layer_bits_under_env(tmp_path, "decode", T, [{}, {}, {"DSV4_KSPLIT": "1"}])
+    the outputs agree to bf16 rounding (a flipped rounding can move an element
+    by one bf16 ulp, a little more after the SwiGLU and FP8 re-quantization:
+    the bound is the layer tolerance and at most 1% of elements differing).
+    Two runs of the split form are bit-identical: the partial sums are added
+    in slice order whichever CTA finishes last."""
+    from spark_b200 import _lib as L
+    from spark_b200.synthetic import CONFIGS, build_moe, make_layer
+
+    lib = L.load()
+    cfg = CONFIGS["decode"].with_tokens(T)
+    layer = make_layer(cfg, seed=11, device="cpu")
+    moe = build_moe(layer, device=cuda_device)
+    x = layer["x"].to(cuda_device)
+    outs, splits = [], []
+    try:
+        for setting in (0, 0, 1):
+            L.check(lib.dsv4_set_k_split(setting), "dsv4_set_k_split")
+            ws = torch.empty(moe.workspace_bytes(T), dtype=torch.uint8, device=cuda_device)
+            outs.append(moe.forward_tokens(x, workspace=ws))
+            d = moe.layer_desc()
+            offs = (ctypes.c_longlong * 20)()
+            L.check(lib.dsv4_moe_workspace_layout(ctypes.byref(d), T, offs, 20))
+            splits.append((offs[18], offs[19]))
+        torch.cuda.synchronize()
+        _no_device_error()
+    finally:
+        lib.dsv4_set_k_split(0)
+    assert splits[0][0] > 1 and splits[0][1] > 1 and splits[2] == (1, 1), splits
+    split, split2, unsplit = (o.view(torch.int16).cpu().numpy() for o in outs)
     assert np.array_equal(split, split2)
-    a = torch.from_numpy(split).view(torch.bfloat16).float().numpy()
-    b = torch.from_numpy(unsplit).view(torch.bfloat16).float().numpy()
-    assert _rel_err(a, b) <= TOL
+    assert _rel_err(_bf16_np(outs[0]), _bf16_np(outs[2])) <= TOL
     assert np.mean(split != unsplit) <= 0.01
 
 
