@@ -134,18 +134,22 @@ static int choose_block_n(int T, int k, int E) {
   return 256;
 }
 
-// Split-K slices for the decode-size GEMMs: with few tokens the layer has few
-// (segment tile, weight block) items, each a long serial stream of k tiles, so
-// most SMs would idle.  Cut each item's k range into S slices (S divides the
-// K/512 scale groups) until there are >= 16 units per SM.  The setting
-// (dsv4_set_k_split; initially DSV4_KSPLIT, default 0) forces S when > 0;
-// 1 turns the split off.
+// Split-K slices for the decode-size GEMMs.  With few tokens the layer has few
+// (segment tile, weight block) items, each a serial stream of k tiles, and
+// 36 of 148 SMs idle at one token; cutting each item's k range into S slices
+// (S divides the K/512 scale groups) gives every SM work.  Measured on B200 at
+// 1/8/16 tokens the split is no faster than the unsplit GEMM (the per-unit
+// accumulator handoff and fixup cost what the idle SMs would have gained), so
+// it is off unless asked for: the setting (dsv4_set_k_split; initially
+// DSV4_KSPLIT, default 1) is 1 = off, 0 = automatic (>= 16 units per SM,
+// slices of at least 8 k tiles), n > 1 = up to n slices.  At most 8 slices
+// (the fixup's registers).
 static std::atomic<int> g_k_split_setting{-1};
 
 static int k_split_setting() {
   int v = g_k_split_setting.load(std::memory_order_relaxed);
   if (v < 0) {
-    v = env_int("DSV4_KSPLIT", 0, 0, 64);
+    v = env_int("DSV4_KSPLIT", 1, 0, 64);
     g_k_split_setting.store(v, std::memory_order_relaxed);
   }
   return v;
@@ -153,14 +157,14 @@ static int k_split_setting() {
 
 static int choose_k_split(int T, int k, int E, int block_n, int nb, int kt, int nsm) {
   const int groups = kt / 4;
-  const int forced = k_split_setting();
-  if (block_n > 64 || groups < 2) return 1;
+  const int setting = k_split_setting();
+  if (setting == 1 || block_n > 64 || groups < 2) return 1;
   int s = 1;
-  if (forced) {
-    while (s * 2 <= forced && s * 2 <= groups) s *= 2;
+  if (setting > 1) {
+    while (s * 2 <= setting && s * 2 <= groups && s * 2 <= 8) s *= 2;
   } else {
     const long long tiles = (long long)((long long)T * k < E ? (long long)T * k : E) + 1;
-    while (s * 2 <= groups && tiles * nb * s < 16LL * nsm) s *= 2;
+    while (s * 2 <= groups / 2 && s * 2 <= 8 && tiles * nb * s < 16LL * nsm) s *= 2;
   }
   while (groups % s) s >>= 1;
   return s;

@@ -225,24 +225,48 @@ __device__ __forceinline__ void split_epilogue(const GemmArgs& args, uint32_t ta
   }
   tc_fence_before();
   mbar_arrive(acc_empty);
-  __threadfence();  // this thread's partial stores, before the count
+  // The barrier orders every epilogue thread's partial stores before the one
+  // counting atomic, whose release (gpu scope, cumulative) publishes them; the
+  // CTA that sees the count complete acquires through the same atomic, and the
+  // barrier after it orders its threads' partial loads behind that acquire.
   epi_bar();
-  if (threadIdx.x == 64) *split_last = atomicAdd(args.item_done + item, 1) == S - 1;
+  if (threadIdx.x == 64) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                 : "=r"(old)
+                 : "l"(args.item_done + item)
+                 : "memory");
+    *split_last = old == S - 1;
+  }
   epi_bar();
   const bool last = *split_last != 0;
   epi_bar();  // everyone read the flag before the next unit may overwrite it
   if (!last) return;
-  __threadfence();
   for (int rr = q; rr < nrows; rr += 4) {
+    // four slices' loads in flight at a time (L2: other SMs wrote them), then
+    // their sum in slice order
     float v[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = 0.f;
-    for (int sl = 0; sl < S; ++sl) {
-      const float4* p = reinterpret_cast<const float4*>(
-          args.partial + ((size_t)sl * args.part_rows + tl.w + rr) * args.part_ld + jb * 256 + 8 * lane);
-      const float4 x0 = __ldcg(p), x1 = __ldcg(p + 1);
-      v[0] += x0.x; v[1] += x0.y; v[2] += x0.z; v[3] += x0.w;
-      v[4] += x1.x; v[5] += x1.y; v[6] += x1.z; v[7] += x1.w;
+    for (int s0 = 0; s0 < S; s0 += 4) {
+      float4 x[8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (s0 + j < S) {
+          const float4* p = reinterpret_cast<const float4*>(
+              args.partial + ((size_t)(s0 + j) * args.part_rows + tl.w + rr) * args.part_ld + jb * 256 +
+              8 * lane);
+          x[2 * j] = __ldcg(p);
+          x[2 * j + 1] = __ldcg(p + 1);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (s0 + j < S) {
+          v[0] += x[2 * j].x; v[1] += x[2 * j].y; v[2] += x[2 * j].z; v[3] += x[2 * j].w;
+          v[4] += x[2 * j + 1].x; v[5] += x[2 * j + 1].y; v[6] += x[2 * j + 1].z; v[7] += x[2 * j + 1].w;
+        }
+      }
     }
     const int row = tl.y + rr;
     if (GATED) {

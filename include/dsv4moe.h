@@ -59,10 +59,11 @@ DSV4_API int dsv4_version(void);
 DSV4_API long long dsv4_kernel_launches(void);
 DSV4_API const char* dsv4_status_string(int status);
 /* Split-K control of the expert GEMMs (no counterpart in the reference; a
- * tuning and testing control).  0 (the default, or the DSV4_KSPLIT environment
- * variable at the first call) lets small decode batches split each GEMM
- * item's k range over several CTAs; 1 turns the split off; n > 1 forces up to
- * n slices.  The split changes only the fp32 summation order of the expert
+ * tuning and testing control).  1 (the default, or the DSV4_KSPLIT environment
+ * variable at the first call) keeps every GEMM item on one CTA; 0 lets small
+ * decode batches split each item's k range over several CTAs automatically;
+ * n > 1 asks for up to n slices (at most 8).  Measured on B200 the split was
+ * no faster at 1-16 tokens.  The split changes only the fp32 summation order of the expert
  * GEMMs.  It also changes dsv4_moe_workspace_bytes and the EP workspace
  * sizes: set it before sizing workspaces, not while calls are in flight. */
 DSV4_API int dsv4_set_k_split(int slices);

@@ -39,7 +39,7 @@ def unsplit_gemms():
     lib = _lib.load()
     _lib.check(lib.dsv4_set_k_split(1), "dsv4_set_k_split")
     yield
-    _lib.check(lib.dsv4_set_k_split(0), "dsv4_set_k_split")
+    _lib.check(lib.dsv4_set_k_split(1), "dsv4_set_k_split")  # the library's default
 
 
 REPO = Path(__file__).resolve().parent.parent

@@ -579,7 +579,7 @@ def test_pair_gemm_bit_identical_to_single_cta_gemm(cuda_device, tmp_path, T):
 
 @pytest.mark.parametrize("T", [1, 8, 37])
 def test_split_k_gemm_matches_unsplit_gemm(cuda_device, T):
-    """Small decode batches split every GEMM item's k range over several CTAs
+    """With the split asked for, small decode batches cut every GEMM item's k range over several CTAs
     (fp32 partial sums added in slice order by the CTA that finishes the item
     last).  Against the unsplit GEMM only the fp32 summation order differs, so
     the outputs agree to bf16 rounding (a flipped rounding can move an element
@@ -597,7 +597,7 @@ def test_split_k_gemm_matches_unsplit_gemm(cuda_device, T):
     x = layer["x"].to(cuda_device)
     outs, splits = [], []
     try:
-        for setting in (0, 0, 1):
+        for setting in (4, 4, 1):  # four slices per item twice, then no split
             L.check(lib.dsv4_set_k_split(setting), "dsv4_set_k_split")
             ws = torch.empty(moe.workspace_bytes(T), dtype=torch.uint8, device=cuda_device)
             outs.append(moe.forward_tokens(x, workspace=ws))
@@ -608,7 +608,7 @@ def test_split_k_gemm_matches_unsplit_gemm(cuda_device, T):
         torch.cuda.synchronize()
         _no_device_error()
     finally:
-        lib.dsv4_set_k_split(0)
+        lib.dsv4_set_k_split(1)  # the library's default: no split
     assert splits[0][0] > 1 and splits[0][1] > 1 and splits[2] == (1, 1), splits
     split, split2, unsplit = (o.view(torch.int16).cpu().numpy() for o in outs)
     assert np.array_equal(split, split2)
