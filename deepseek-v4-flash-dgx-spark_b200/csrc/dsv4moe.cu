@@ -3,6 +3,7 @@
 // together.
 #include "gate.cu"
 #include "route.cu"
+#include "prefetch.cu"
 #include "expert_gemm.cu"
 #include "expert_gemm_pair.cu"
 #include "gate_gemm.cu"
