@@ -155,28 +155,6 @@ static int k_split_setting() {
   return v;
 }
 
-// The caller's stream waits for the prefetch side stream before a layer call
-// returns, on every path (a stream capture must not end with it unjoined).
-struct SideJoin {
-  cudaStream_t side, st;
-  int join() {
-    const int rc = join_side_stream(side, st);
-    side = nullptr;
-    return rc;
-  }
-  ~SideJoin() {
-    if (side) join_side_stream(side, st);
-  }
-};
-
-// L2 prefetch of the expert weights at decode sizes (prefetch.cu): up to
-// DSV4_PREFETCH_MB megabytes (default 96, below the 126 MB L2; 0 turns it off).
-constexpr int kPrefetchMaxTokens = 512;
-static long long prefetch_budget() {
-  static const long long mb = env_int("DSV4_PREFETCH_MB", 96, 0, 120);
-  return mb << 20;
-}
-
 static int choose_k_split(int T, int k, int E, int block_n, int nb, int kt, int nsm) {
   const int groups = kt / 4;
   const int setting = k_split_setting();
@@ -694,11 +672,6 @@ int dsv4_moe_forward(const dsv4_moe_layer* L, const void* x, int T, void* y,
     ri = indices;
   }
   stage_mark(1, st);
-  // decode sizes: the touched experts' weights start moving into L2 now, on a
-  // side stream, while the routing kernels below run
-  SideJoin side{T <= kPrefetchMaxTokens ? launch_weight_prefetch(L, ri, T * k, prefetch_budget(), nsm, st)
-                                        : nullptr,
-                st};
   int* chunk_cnt = reinterpret_cast<int*>(ws + p.off[16]);
   int* chunk_base = reinterpret_cast<int*>(ws + p.off[17]);
   int* ctrl = reinterpret_cast<int*>(ws + p.off[18]);
@@ -719,8 +692,7 @@ int dsv4_moe_forward(const dsv4_moe_layer* L, const void* x, int T, void* y,
     return rc;
   rc = launch_combine(O, H, route_slot, ri, T, k, p.S ? seg_start + E : nullptr, y, st);
   stage_mark(6, st);
-  const int rj = side.join();
-  return rc ? rc : rj;
+  return rc;
 }
 
 long long dsv4_expert_workspace_bytes(const dsv4_moe_layer* L, int T) {

@@ -3,7 +3,6 @@
 // together.
 #include "gate.cu"
 #include "route.cu"
-#include "prefetch.cu"
 #include "expert_gemm.cu"
 #include "expert_gemm_pair.cu"
 #include "gate_gemm.cu"

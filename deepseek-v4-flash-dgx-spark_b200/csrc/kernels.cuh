@@ -94,9 +94,6 @@ int launch_ep_unpack(const uint8_t* recv, int R, int T_own, int k, int H, int e_
 int launch_ep_return_gather(const void* O, int H, const int* route_slot, const int* ret_dst,
                             int n_routes, long long ret_rows, void* ret, int num_sms,
                             cudaStream_t st);
-cudaStream_t launch_weight_prefetch(const dsv4_moe_layer* L, const int64_t* indices, int n_idx,
-                                    long long budget, int num_sms, cudaStream_t st);
-int join_side_stream(cudaStream_t side, cudaStream_t st);
 int launch_combine(const void* O, int H, const int* route_slot, const int64_t* indices, int T,
                    int k, const int* shared_base, void* y, cudaStream_t st,
                    const void* O_shared = nullptr);
