@@ -187,7 +187,10 @@ class PeerExchange:
     def check_poisoned(self) -> None:
         """Raise if an earlier call's peer wait ran out (non-blocking: reads
         the error word the last finished call copied back)."""
-        if self.poisoned is None and self._err_event is not None and self._err_event.query():
+        # an event cannot be queried while the stream is being captured: then
+        # only an already-latched poisoning is reported
+        if (self.poisoned is None and self._err_event is not None and not torch.cuda.is_current_stream_capturing()
+                and self._err_event.query()):
             code = int(self._err_host[0])
             if code == 107:  # DSV4_DEVERR_TIMEOUT_PEER
                 self.poisoned = _lib.DEVERR_NAMES[code]

@@ -271,6 +271,15 @@ def test_peer_wait_times_out_with_an_error_not_a_hang(cuda_device):
         ex.check_poisoned()  # nothing recorded yet: no error
         ex.note_call_end()
         torch.cuda.synchronize()
+        # inside a stream capture (a CUDA graph of the layer) the check must not
+        # touch the event, which cannot be queried then
+        g, s = torch.cuda.CUDAGraph(), torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.graph(g, stream=s):
+            ex.check_poisoned()
+            ex.note_call_end()  # no copy is enqueued into the graph either
+            torch.ones(4, device="cuda").mul_(2)
+        del g
         for _ in range(2):  # poisoned for good, not just once
             with pytest.raises(RuntimeError, match="poisoned"):
                 ex.check_poisoned()
