@@ -26,7 +26,7 @@ TORCH_OPS_LIB = LIB_DIR / "libdsv4moe_torch.so"
 INCLUDE = REPO / "include"
 
 SOURCES = ["dsv4moe.cu", "loader.cpp"]
-DEPS = ["gate.cu", "route.cu", "expert_gemm.cu", "expert_gemm_pair.cu", "materialize.cu", "capi.cu", "no_alloc.cu", "gate_gemm.cu", "ep.cu"]
+DEPS = ["gate.cu", "route.cu", "expert_gemm.cu", "expert_gemm_pair.cu", "materialize.cu", "capi.cu", "no_alloc.cu", "gate_gemm.cu", "ep.cu", "sparse_attn.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",

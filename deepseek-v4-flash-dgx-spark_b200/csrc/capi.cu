@@ -749,6 +749,135 @@ int dsv4_expert_forward(const dsv4_moe_layer* L, int expert, const void* x, int 
                           p.block_n, L->expert_slot, Lx.n_routed, nsm, st);
 }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Dense FP8 linear layers (the attention block's projections): act_quant of x
+// then the non-gated grouped GEMM over one segment of M rows, B = the e4m3
+// weight with its 128x128 block scales expanded into scale atoms.
+// ---------------------------------------------------------------------------
+namespace dsv4 {
+
+struct LinearPlan {
+  int rows_pad, block_n, max_tiles;
+  long long off[6];
+  long long total;
+};
+
+static LinearPlan make_linear_plan(int M, int K) {
+  LinearPlan p{};
+  p.block_n = M <= 32 ? 32 : (M <= 64 ? 64 : 128);
+  p.rows_pad = (M + 31) / 32 * 32;
+  p.max_tiles = (M + p.block_n - 1) / p.block_n + 1;
+  const long long groups = p.rows_pad / 32 + 4;
+  long long sz[6] = {
+      16,                                  // n_tiles, total_rows
+      (long long)p.rows_pad * 4,           // slot_token
+      (long long)p.rows_pad * 4,           // slot_weight (unused by the non-gated epilogue)
+      (long long)p.max_tiles * 16,         // tiles
+      (long long)p.rows_pad * K,           // xq
+      groups * (K / 512) * 512,            // xsf
+  };
+  long long o = 0;
+  for (int i = 0; i < 6; ++i) {
+    p.off[i] = o;
+    o += align256(sz[i]);
+  }
+  p.total = o;
+  return p;
+}
+
+static bool linear_shape_ok(int M, int N, int K) { return M >= 0 && N > 0 && K > 0 && N % 256 == 0 && K % 512 == 0; }
+
+}  // namespace dsv4
+
+extern "C" {
+
+long long dsv4_fp8_weight_atoms_bytes(int N, int K) {
+  if (N <= 0 || K <= 0 || N % 128 || K % 128) return -1;
+  return (long long)N * K / 32;
+}
+
+int dsv4_build_fp8_weight_atoms(const uint8_t* scale, int N, int K, uint8_t* atoms, void* stream) {
+  if (!scale || !atoms || N <= 0 || K <= 0 || N % 128 || K % 128) return DSV4_ERR_ARG;
+  bind_device(atoms);
+  return launch_build_sf_fp8(scale, N, K, atoms, num_sms(), static_cast<cudaStream_t>(stream));
+}
+
+long long dsv4_fp8_linear_workspace_bytes(int M, int N, int K) {
+  if (!linear_shape_ok(M, N, K)) return -1;
+  return make_linear_plan(M, K).total;
+}
+
+int dsv4_fp8_linear(const void* x, int M, int K, const uint8_t* w, const uint8_t* w_atoms, int N, void* y,
+                    void* workspace, long long workspace_bytes, void* stream) {
+  if (!linear_shape_ok(M, N, K)) return N % 256 || K % 512 ? DSV4_ERR_UNSUPPORTED : DSV4_ERR_ARG;
+  if (M == 0) return DSV4_OK;
+  if (!x || !w || !w_atoms || !y) return DSV4_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15) ||
+      (reinterpret_cast<uintptr_t>(y) & 15))
+    return DSV4_ERR_ARG;
+  const LinearPlan p = make_linear_plan(M, K);
+  if (!workspace || workspace_bytes < p.total) return DSV4_ERR_WORKSPACE;
+  bind_device(workspace);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* n_tiles = reinterpret_cast<int*>(ws + p.off[0]);
+  int* total_rows = n_tiles + 1;
+  int* slot_token = reinterpret_cast<int*>(ws + p.off[1]);
+  float* slot_weight = reinterpret_cast<float*>(ws + p.off[2]);
+  int4* tiles = reinterpret_cast<int4*>(ws + p.off[3]);
+  uint8_t* xq = ws + p.off[4];
+  uint8_t* xsf = ws + p.off[5];
+  const int nsm = num_sms();
+  int rc;
+  // one segment (id 0 with no routed experts: the e4m3 "shared" weight path)
+  if ((rc = launch_single_segment_plan(M, 0, p.block_n, p.rows_pad, nullptr, slot_token, slot_weight, tiles,
+                                       n_tiles, total_rows, st)))
+    return rc;
+  if ((rc = launch_permute_quant(x, K, slot_token, total_rows, p.rows_pad, xq, xsf, nsm, st))) return rc;
+  CUtensorMap tw, tx;
+  if ((rc = make_tmap_u8(&tw, w, K, N, 128))) return rc;
+  if ((rc = make_tmap_u8(&tx, xq, K, p.rows_pad, p.block_n))) return rc;
+  GemmArgs g{};
+  g.tiles = tiles;
+  g.n_tiles = n_tiles;
+  g.n_routed = 0;
+  g.kt_count = K / 128;
+  g.nb_count = N / 256;
+  g.sf_shared0 = w_atoms;
+  g.sf_shared1 = w_atoms;
+  g.sfb = xsf;
+  g.slot_weight = slot_weight;
+  g.out_bf16 = static_cast<__nv_bfloat16*>(y);
+  g.out_ld = N;
+  g.k_split = 1;
+  const long long work = (long long)p.max_tiles * g.nb_count;
+  const int grid = (int)(work < nsm ? work : nsm);
+  return launch_expert_gemm(false, p.block_n, tw, tw, tw, tw, tx, g, grid, st);
+}
+
+long long dsv4_sparse_attn_workspace_bytes(int B, int S, int K) {
+  if (B < 0 || S < 0 || K <= 0) return -1;
+  return sparse_attn_workspace(B * S, K, num_sms(), nullptr, nullptr);
+}
+
+int dsv4_sparse_attn(const void* q, const void* kv, const float* attn_sink, const int* topk_idxs, int B, int S,
+                     int H, int N, int D, int K, float softmax_scale, void* out, void* workspace,
+                     long long workspace_bytes, void* stream) {
+  if (B < 0 || S < 0 || N <= 0 || K <= 0) return DSV4_ERR_ARG;
+  if (H != 64 || D != 512) return DSV4_ERR_UNSUPPORTED;
+  if ((long long)B * S == 0) return DSV4_OK;
+  if (!q || !kv || !attn_sink || !topk_idxs || !out) return DSV4_ERR_ARG;
+  // 16-byte row copies in, 2-byte stores out
+  if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(kv) & 15) ||
+      (reinterpret_cast<uintptr_t>(out) & 3))
+    return DSV4_ERR_ARG;
+  bind_device(out);
+  return launch_sparse_attn(q, kv, attn_sink, topk_idxs, B, S, N, K, softmax_scale, out, workspace,
+                            workspace ? workspace_bytes : 0, num_sms(), static_cast<cudaStream_t>(stream));
+}
+
 int dsv4_materialize(const uint8_t* slab, const long long* src_off, const int* dst_slot, int n,
                      int hidden, int inter, uint8_t* arena, long long slot_stride,
                      uint8_t* arena_sf, long long sf_slot_stride, void* bf16_out,

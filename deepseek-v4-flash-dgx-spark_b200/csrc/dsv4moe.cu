@@ -8,5 +8,6 @@
 #include "gate_gemm.cu"
 #include "materialize.cu"
 #include "ep.cu"
+#include "sparse_attn.cu"
 #include "capi.cu"
 #include "no_alloc.cu"

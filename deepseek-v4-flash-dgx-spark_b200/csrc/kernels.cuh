@@ -94,6 +94,10 @@ int launch_ep_unpack(const uint8_t* recv, int R, int T_own, int k, int H, int e_
 int launch_ep_return_gather(const void* O, int H, const int* route_slot, const int* ret_dst,
                             int n_routes, long long ret_rows, void* ret, int num_sms,
                             cudaStream_t st);
+long long sparse_attn_workspace(int tokens, int K, int num_sms, int* splits_out, int* cps_out);
+int launch_sparse_attn(const void* q, const void* kv, const float* sink, const int* idx, int B, int S,
+                       int N, int K, float scale, void* out, void* ws, long long ws_bytes, int num_sms,
+                       cudaStream_t st);
 int launch_combine(const void* O, int H, const int* route_slot, const int64_t* indices, int T,
                    int k, const int* shared_base, void* y, cudaStream_t st,
                    const void* O_shared = nullptr);

@@ -80,6 +80,13 @@ _SIGNATURES = {
     "dsv4_device_error": (c_int, [c_int, c_ip]),
     "dsv4_device_error_async": (c_int, [c_vp, c_vp]),
     "dsv4_set_k_split": (c_int, [c_int]),
+    "dsv4_fp8_weight_atoms_bytes": (c_ll, [c_int, c_int]),
+    "dsv4_build_fp8_weight_atoms": (c_int, [c_vp, c_int, c_int, c_vp, c_vp]),
+    "dsv4_fp8_linear_workspace_bytes": (c_ll, [c_int, c_int, c_int]),
+    "dsv4_fp8_linear": (c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_int, c_vp, c_vp, c_ll, c_vp]),
+    "dsv4_sparse_attn_workspace_bytes": (c_ll, [c_int, c_int, c_int]),
+    "dsv4_sparse_attn": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_float,
+                                 c_vp, c_vp, c_ll, c_vp]),
     "dsv4_moe_workspace_bytes": (c_ll, [ctypes.POINTER(MoELayerDesc), c_int]),
     "dsv4_moe_workspace_layout": (c_int, [ctypes.POINTER(MoELayerDesc), c_int, c_llp, c_int]),
     "dsv4_moe_forward": (c_int, [ctypes.POINTER(MoELayerDesc), c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_ll, c_vp]),

@@ -216,6 +216,40 @@ DSV4_API int dsv4_gate_route_hash(const void* x, const void* w, int w_is_fp32, c
  * 44-49): bf16 [M,K] -> e4m3 codes [M,K] + ue8m0 scales [M,K/128]. */
 DSV4_API int dsv4_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* scale, void* stream);
 
+/* ---- attention block: dense FP8 linear layers ---------------------------
+ * The official linear(x, W) for an FP8 weight (act_quant(x, 128, "ue8m0") ->
+ * fp8_gemm -> bf16; kernel API scripts/smoke_official_kernels.py:36-43), as the
+ * attention projections wq_a [1024,4096], wq_b [32768,1024], wkv [512,4096],
+ * wo_a [8192,4096], wo_b [4096,8192] use it (e4m3 weights with 128x128 ue8m0
+ * block scales, results/spark-66c9/checkpoint-tensors.csv layers.L.attn.*).
+ * y[M,N] bf16 = act_quant(x[M,K] bf16) . W[N,K]^T on the tensor core
+ * (kind::mxf8f6f4, fp32 accumulate).  N % 256 == 0 and K % 512 == 0
+ * (DSV4_ERR_UNSUPPORTED otherwise); x, W and y 16-byte aligned.
+ * w_atoms: the weight's scales expanded once by dsv4_build_fp8_weight_atoms
+ * (dsv4_fp8_weight_atoms_bytes(N, K) bytes) from scale [N/128][K/128]. */
+DSV4_API long long dsv4_fp8_weight_atoms_bytes(int N, int K);
+DSV4_API int dsv4_build_fp8_weight_atoms(const uint8_t* scale, int N, int K, uint8_t* atoms, void* stream);
+DSV4_API long long dsv4_fp8_linear_workspace_bytes(int M, int N, int K);
+DSV4_API int dsv4_fp8_linear(const void* x, int M, int K, const uint8_t* w, const uint8_t* w_atoms, int N,
+                             void* y, void* workspace, long long workspace_bytes, void* stream);
+
+/* Official kernel.sparse_attn(q, kv, attn_sink, topk_idxs, softmax_scale)
+ * (scripts/smoke_official_kernels.py:53-57), which the reference replaces by
+ * its per-token fallback spark_runtime/lazy_official_runtime.py:1024-1049
+ * because the official kernel fails at h=64, d=512 on GB10 (LOG.md:134-135).
+ * q [B,S,H,D] bf16, kv [B,N,D] bf16 (one KV row for every head), attn_sink
+ * [H] fp32, topk_idxs [B,S,K] int32 (-1 = no row), out [B,S,H,D] bf16:
+ * out[b,s,h] = sum_j p[h,j] kv[b,idx_j] over the valid indices, p = softmax of
+ * softmax_scale * q.kv with the sink's exp in the denominator; zeros when no
+ * index is valid.  H = 64 and D = 512 (DSV4_ERR_UNSUPPORTED otherwise); q and
+ * kv 16-byte aligned.  Indices >= N count as invalid and latch
+ * DSV4_DEVERR_BAD_INDEX.  Workspace: dsv4_sparse_attn_workspace_bytes(B, S,
+ * K) bytes (0 when every token fits one CTA's pass over its indices). */
+DSV4_API long long dsv4_sparse_attn_workspace_bytes(int B, int S, int K);
+DSV4_API int dsv4_sparse_attn(const void* q, const void* kv, const float* attn_sink, const int* topk_idxs,
+                              int B, int S, int H, int N, int D, int K, float softmax_scale, void* out,
+                              void* workspace, long long workspace_bytes, void* stream);
+
 /* ---- expert arena / materializer ---------------------------------------
  * LazyRoutedExpert.materialize + ExpertCopyPlan::read_into_and_copy_cuda
  * (lazy_official_runtime.py:761-917; native_packed_loader.cpp:122-174,281-316),

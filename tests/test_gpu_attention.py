@@ -1,0 +1,96 @@
+"""GPU parity of the attention block's hot ops against the oracle
+(oracle/attention_oracle.py, pinned to the reference's own
+sparse_attn_fallback): the tcgen05 sparse attention at h=64, d=512 on decode
+and prefill shapes (split and unsplit index lists, ragged lists, invalid
+indices, a query with none), and the FP8 linear at the attention projections'
+shapes.  Bar: max |err| <= 1e-2 (sparse attention: bf16 probabilities and
+rows, fp32 sums) / 2e-2 (FP8 linear, the layer bar) of the reference RMS."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention_oracle as A
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel_err(got, ref):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    return float(np.max(np.abs(got - ref)) / (np.sqrt(np.mean(ref ** 2)) + 1e-30))
+
+
+def _case(B, S, N, K, seed, invalid_frac=0.1, empty_query=False):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, S, 64, 512, generator=g).to(torch.bfloat16)
+    kv = torch.randn(B, N, 512, generator=g).to(torch.bfloat16)
+    sink = torch.randn(64, generator=g)
+    idx = torch.stack([torch.stack([torch.randperm(N, generator=g)[:K] for _ in range(S)]) for _ in range(B)])
+    idx = idx.to(torch.int32)
+    drop = torch.rand(B, S, K, generator=g) < invalid_frac
+    idx[drop] = -1
+    if empty_query:
+        idx[0, 0, :] = -1
+    return q, kv, sink, idx
+
+
+@pytest.mark.parametrize("B,S,N,K", [
+    (1, 1, 4096, 2048),   # decode, one query: the index list split over many CTAs
+    (1, 1, 700, 100),     # ragged list shorter than one 128-row chunk
+    (2, 40, 300, 256),    # a few queries: two chunks, split in two
+    (1, 320, 512, 128),   # many queries: one CTA per query, no combine
+])
+def test_sparse_attn_matches_the_reference_fallback(cuda_device, B, S, N, K):
+    from spark_b200 import _lib
+    from spark_b200.attention import sparse_attn
+
+    q, kv, sink, idx = _case(B, S, N, K, seed=B * 1000 + S + K, empty_query=(S > 1))
+    scale = 512 ** -0.5
+    out = sparse_attn(q.to(cuda_device), kv.to(cuda_device), sink.to(cuda_device), idx.to(cuda_device), scale)
+    torch.cuda.synchronize()
+    _lib.raise_on_device_error()
+    ref = A.sparse_attn(q.float().numpy(), kv.float().numpy(), sink.numpy(), idx.numpy(), scale)
+    got = out.float().cpu().numpy()
+    assert _rel_err(got, ref) <= 1e-2, _rel_err(got, ref)
+    if S > 1:
+        assert np.all(got[0, 0] == 0)  # no valid index: zeros, as the reference
+
+
+def test_sparse_attn_out_of_range_index_is_reported_and_skipped(cuda_device):
+    from spark_b200 import _lib
+    from spark_b200.attention import sparse_attn
+
+    q, kv, sink, idx = _case(1, 2, 256, 64, seed=5, invalid_frac=0.0)
+    bad = idx.clone()
+    bad[0, 1, 3] = 256  # one past the last kv row
+    out = sparse_attn(q.to(cuda_device), kv.to(cuda_device), sink.to(cuda_device), bad.to(cuda_device), 0.05)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="expert index out of range"):
+        _lib.raise_on_device_error()
+    skipped = idx.clone()
+    skipped[0, 1, 3] = -1
+    ref = A.sparse_attn(q.float().numpy(), kv.float().numpy(), sink.numpy(), skipped.numpy(), 0.05)
+    assert _rel_err(out.float().cpu().numpy(), ref) <= 1e-2
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 4096, 1024), (37, 4096, 512), (5, 1024, 32768), (200, 8192, 4096),
+                                   (130, 4096, 8192)])
+def test_fp8_linear_matches_the_oracle(cuda_device, M, K, N):
+    from spark_b200 import _lib
+    from spark_b200.attention import FP8Linear
+
+    g = torch.Generator().manual_seed(M + K + N)
+    lin = FP8Linear(K, N, device=cuda_device)
+    w = torch.randn(N, K, generator=g).to(torch.float8_e4m3fn)
+    s = torch.randint(119, 124, (N // 128, K // 128), generator=g, dtype=torch.uint8)
+    with torch.no_grad():
+        lin.weight.view(torch.uint8).copy_(w.view(torch.uint8).to(cuda_device))
+        lin.scale.view(torch.uint8).copy_(s.to(cuda_device))
+    lin.refresh_scale_atoms()
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    y = lin(x.to(cuda_device))
+    torch.cuda.synchronize()
+    _lib.raise_on_device_error()
+    ref = A.fp8_linear(x.float().numpy(), w.view(torch.uint8).numpy(), s.numpy())
+    assert _rel_err(y.float().cpu().numpy(), ref) <= 2e-2
