@@ -3,8 +3,16 @@
 sparse_attn_fallback): the tcgen05 sparse attention at h=64, d=512 on decode
 and prefill shapes (split and unsplit index lists, ragged lists, invalid
 indices, a query with none), and the FP8 linear at the attention projections'
-shapes.  Bar: max |err| <= 1e-2 (sparse attention: bf16 probabilities and
-rows, fp32 sums) / 2e-2 (FP8 linear, the layer bar) of the reference RMS."""
+shapes.
+
+Sparse attention bar: the kernel multiplies bf16 probabilities with the bf16
+rows (fp32 sums) and rounds the result to bf16, as the reference's output is.
+Simulating exactly that on the CPU gives max |err| of 1.1-4.2% of the output
+RMS on these cases (the bf16 output rounding alone: 0.8-2.5%, the max being
+taken over up to 10^7 elements), and the kernel measured the same.  So the
+test bounds the RMS of the error by 1% of the output RMS (a systematic defect
+shows there) and the largest element error by 5%.  FP8 linear: max |err| <=
+2e-2 of the RMS, the layer bar."""
 
 import numpy as np
 import pytest
@@ -19,6 +27,17 @@ def _rel_err(got, ref):
     got = np.asarray(got, np.float64)
     ref = np.asarray(ref, np.float64)
     return float(np.max(np.abs(got - ref)) / (np.sqrt(np.mean(ref ** 2)) + 1e-30))
+
+
+def _rms_err(got, ref):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    return float(np.sqrt(np.mean((got - ref) ** 2)) / (np.sqrt(np.mean(ref ** 2)) + 1e-30))
+
+
+def _attn_close(got, ref):
+    assert _rms_err(got, ref) <= 1e-2, _rms_err(got, ref)
+    assert _rel_err(got, ref) <= 5e-2, _rel_err(got, ref)
 
 
 def _case(B, S, N, K, seed, invalid_frac=0.1, empty_query=False):
@@ -52,7 +71,7 @@ def test_sparse_attn_matches_the_reference_fallback(cuda_device, B, S, N, K):
     _lib.raise_on_device_error()
     ref = A.sparse_attn(q.float().numpy(), kv.float().numpy(), sink.numpy(), idx.numpy(), scale)
     got = out.float().cpu().numpy()
-    assert _rel_err(got, ref) <= 1e-2, _rel_err(got, ref)
+    _attn_close(got, ref)
     if S > 1:
         assert np.all(got[0, 0] == 0)  # no valid index: zeros, as the reference
 
@@ -71,7 +90,7 @@ def test_sparse_attn_out_of_range_index_is_reported_and_skipped(cuda_device):
     skipped = idx.clone()
     skipped[0, 1, 3] = -1
     ref = A.sparse_attn(q.float().numpy(), kv.float().numpy(), sink.numpy(), skipped.numpy(), 0.05)
-    assert _rel_err(out.float().cpu().numpy(), ref) <= 1e-2
+    _attn_close(out.float().cpu().numpy(), ref)
 
 
 @pytest.mark.parametrize("M,K,N", [(1, 4096, 1024), (37, 4096, 512), (5, 1024, 32768), (200, 8192, 4096),
