@@ -1,7 +1,7 @@
 """Benchmark of the B200 routed-expert MoE layer.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|prefill] [--tokens T]
+                    [--workload decode|prefill|stack|attention] [--tokens T]
 
 One step = one MoE layer forward (gate -> route plan -> permute/quant ->
 grouped GEMM1 -> grouped GEMM2 -> combine) over one batch of synthetic tokens,
@@ -53,7 +53,7 @@ def _parse():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--workload", default="decode", choices=["decode", "prefill", "stack"],
+    p.add_argument("--workload", default="decode", choices=["decode", "prefill", "stack", "attention"],
                    help="stack: the full-depth MoE-only decode stack (--layers layers, bf16 residual)")
     p.add_argument("--layers", type=int, default=43)
     p.add_argument("--tokens", type=int, default=None)
@@ -881,6 +881,7 @@ def _sweep(args, local):
         torch.cuda.empty_cache()
     out.update(_materializer(args, dev, flush))
     out["upload_32_experts"] = _upload_rate(args, dev)
+    out["attention"] = _attention(args, dev, flush)
     return out
 
 
@@ -1051,6 +1052,117 @@ def _materializer(args, dev, flush):
     return out
 
 
+def _graph_ms(fn, flush, reps=10):
+    """Median CUDA-event time of fn replayed as a CUDA graph, L2 flushed
+    before each replay (outside the events)."""
+    import torch
+
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    s_cap = torch.cuda.Stream()
+    s_cap.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s_cap):
+        fn()
+    torch.cuda.current_stream().wait_stream(s_cap)
+    ts = []
+    for _ in range(reps):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        e1.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    del graph
+    return statistics.median(ts)
+
+
+def _attention(args, dev, flush):
+    """The attention block's hot ops (h=64 heads, d=512): sparse attention at
+    decode and prefill shapes and the FP8 linear at the projection shapes,
+    each as a replayed CUDA graph with L2 flushed between replays.  Sparse
+    attention's algorithmic work is 4*B*S*64*512*K FLOPs (the score and the
+    output product over the K gathered rows), bounded by the measured bf16
+    tensor peak; its gathered bytes (K rows of 1 KB per query) are given
+    beside.  FP8 linear: decode M=64 is bound by the weight bytes (HBM),
+    prefill M=8192 by the FP8 rate (2x the measured bf16 peak).  A small case
+    of each is checked against the oracle first (outside the timings)."""
+    import numpy as np
+    import torch
+
+    from oracle import attention_oracle as A
+    from spark_b200 import _lib
+    from spark_b200.attention import FP8Linear, sparse_attn
+
+    peaks, src = _peaks()
+    bf16_peak, hbm = peaks.get("bf16_tflops", 1590.0), peaks.get("hbm_gbs", 6650.0)
+    g = torch.Generator(device=dev).manual_seed(args.seed + 23)
+    out = {}
+
+    # parity, small cases
+    gc = torch.Generator().manual_seed(args.seed + 29)
+    q = torch.randn(1, 3, 64, 512, generator=gc).to(torch.bfloat16)
+    kv = torch.randn(1, 700, 512, generator=gc).to(torch.bfloat16)
+    sink = torch.randn(64, generator=gc)
+    idx = torch.stack([torch.randperm(700, generator=gc)[:300] for _ in range(3)])[None].to(torch.int32)
+    got = sparse_attn(q.to(dev), kv.to(dev), sink.to(dev), idx.to(dev), 0.044).float().cpu().numpy()
+    ref = A.sparse_attn(q.float().numpy(), kv.float().numpy(), sink.numpy(), idx.numpy(), 0.044)
+    rms = float(np.sqrt(np.mean((got - ref) ** 2)) / np.sqrt(np.mean(ref ** 2)))
+    lin = FP8Linear(1024, 512, device=dev)
+    lin.weight.data.view(torch.uint8).copy_(torch.randint(0, 126, (512, 1024), generator=gc, dtype=torch.uint8))
+    lin.scale.data.view(torch.uint8).copy_(torch.randint(120, 130, (4, 8), generator=gc, dtype=torch.uint8))
+    lin.refresh_scale_atoms()
+    xl = torch.randn(8, 1024, generator=gc).to(torch.bfloat16)
+    yl = lin(xl.to(dev)).float().cpu().numpy()
+    refl = A.fp8_linear(xl.float().numpy(), lin.weight.view(torch.uint8).cpu().numpy(),
+                        lin.scale.view(torch.uint8).cpu().numpy())
+    out["parity"] = {"sparse_attn_rms_err": round(rms, 6),
+                     "fp8_linear_max_err_rms": round(float(np.max(np.abs(yl - refl)) / np.sqrt(np.mean(refl ** 2))), 6),
+                     "oracle": "oracle/attention_oracle.py (the reference's sparse_attn_fallback, float64)"}
+
+    # the profiled small prefill case runs first
+    for name, (B, S, N, K) in (("prefill_S512_K512", (1, 512, 4096, 512)),
+                               ("decode_B1_K2048", (1, 1, 65536, 2048)),
+                               ("decode_B8_K2048", (8, 1, 65536, 2048)),
+                               ("prefill_S2048_K2048", (1, 2048, 8192, 2048))):
+        q = torch.randn(B, S, 64, 512, device=dev, generator=g).to(torch.bfloat16)
+        kv = torch.randn(B, N, 512, device=dev, generator=g).to(torch.bfloat16)
+        sink = torch.randn(64, device=dev, generator=g)
+        idx = torch.randint(0, N, (B, S, K), device=dev, dtype=torch.int32, generator=g)
+        ms = _graph_ms(lambda: sparse_attn(q, kv, sink, idx, 0.044), flush)
+        flops = 4.0 * B * S * 64 * 512 * K
+        tf = flops / (ms * 1e-3) / 1e12
+        out[f"sparse_attn_{name}"] = {
+            "B": B, "S": S, "N": N, "K": K, "ms": round(ms, 4), "achieved_tflops": round(tf, 1),
+            "frac_bf16": round(tf / bf16_peak, 4), "gathered_gb_per_s": round(B * S * K * 1024 / (ms * 1e-3) / 1e9, 1)}
+        del q, kv, sink, idx
+    for name, (M, K, N) in (("decode_M64_K4096_N1024", (64, 4096, 1024)),
+                            ("decode_M64_K1024_N32768", (64, 1024, 32768)),
+                            ("prefill_M8192_K1024_N32768", (8192, 1024, 32768))):
+        lin = FP8Linear(K, N, device=dev)
+        lin.weight.data.view(torch.uint8).copy_(torch.randint(0, 126, (N, K), device=dev, generator=g,
+                                                              dtype=torch.uint8))
+        lin.refresh_scale_atoms()
+        x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+        ms = _graph_ms(lambda: lin(x), flush)
+        nbytes = N * K + (N // 128) * (K // 128) + 2 * M * K + 2 * M * N
+        tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+        entry = {"M": M, "K": K, "N": N, "ms": round(ms, 4), "achieved_tflops": round(tf, 1),
+                 "GB_per_s": round(nbytes / (ms * 1e-3) / 1e9, 1)}
+        if M <= 64:
+            entry["frac_hbm"] = round(entry["GB_per_s"] / hbm, 4)
+        else:
+            entry["frac_fp8"] = round(tf / (2 * bf16_peak), 4)
+        out[f"fp8_linear_{name}"] = entry
+        del lin, x
+    _lib.raise_on_device_error()
+    out["peak_source"] = f"{src}: bf16 {bf16_peak} TFLOP/s (FP8 = 2x), HBM {hbm} GB/s"
+    torch.cuda.empty_cache()
+    return out
+
+
 # ---------------------------------------------------------------------------
 # CPU arm: the oracle restatement of the reference's layer on the host cores
 # ---------------------------------------------------------------------------
@@ -1092,6 +1204,9 @@ def run_reference(args, world, rank):
     if args.workload == "stack":  # the oracle's per-layer rate already bounds it: layers x one layer
         return {"impl": "reference", "unavailable": "the full-depth stack has no CPU arm of its own; "
                 "the per-layer CPU rate is the decode workload's reference line"}
+    if args.workload == "attention":
+        return {"impl": "reference", "unavailable": "the reference's attention fallback is a per-token Python loop; "
+                "its restatement is the parity oracle of the attention block, not a timed arm"}
     import torch
 
     threads = os.cpu_count() or 1
@@ -1165,6 +1280,20 @@ def main():
             print(json.dumps(res), flush=True)
         return
     world, rank, local = _dist_init(args.gpus)
+    if args.workload == "attention":
+        # the attention block's ops alone (one GPU; the other ranks idle)
+        if rank == 0:
+            import torch
+
+            dev = torch.device("cuda", local)
+            flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+            print(json.dumps({"workload": "attention", **_attention(args, dev, flush)}), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.workload == "stack":
         res = run_stack(args, world, rank, local)
         if rank == 0:

@@ -20,16 +20,21 @@
 // tcgen05 (kind::f16, bf16 inputs, fp32 accumulators in TMEM).
 //
 // Each CTA takes one query token and a range of 128-row chunks of its index
-// list (a split).  Pass 1 computes the scores chunk by chunk and keeps the
-// running per-head max and sum of exponentials; pass 2 recomputes the scores,
-// forms the final probabilities in bf16 and accumulates O^T in TMEM.  A token
-// with one split writes out directly; several splits write fp32 partials
-// (max, sum, unnormalised O) that sparse_attn_combine_kernel merges with the
-// sink term.
+// list (a split), in one pass with an online softmax: per chunk the rows are
+// gathered (cp.async, 16 B; the next chunk's rows are prefetched to L2 while
+// the tensor core works), the scores land in TMEM, every thread reads its row's
+// scores for 32 heads, P = exp(z - m) goes to shared memory in bf16 and the
+// output product accumulates O^T in TMEM.  The running max m of a head is
+// raised only when a score exceeds it by more than kSaRescaleLog (then O^T and
+// the partial sums are rescaled); the per-head max is a recursive-halving
+// reduction over the warp's lanes plus a 4-way combine in shared memory.  A
+// token with one split writes out directly with the sink folded into the
+// denominator; several splits write fp32 partials (max, sum, O relative to the
+// max) that sparse_attn_combine_kernel merges with the sink term.
 //
-// Warp roles (256 threads): all warps gather rows (cp.async, 16 B); warp 0,
-// lane 0 issues the MMAs; warps 0-3 own the TMEM lane quarters (lane = gathered
-// row in the score product, = d in the output product).
+// Warp roles (256 threads): all warps gather rows; warp 0, lane 0 issues the
+// MMAs; warp w reads TMEM lane quarter w % 4 (lane = gathered row in the score
+// product, = d in the output product) for heads 32 (w / 4) .. +31.
 #include "kernels.cuh"
 
 namespace dsv4 {
@@ -44,6 +49,7 @@ constexpr int kSaPBytes = kSaHeads * kSaChunk * 2; // 16 KB: P, 2 k tiles of [64
 constexpr int kSaCtrl = 4096;  // barrier, TMEM slot, 128 row indices, reductions
 constexpr size_t kSaSmem = 1024 + kSaQBytes + kSaCBytes + kSaPBytes + kSaCtrl;
 constexpr int kSaTmemCols = 512;  // S: cols 0..63; O^T: 4 d tiles x 64 cols at 256..511
+constexpr float kSaRescaleLog = 8.0f;  // headroom of the running max (natural log)
 
 // Byte offset of element (row, col) of a K-major tile set: 64-element k tiles of
 // [rows][128 B], 128-byte swizzle (16-byte unit index XOR row % 8).
@@ -78,17 +84,41 @@ __device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-// Load 64 consecutive fp32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
-  uint32_t a[32], b[32];
-  tmem_ld32_issue(taddr, a);
-  tmem_ld32_issue(taddr + 32, b);
-  tmem_wait_ld2(a, b);
+// Load 32 consecutive fp32 columns of this thread's TMEM lane and wait.
+__device__ __forceinline__ void tmem_ld32_wait(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  tmem_ld32_issue(taddr, r);
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31]) : : "memory");
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    v[i] = __uint_as_float(a[i]);
-    v[32 + i] = __uint_as_float(b[i]);
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Store 32 consecutive fp32 columns of this thread's TMEM lane (tcgen05.wait::st
+// before the tensor core reads them).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+               :: "r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])), "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31])) : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Reduce 32 values per lane over the warp's 32 lanes (max, or sum when kSum) by
+// recursive halving: at each step a lane keeps one half of its values, sends
+// the other half to its partner and combines (31 shuffles in all).  Afterwards
+// lane l holds the reduction of value l, which is returned.
+template <bool kSum>
+__device__ __forceinline__ float warp_reduce_scatter32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < o; ++i) {
+      const float send = up ? v[i] : v[i + o];
+      const float keep = up ? v[i + o] : v[i];
+      const float r = __shfl_xor_sync(0xffffffffu, send, o);
+      v[i] = kSum ? keep + r : fmaxf(keep, r);
+    }
   }
+  return v[0];
 }
 
 struct SaArgs {
@@ -113,12 +143,17 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_kernel(const SaArgs
   uint8_t* ctrl = sP + kSaPBytes;
   uint64_t* mma_bar = reinterpret_cast<uint64_t*>(ctrl);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctrl + 8);
-  int* s_idx = reinterpret_cast<int*>(ctrl + 16);            // [128] this chunk's kv rows (-1 invalid)
-  // [4 quarters][64] partial reductions, [64] reduced, [64] final max, [64] final 1 / sum: 448 floats
-  float* s_red = reinterpret_cast<float*>(ctrl + 16 + 4 * kSaChunk);
-  static_assert(16 + 4 * kSaChunk + 448 * 4 <= kSaCtrl, "control block too small");
+  int* s_idx = reinterpret_cast<int*>(ctrl + 16);                 // [128] this chunk's kv rows (-1 invalid)
+  float* s_red = reinterpret_cast<float*>(ctrl + 16 + 4 * kSaChunk);  // [4 quarters][64] partial reductions
+  float* s_m = s_red + 4 * kSaHeads;                             // [64] running max per head
+  float* s_f = s_m + kSaHeads;                                   // [64] rescale factor, then output factor
+  static_assert(16 + 4 * kSaChunk + 6 * kSaHeads * 4 <= kSaCtrl, "control block too small");
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int q4 = warp & 3;           // TMEM lane quarter: rows 32 q4 .. +31 of a chunk (or of a d tile)
+  const int h0 = (warp >> 2) * 32;   // warps 0-3 take heads 0-31, warps 4-7 heads 32-63
+  const int row = q4 * 32 + lane;    // this thread's gathered row (scores) and d within a d tile (output)
+  const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
   const int token = blockIdx.x / a.splits, split = blockIdx.x % a.splits;
   const int b = token / a.S;
   const int n_chunks = (a.K + kSaChunk - 1) / kSaChunk;
@@ -126,6 +161,17 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_kernel(const SaArgs
   const int c_end = min(n_chunks, c_begin + a.chunks_per_split);
   const __nv_bfloat16* kvb = a.kv + (size_t)b * a.N * kSaDim;
   const int* idx = a.idx + (size_t)token * a.K;
+  const __nv_bfloat16* qt = a.q + (size_t)token * kSaHeads * kSaDim;
+
+  auto load_index = [&](int c) -> int {
+    const int p = c * kSaChunk + tid;
+    int r = p < a.K ? __ldg(idx + p) : -1;
+    if (r >= a.N) {
+      record_error(DSV4_DEVERR_BAD_INDEX);
+      r = -1;
+    }
+    return r;
+  };
 
   if (tid == 0) {
     mbar_init(mma_bar, 1);
@@ -135,60 +181,65 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_kernel(const SaArgs
     tmem_alloc(tmem_slot, kSaTmemCols);
     tmem_relinquish();
   }
-  // Q of this token: 64 rows x 512, swizzled K-major
-  const __nv_bfloat16* qt = a.q + (size_t)token * kSaHeads * kSaDim;
-  for (int u = tid; u < kSaHeads * kSaDim / 8; u += kSaThreads) {
-    const int row = u / (kSaDim / 8), col = (u % (kSaDim / 8)) * 8;
-    cp_async16(smem_u32(sQ + sw128_offset(kSaHeads, row, col)), qt + (size_t)row * kSaDim + col);
+  if (tid < kSaHeads) s_m[tid] = -INFINITY;
+  int next_row = (tid < kSaChunk && c_begin < c_end) ? load_index(c_begin) : -1;
+
+  // Online softmax over the chunks: this thread keeps, for its row and its 32
+  // heads, the running max (the same in every thread of the head half) and a
+  // partial sum of the bf16 probabilities; O^T accumulates in TMEM relative to
+  // the running max.  The max is raised (and O, the sums rescaled) only when a
+  // score exceeds it by more than kSaRescaleLog, so probabilities stay below
+  // e^kSaRescaleLog and most chunks need no reduction at all.
+  float m_run[32], l_run[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    m_run[i] = -INFINITY;
+    l_run[i] = 0.f;
   }
-  cp_async_wait_all();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t t_s = tmem;          // scores: 64 columns
-  const uint32_t t_o = tmem + 256;    // O^T: 4 x 64 columns
-  const int q4 = warp & 3;            // TMEM lane quarter of warps 0-3 and 4-7
-  const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
-  const bool tmem_warp = warp < 4;    // warps 0-3 read the accumulators (lanes = their quarter)
-
-  float m_run = -INFINITY, l_run = 0.f;  // per head (thread h < 64 of warps 0-1 keeps head h)
   uint32_t mma_phase = 0;
-  bool any_valid = false;
+  bool first = true, any_valid = false;
   // A wait that runs out fails the whole CTA at once (every thread leaves the
-  // chunk loops at the same point, so no barrier is left waiting).
+  // chunk loop at the same point, so no barrier is left waiting).
   bool failed = false;
+  uint32_t tmem = 0;
 
-  // gather chunk c into sC (K-major swizzled), indices into s_idx
-  auto gather = [&](int c) {
-    for (int j = tid; j < kSaChunk; j += kSaThreads) {
-      const int p = c * kSaChunk + j;
-      int r = p < a.K ? idx[p] : -1;
-      if (r >= a.N) {
-        record_error(DSV4_DEVERR_BAD_INDEX);
-        r = -1;
-      }
-      s_idx[j] = r;
+  for (int c = c_begin; c < c_end; ++c) {
+    if (!first) {
+      // the previous chunk's output product is done with sC and sP
+      const bool ok = mbar_wait(mma_bar, mma_phase, DSV4_DEVERR_TIMEOUT_MMA);
+      mma_phase ^= 1;
+      failed = __syncthreads_or(!ok) != 0;
+      if (failed) break;
     }
+    if (tid < kSaChunk) s_idx[tid] = next_row;
     __syncthreads();
+    if (c == c_begin) {
+      for (int u = tid; u < kSaHeads * kSaDim / 8; u += kSaThreads) {
+        const int r = u / (kSaDim / 8), col = (u % (kSaDim / 8)) * 8;
+        cp_async16(smem_u32(sQ + sw128_offset(kSaHeads, r, col)), qt + (size_t)r * kSaDim + col);
+      }
+    }
     for (int u = tid; u < kSaChunk * kSaDim / 8; u += kSaThreads) {
-      const int row = u / (kSaDim / 8), col = (u % (kSaDim / 8)) * 8;
-      const int r = s_idx[row];
-      const uint32_t dst = smem_u32(sC + sw128_offset(kSaChunk, row, col));
-      if (r >= 0)
-        cp_async16(dst, kvb + (size_t)r * kSaDim + col);
+      const int r = u / (kSaDim / 8), col = (u % (kSaDim / 8)) * 8;
+      const int kr = s_idx[r];
+      const uint32_t dst = smem_u32(sC + sw128_offset(kSaChunk, r, col));
+      if (kr >= 0)
+        cp_async16(dst, kvb + (size_t)kr * kSaDim + col);
       else
         asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "r"(0) : "memory");
     }
+    // the next chunk's indices load while this one is gathered
+    next_row = (tid < kSaChunk && c + 1 < c_end) ? load_index(c + 1) : -1;
     cp_async_wait_all();
     fence_proxy_async_shared();  // the generic-proxy writes, before the tensor core reads them
+    tc_fence_before();
     __syncthreads();
-  };
+    tc_fence_after();
+    tmem = *tmem_slot;
+    const uint32_t t_s = tmem, t_o = tmem + 256;
 
-  // S^T = C . Q^T into t_s; waits for completion (bounded)
-  auto scores = [&]() -> bool {
+    // S^T[j, h] = C[j, :] . Q[h, :]
     if (tid == 0) {
-      tc_fence_after();
       const uint32_t idesc = idesc_bf16_major(kSaHeads, 0, 0);
 #pragma unroll 1
       for (int kt = 0; kt < kSaDim / 64; ++kt) {
@@ -199,112 +250,73 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_kernel(const SaArgs
       }
       tc_commit(mma_bar);
     }
+    // the next chunk's rows start towards L2 while the tensor core works
+    if (tid < kSaChunk && next_row >= 0) {
+      const char* src = reinterpret_cast<const char*>(kvb + (size_t)next_row * kSaDim);
+#pragma unroll
+      for (int l = 0; l < kSaDim * 2 / 128; ++l)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(src + l * 128)));
+    }
     __syncwarp();
-    const bool ok = mbar_wait(mma_bar, mma_phase, DSV4_DEVERR_TIMEOUT_MMA);
-    mma_phase ^= 1;
-    failed = __syncthreads_or(!ok) != 0;
+    {
+      const bool ok = mbar_wait(mma_bar, mma_phase, DSV4_DEVERR_TIMEOUT_MMA);
+      mma_phase ^= 1;
+      failed = __syncthreads_or(!ok) != 0;
+    }
     tc_fence_after();
-    return !failed;
-  };
+    if (failed) break;
 
-  // per-head max (mode 0) or sum (mode 1) over the 128 rows of v[64] held by
-  // the threads of warps 0-3 (thread = row); result for head h at s_red[h]
-  auto head_reduce = [&](float* v, int mode) {
-    if (tmem_warp) {
-#pragma unroll 8
-      for (int h = 0; h < kSaHeads; ++h) {
-        float x = v[h];
+    float z[32];
+    tmem_ld32_wait(t_s + lane_base + h0, z);
+    const bool valid = s_idx[row] >= 0;
+    any_valid |= valid;
+    bool raise = false;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          const float y = __shfl_xor_sync(0xffffffffu, x, o);
-          x = mode == 0 ? fmaxf(x, y) : x + y;
+    for (int i = 0; i < 32; ++i) {
+      z[i] = valid ? z[i] * a.scale : -INFINITY;
+      raise |= z[i] > m_run[i] + kSaRescaleLog;
+    }
+    if (__syncthreads_or(raise)) {
+      float t[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) t[i] = z[i];
+      s_red[q4 * kSaHeads + h0 + lane] = warp_reduce_scatter32<false>(t, lane);
+      __syncthreads();
+      if (tid < kSaHeads) {
+        float cm = s_red[tid];
+#pragma unroll
+        for (int w = 1; w < 4; ++w) cm = fmaxf(cm, s_red[w * kSaHeads + tid]);
+        const float mo = s_m[tid], mn = fmaxf(mo, cm);
+        s_f[tid] = mo == -INFINITY ? 0.f : __expf(mo - mn);
+        s_m[tid] = mn;
+      }
+      __syncthreads();
+      float alpha[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        alpha[i] = s_f[h0 + i];
+        m_run[i] = s_m[h0 + i];
+        l_run[i] *= alpha[i];
+      }
+      if (!first) {
+        // O^T columns of this thread's heads, in each of the 4 d tiles
+#pragma unroll 1
+        for (int dt = 0; dt < kSaDim / 128; ++dt) {
+          float o[32];
+          tmem_ld32_wait(t_o + 64 * dt + h0 + lane_base, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= alpha[i];
+          tmem_st32(t_o + 64 * dt + h0 + lane_base, o);
         }
-        if (lane == 0) s_red[q4 * kSaHeads + h] = x;  // [4 quarters][64], 1 KB
+        tmem_wait_st();
       }
     }
-    __syncthreads();
-    if (tid < kSaHeads) {
-      float x = s_red[tid];
-      for (int w = 1; w < 4; ++w) x = mode == 0 ? fmaxf(x, s_red[w * kSaHeads + tid]) : x + s_red[w * kSaHeads + tid];
-      s_red[4 * kSaHeads + tid] = x;
-    }
-    __syncthreads();
-  };
-
-  float z[kSaHeads];
-  // ---------------------------------------------------------------- pass 1
-  for (int c = c_begin; c < c_end && !failed; ++c) {
-    gather(c);
-    if (!scores()) break;
-    bool valid = false;
-    if (tmem_warp) {
-      tmem_ld64(t_s + lane_base, z);
-      valid = s_idx[q4 * 32 + lane] >= 0;
+    // P[h][j] in bf16 (K-major over j: 2 k tiles of [64 rows][128 B])
 #pragma unroll
-      for (int h = 0; h < kSaHeads; ++h) z[h] = valid ? z[h] * a.scale : -INFINITY;
-    }
-    any_valid |= __syncthreads_or(valid);
-    head_reduce(z, 0);
-    // every thread needs the new running max of every head: read s_red[256 + h]
-    if (tmem_warp) {
-#pragma unroll
-      for (int h = 0; h < kSaHeads; ++h) {
-        const float mn = s_red[4 * kSaHeads + h];
-        z[h] = (valid && mn > -INFINITY) ? __expf(z[h] - mn) : 0.f;
-      }
-    }
-    // the chunk's max must be read by all before the sums overwrite s_red
-    float cmax = tid < kSaHeads ? s_red[4 * kSaHeads + tid] : 0.f;
-    __syncthreads();
-    head_reduce(z, 1);
-    if (tid < kSaHeads) {
-      const float csum = s_red[4 * kSaHeads + tid];
-      if (cmax > -INFINITY) {
-        const float mn = fmaxf(m_run, cmax);
-        l_run = (m_run > -INFINITY ? l_run * __expf(m_run - mn) : 0.f) + csum * __expf(cmax - mn);
-        m_run = mn;
-      }
-    }
-    tc_fence_before();
-    __syncthreads();
-  }
-  // the per-head max and sum of this split: published for pass 2 (and the
-  // sink folded in when this split is the token's only one)
-  float* s_m = s_red + 5 * kSaHeads;  // [64] final max
-  float* s_l = s_m + kSaHeads;        // [64] final 1 / denominator (or sum)
-  if (tid < kSaHeads) {
-    float m = m_run, l = l_run;
-    if (a.splits == 1) {
-      const float sk = a.sink[tid];
-      const float mn = fmaxf(m, sk);
-      l = (m > -INFINITY ? l * __expf(m - mn) : 0.f) + __expf(sk - mn);
-      m = mn;
-    }
-    s_m[tid] = m;
-    s_l[tid] = l > 0.f ? 1.0f / l : 0.f;
-    if (a.splits > 1) {
-      float* ml = a.part_ml + ((size_t)token * a.splits + split) * kSaHeads * 2;
-      ml[2 * tid] = m_run;
-      ml[2 * tid + 1] = l_run;
-    }
-  }
-  __syncthreads();
-
-  // ---------------------------------------------------------------- pass 2
-  bool first = true;
-  for (int c = c_begin; c < c_end && !failed; ++c) {
-    gather(c);
-    if (!scores()) break;
-    if (tmem_warp) {
-      tmem_ld64(t_s + lane_base, z);
-      const int j = q4 * 32 + lane;
-      const bool valid = s_idx[j] >= 0;
-      // P[h][j] (bf16, K-major over j: 2 k tiles of [64 rows][128 B])
-#pragma unroll 8
-      for (int h = 0; h < kSaHeads; ++h) {
-        const float p = valid ? __expf(z[h] * a.scale - s_m[h]) * s_l[h] : 0.f;
-        *reinterpret_cast<__nv_bfloat16*>(sP + sw128_offset(kSaHeads, h, j)) = __float2bfloat16_rn(p);
-      }
+    for (int i = 0; i < 32; ++i) {
+      const __nv_bfloat16 pb = __float2bfloat16_rn(valid ? __expf(z[i] - m_run[i]) : 0.f);
+      l_run[i] += __bfloat162float(pb);
+      *reinterpret_cast<__nv_bfloat16*>(sP + sw128_offset(kSaHeads, h0 + i, row)) = pb;
     }
     fence_proxy_async_shared();
     tc_fence_before();
@@ -329,36 +341,60 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_kernel(const SaArgs
       }
       tc_commit(mma_bar);
     }
-    __syncwarp();
+    first = false;
+  }
+  if (!first && !failed) {
     const bool ok = mbar_wait(mma_bar, mma_phase, DSV4_DEVERR_TIMEOUT_MMA);
     mma_phase ^= 1;
     failed = __syncthreads_or(!ok) != 0;
-    tc_fence_after();
-    first = false;
   }
+  tc_fence_after();
 
   // ---------------------------------------------------------------- output
-  // thread (quarter q4, lane) of warps 0-3 holds d = 128 dt + 32 q4 + lane
-  if (tmem_warp && !failed) {
-    const int tok_out = token;
+  // per-head sums over the 128 rows, then the factor each head's O^T column
+  // is scaled by: the sink folded in when this split is the token's only one
+  {
+    float t[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) t[i] = l_run[i];
+    s_red[q4 * kSaHeads + h0 + lane] = warp_reduce_scatter32<true>(t, lane);
+  }
+  const bool any = __syncthreads_or(any_valid) != 0;
+  if (tid < kSaHeads) {
+    const float l = s_red[tid] + s_red[kSaHeads + tid] + s_red[2 * kSaHeads + tid] + s_red[3 * kSaHeads + tid];
+    const float m = s_m[tid];
+    if (a.splits == 1) {
+      const float sk = a.sink[tid];
+      const float M = fmaxf(m, sk);
+      const float den = (m > -INFINITY ? l * __expf(m - M) : 0.f) + __expf(sk - M);
+      s_f[tid] = (any && m > -INFINITY) ? __expf(m - M) / den : 0.f;
+    } else {
+      float* ml = a.part_ml + ((size_t)token * a.splits + split) * kSaHeads * 2;
+      ml[2 * tid] = m;
+      ml[2 * tid + 1] = l;
+    }
+  }
+  __syncthreads();
+  if (!failed) {
 #pragma unroll 1
     for (int dt = 0; dt < kSaDim / 128; ++dt) {
-      float o[kSaHeads];
-      if (!first) tmem_ld64(t_o + 64 * dt + lane_base, o);
-      const int d = 128 * dt + 32 * q4 + lane;
-      if (a.splits == 1) {
-        __nv_bfloat16* dst = a.out + (size_t)tok_out * kSaHeads * kSaDim + d;
-#pragma unroll 8
-        for (int h = 0; h < kSaHeads; ++h)
-          dst[(size_t)h * kSaDim] = __float2bfloat16_rn((first || !any_valid) ? 0.f : o[h]);
+      float o[32];
+      if (!first) {
+        tmem_ld32_wait((*tmem_slot + 256) + 64 * dt + h0 + lane_base, o);
       } else {
-        // unnormalised partial: O * sum (so the combine can rescale by max)
-        float* dst = a.part_o + ((size_t)tok_out * a.splits + split) * kSaHeads * kSaDim + d;
-#pragma unroll 8
-        for (int h = 0; h < kSaHeads; ++h) {
-          const float l = s_l[h] > 0.f ? 1.0f / s_l[h] : 0.f;
-          dst[(size_t)h * kSaDim] = first ? 0.f : o[h] * l;
-        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = 0.f;
+      }
+      const int d = 128 * dt + row;
+      if (a.splits == 1) {
+        __nv_bfloat16* dst = a.out + ((size_t)token * kSaHeads + h0) * kSaDim + d;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) dst[(size_t)i * kSaDim] = __float2bfloat16_rn(o[i] * s_f[h0 + i]);
+      } else {
+        // O relative to this split's running max (the combine rescales it)
+        float* dst = a.part_o + (((size_t)token * a.splits + split) * kSaHeads + h0) * kSaDim + d;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) dst[(size_t)i * kSaDim] = o[i];
       }
     }
   }
@@ -366,7 +402,7 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_kernel(const SaArgs
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kSaTmemCols);
+    tmem_dealloc(*tmem_slot, kSaTmemCols);
   }
 }
 

@@ -252,6 +252,71 @@ std::tuple<at::Tensor, at::Tensor> act_quant(const at::Tensor& x) {
   return {q, s};
 }
 
+// ---------------------------------------------------------- attention block
+// The official kernel.sparse_attn(q, kv, attn_sink, topk_idxs, softmax_scale)
+// (spark_runtime/lazy_official_runtime.py:1016-1049 swaps in a Python fallback).
+at::Tensor sparse_attn(const at::Tensor& q, const at::Tensor& kv, const at::Tensor& attn_sink,
+                       const at::Tensor& topk_idxs, double softmax_scale) {
+  check_cuda(q, "q");
+  check_cuda(kv, "kv");
+  TORCH_CHECK(q.dim() == 4 && kv.dim() == 3 && topk_idxs.dim() == 3, "q [B,S,H,D], kv [B,N,D], topk_idxs [B,S,K]");
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && kv.scalar_type() == at::kBFloat16, "q and kv must be bfloat16");
+  c10::cuda::CUDAGuard guard(q.device());
+  const int B = static_cast<int>(q.size(0)), S = static_cast<int>(q.size(1));
+  const int H = static_cast<int>(q.size(2)), D = static_cast<int>(q.size(3));
+  const int N = static_cast<int>(kv.size(1)), K = static_cast<int>(topk_idxs.size(2));
+  TORCH_CHECK(kv.size(0) == B && kv.size(2) == D && topk_idxs.size(0) == B && topk_idxs.size(1) == S,
+              "q, kv and topk_idxs disagree on batch, positions or head dim");
+  const at::Tensor sink = attn_sink.to(q.device(), at::kFloat).contiguous();
+  const at::Tensor idx = topk_idxs.to(q.device(), at::kInt).contiguous();
+  at::Tensor out = at::empty_like(q);
+  const long long need = dsv4_sparse_attn_workspace_bytes(B, S, K);
+  TORCH_CHECK(need >= 0, "sparse_attn: invalid shape");
+  at::Tensor ws = at::empty({std::max<long long>(need, 1)}, q.options().dtype(at::kByte));
+  check_status(dsv4_sparse_attn(q.data_ptr(), kv.data_ptr(), sink.data_ptr<float>(), idx.data_ptr<int>(), B, S, H,
+                                N, D, K, static_cast<float>(softmax_scale), out.data_ptr(), ws.data_ptr(), need,
+                                stream_of(q)),
+               "dsv4_sparse_attn");
+  return out;
+}
+
+// The official linear for an FP8 weight: act_quant(x) then fp8_gemm with the
+// weight's 128x128 ue8m0 block scales, given here as the atoms
+// build_fp8_weight_atoms lays out once per weight.
+at::Tensor build_fp8_weight_atoms(const at::Tensor& scale, int64_t out_features, int64_t in_features) {
+  check_cuda(scale, "scale");
+  c10::cuda::CUDAGuard guard(scale.device());
+  const long long n = dsv4_fp8_weight_atoms_bytes(static_cast<int>(out_features), static_cast<int>(in_features));
+  TORCH_CHECK(n > 0, "in and out features must be multiples of 128");
+  at::Tensor atoms = at::empty({n}, scale.options().dtype(at::kByte));
+  check_status(dsv4_build_fp8_weight_atoms(static_cast<const uint8_t*>(scale.data_ptr()),
+                                           static_cast<int>(out_features), static_cast<int>(in_features),
+                                           atoms.data_ptr<uint8_t>(), stream_of(scale)),
+               "dsv4_build_fp8_weight_atoms");
+  return atoms;
+}
+
+at::Tensor fp8_linear(const at::Tensor& x, const at::Tensor& weight, const at::Tensor& weight_atoms) {
+  check_cuda(weight, "weight");
+  check_cuda(weight_atoms, "weight_atoms");
+  TORCH_CHECK(weight.dim() == 2 && weight.element_size() == 1, "weight must be [out, in] e4m3");
+  const int64_t N = weight.size(0), K = weight.size(1);
+  const at::Tensor x2 = bf16_rows(x, K).contiguous();
+  c10::cuda::CUDAGuard guard(x2.device());
+  const int M = static_cast<int>(x2.size(0));
+  const long long need = dsv4_fp8_linear_workspace_bytes(M, static_cast<int>(N), static_cast<int>(K));
+  TORCH_CHECK(need >= 0, "fp8_linear: out_features must be a multiple of 256, in_features of 512");
+  at::Tensor ws = at::empty({std::max<long long>(need, 1)}, x2.options().dtype(at::kByte));
+  std::vector<int64_t> shape(x.sizes().begin(), x.sizes().end());
+  shape.back() = N;
+  at::Tensor y = at::empty(shape, x2.options());
+  check_status(dsv4_fp8_linear(x2.data_ptr(), M, static_cast<int>(K), static_cast<const uint8_t*>(weight.data_ptr()),
+                               weight_atoms.data_ptr<uint8_t>(), static_cast<int>(N), y.data_ptr(), ws.data_ptr(),
+                               need, stream_of(x2)),
+               "dsv4_fp8_linear");
+  return y;
+}
+
 // ---------------------------------------------------------- arena / materializer
 int64_t materialize(const at::Tensor& slab, const at::Tensor& src_off, const at::Tensor& dst_slot,
                     const OptT& arena, int64_t slot_stride, const OptT& arena_sf, int64_t sf_slot_stride,
@@ -465,6 +530,9 @@ TORCH_LIBRARY(dsv4moe, m) {
         ", int rank, int world, int exchange, Tensor ret_pos, Tensor indices, Tensor x_own, int cap, int epoch, "
         "Tensor workspace) -> Tensor");
   m.def("read_into(int fd, Tensor(a!) destination, int size, int offset) -> int");
+  m.def("sparse_attn(Tensor q, Tensor kv, Tensor attn_sink, Tensor topk_idxs, float softmax_scale) -> Tensor");
+  m.def("build_fp8_weight_atoms(Tensor scale, int out_features, int in_features) -> Tensor");
+  m.def("fp8_linear(Tensor x, Tensor weight, Tensor weight_atoms) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(dsv4moe, CUDA, m) {
@@ -484,6 +552,9 @@ TORCH_LIBRARY_IMPL(dsv4moe, CUDA, m) {
   m.impl("ep_dispatch_p2p", &ep_dispatch_p2p);
   m.impl("ep_expert_forward_p2p", &ep_expert_forward_p2p);
   m.impl("ep_combine_p2p", &ep_combine_p2p);
+  m.impl("sparse_attn", &sparse_attn);
+  m.impl("build_fp8_weight_atoms", &build_fp8_weight_atoms);
+  m.impl("fp8_linear", &fp8_linear);
 }
 
 // Ops without tensor inputs on a device (sizes, host reads) dispatch here.

@@ -21,8 +21,7 @@ from __future__ import annotations
 import torch
 from torch import nn
 
-from . import _lib
-from ._lib import check, ptr, stream_ptr
+from . import _lib, ops
 
 E4M3 = torch.float8_e4m3fn
 E8M0 = torch.float8_e8m0fnu
@@ -31,21 +30,10 @@ E8M0 = torch.float8_e8m0fnu
 def sparse_attn(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor, topk_idxs: torch.Tensor,
                 softmax_scale: float) -> torch.Tensor:
     """q [B,S,H,D] bf16, kv [B,N,D] bf16, attn_sink [H], topk_idxs [B,S,K]
-    (-1 = no row) -> [B,S,H,D] in q's dtype.  H = 64, D = 512."""
-    B, S, H, D = q.shape
-    N, K = kv.shape[1], topk_idxs.shape[-1]
-    qb = q.to(torch.bfloat16).contiguous()
-    kvb = kv.to(torch.bfloat16).contiguous()
-    sink = attn_sink.to(device=q.device, dtype=torch.float32).contiguous()
-    idx = topk_idxs.to(device=q.device, dtype=torch.int32).contiguous()
-    out = torch.empty((B, S, H, D), dtype=torch.bfloat16, device=q.device)
-    lib = _lib.load()
-    need = int(lib.dsv4_sparse_attn_workspace_bytes(B, S, K))
-    if need < 0:
-        raise RuntimeError("dsv4_sparse_attn_workspace_bytes: invalid shape")
-    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device) if need else None
-    check(lib.dsv4_sparse_attn(ptr(qb), ptr(kvb), ptr(sink), ptr(idx), B, S, H, N, D, K, float(softmax_scale),
-                               ptr(out), ptr(ws), need, stream_ptr()), "dsv4_sparse_attn")
+    (-1 = no row) -> [B,S,H,D] in q's dtype.  H = 64, D = 512.  Runs
+    ``torch.ops.dsv4moe.sparse_attn`` (one call into ``dsv4_sparse_attn``)."""
+    out = ops.load().sparse_attn(q.to(torch.bfloat16).contiguous(), kv.to(torch.bfloat16).contiguous(),
+                                 attn_sink, topk_idxs, float(softmax_scale))
     return out.to(q.dtype)
 
 
@@ -62,28 +50,16 @@ class FP8Linear(nn.Module):
                                    requires_grad=False)
         self.scale = nn.Parameter(torch.full((out_features // 128, in_features // 128), 127, dtype=torch.uint8,
                                              device=device).view(E8M0), requires_grad=False)
-        n = int(_lib.load().dsv4_fp8_weight_atoms_bytes(out_features, in_features))
-        if n <= 0:
+        if int(_lib.load().dsv4_fp8_weight_atoms_bytes(out_features, in_features)) <= 0:
             raise RuntimeError("FP8Linear needs in and out features that are multiples of 128")
-        self.register_buffer("scale_atoms", torch.zeros(n, dtype=torch.uint8, device=device), persistent=False)
+        self.register_buffer("scale_atoms", torch.zeros(0, dtype=torch.uint8, device=device), persistent=False)
         self.register_load_state_dict_post_hook(lambda m, _keys: m.refresh_scale_atoms())
         self.refresh_scale_atoms()
 
     def refresh_scale_atoms(self) -> None:
-        check(_lib.load().dsv4_build_fp8_weight_atoms(ptr(self.scale), self.out_features, self.in_features,
-                                                      ptr(self.scale_atoms), stream_ptr()),
-              "dsv4_build_fp8_weight_atoms")
+        self.scale_atoms = ops.load().build_fp8_weight_atoms(self.scale, self.out_features, self.in_features)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        shape = x.shape
-        x2 = x.reshape(-1, self.in_features).to(torch.bfloat16).contiguous()
-        M = x2.shape[0]
-        y = torch.empty((M, self.out_features), dtype=torch.bfloat16, device=x2.device)
-        lib = _lib.load()
-        need = int(lib.dsv4_fp8_linear_workspace_bytes(M, self.out_features, self.in_features))
-        if need < 0:
-            raise RuntimeError("FP8Linear: out_features must be a multiple of 256, in_features of 512")
-        ws = torch.empty(max(need, 1), dtype=torch.uint8, device=x2.device)
-        check(lib.dsv4_fp8_linear(ptr(x2), M, self.in_features, ptr(self.weight), ptr(self.scale_atoms),
-                                  self.out_features, ptr(y), ptr(ws), need, stream_ptr()), "dsv4_fp8_linear")
-        return y.view(*shape[:-1], self.out_features).to(x.dtype)
+        """``torch.ops.dsv4moe.fp8_linear`` (act_quant + the FP8 GEMM) in bf16, cast to x's dtype."""
+        y = ops.load().fp8_linear(x.to(torch.bfloat16).contiguous(), self.weight, self.scale_atoms)
+        return y.to(x.dtype)

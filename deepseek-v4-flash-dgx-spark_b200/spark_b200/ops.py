@@ -103,3 +103,16 @@ def _register_fakes() -> None:
     @fake("ep_combine")
     def _(layer, dims, scalars, rank, world, ret_recv, ret_pos, indices, x_own, R, workspace):
         return torch.empty_like(x_own)
+
+    @fake("sparse_attn")
+    def _(q, kv, attn_sink, topk_idxs, softmax_scale):
+        return torch.empty_like(q)
+
+    @fake("build_fp8_weight_atoms")
+    def _(scale, out_features, in_features):
+        n = int(_lib.load().dsv4_fp8_weight_atoms_bytes(out_features, in_features))
+        return scale.new_empty((n,), dtype=torch.uint8)
+
+    @fake("fp8_linear")
+    def _(x, weight, weight_atoms):
+        return x.new_empty((*x.shape[:-1], weight.shape[0]))

@@ -113,3 +113,28 @@ def test_fp8_linear_matches_the_oracle(cuda_device, M, K, N):
     _lib.raise_on_device_error()
     ref = A.fp8_linear(x.float().numpy(), w.view(torch.uint8).numpy(), s.numpy())
     assert _rel_err(y.float().cpu().numpy(), ref) <= 2e-2
+
+
+def test_raw_c_abi_and_torch_op_agree_bit_for_bit(cuda_device):
+    """The same kernel reached through ctypes (dsv4_sparse_attn with a caller
+    workspace) and through torch.ops.dsv4moe.sparse_attn gives equal bytes."""
+    from spark_b200 import _lib, ops
+
+    q, kv, sink, idx = _case(1, 3, 900, 384, seed=17)
+    q, kv, sink, idx = q.cuda(), kv.cuda(), sink.cuda(), idx.cuda()
+    lib = _lib.load()
+    B, S, H, D = q.shape
+    need = int(lib.dsv4_sparse_attn_workspace_bytes(B, S, idx.shape[-1]))
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
+    out = torch.empty_like(q)
+    _lib.check(lib.dsv4_sparse_attn(_lib.ptr(q), _lib.ptr(kv), _lib.ptr(sink), _lib.ptr(idx), B, S, H, kv.shape[1],
+                                    D, idx.shape[-1], 0.05, _lib.ptr(out), _lib.ptr(ws), need, _lib.stream_ptr()),
+               "dsv4_sparse_attn")
+    via_op = ops.load().sparse_attn(q, kv, sink, idx, 0.05)
+    torch.cuda.synchronize()
+    _lib.raise_on_device_error()
+    assert torch.equal(out, via_op)
+    with pytest.raises(RuntimeError):
+        _lib.check(lib.dsv4_sparse_attn(_lib.ptr(q), _lib.ptr(kv), _lib.ptr(sink), _lib.ptr(idx), B, S, H, kv.shape[1],
+                                        D, idx.shape[-1], 0.05, _lib.ptr(out), _lib.ptr(ws), max(need - 256, 0),
+                                        _lib.stream_ptr()), "dsv4_sparse_attn")

@@ -12,7 +12,7 @@ import torch
 OPS = ["moe_forward", "moe_forward_out", "moe_workspace_bytes", "expert_forward", "gate_route", "gate_logits",
        "gate_topk", "act_quant", "materialize", "build_scale_atoms", "build_shared_scale_atoms", "ep_dispatch",
        "ep_expert_forward", "ep_combine", "ep_dispatch_p2p", "ep_expert_forward_p2p", "ep_combine_p2p",
-       "read_into"]
+       "read_into", "sparse_attn", "build_fp8_weight_atoms", "fp8_linear"]
 
 
 @pytest.fixture(scope="module")
@@ -48,6 +48,15 @@ def test_fake_kernels_give_output_shapes_on_meta(dsv4):
     assert dsv4.gate_logits(x, layer[0]).shape == (T, E)
     assert dsv4.expert_forward(x, 0, None, layer, dims, [1.0, 0.0]).shape == (T, H)
     assert ops.OPS_LIB.name == "libdsv4moe_torch.so"
+    q = torch.empty(2, 3, 64, 512, dtype=torch.bfloat16, device=m)
+    kv = torch.empty(2, 100, 512, dtype=torch.bfloat16, device=m)
+    o = dsv4.sparse_attn(q, kv, torch.empty(64, device=m), torch.empty(2, 3, 16, dtype=torch.int32, device=m), 0.04)
+    assert o.shape == q.shape and o.dtype == torch.bfloat16
+    atoms = dsv4.build_fp8_weight_atoms(torch.empty(4, 8, dtype=torch.uint8, device=m), 512, 1024)
+    assert atoms.dtype == torch.uint8 and atoms.numel() > 0
+    y = dsv4.fp8_linear(torch.empty(2, 5, 1024, dtype=torch.bfloat16, device=m),
+                        torch.empty(512, 1024, dtype=torch.uint8, device=m), atoms)
+    assert y.shape == (2, 5, 512) and y.dtype == torch.bfloat16
 
 
 def test_read_into_op_matches_the_reference_loader():
