@@ -759,27 +759,47 @@ int dsv4_expert_forward(const dsv4_moe_layer* L, int expert, const void* x, int 
 namespace dsv4 {
 
 struct LinearPlan {
-  int rows_pad, block_n, max_tiles;
-  long long off[6];
+  int rows_pad, block_n, max_tiles, split;
+  long long off[8];
   long long total;
 };
 
-static LinearPlan make_linear_plan(int M, int K) {
+// A linear layer of few rows has few work items (one per 256 output features
+// and row tile): N = 1024 at decode is 4 items for 148 SMs.  Under the split-K
+// setting (dsv4_set_k_split: 1 = off, the default; 0 = auto; n = up to n) its
+// k range is cut into S slices of whole scale groups: in auto, the largest
+// power of two up to 8 that divides the groups and keeps items x S within the
+// SM count.
+static int linear_split(int tiles, int N, int K, int block_n, int nsm) {
+  const int groups = K / 512;
+  const int setting = k_split_setting();
+  if (setting == 1 || block_n > 64) return 1;
+  const long long work = (long long)tiles * (N / 256);
+  const int cap = setting > 1 ? (setting < 8 ? setting : 8) : 8;
+  int s = 1;
+  while (s * 2 <= cap && groups % (s * 2) == 0 && (setting > 1 || work * s * 2 <= nsm)) s *= 2;
+  return s;
+}
+
+static LinearPlan make_linear_plan(int M, int N, int K) {
   LinearPlan p{};
   p.block_n = M <= 32 ? 32 : (M <= 64 ? 64 : 128);
   p.rows_pad = (M + 31) / 32 * 32;
   p.max_tiles = (M + p.block_n - 1) / p.block_n + 1;
+  p.split = linear_split((M + p.block_n - 1) / p.block_n, N, K, p.block_n, num_sms());
   const long long groups = p.rows_pad / 32 + 4;
-  long long sz[6] = {
+  long long sz[8] = {
       16,                                  // n_tiles, total_rows
       (long long)p.rows_pad * 4,           // slot_token
       (long long)p.rows_pad * 4,           // slot_weight (unused by the non-gated epilogue)
       (long long)p.max_tiles * 16,         // tiles
       (long long)p.rows_pad * K,           // xq
       groups * (K / 512) * 512,            // xsf
+      p.split > 1 ? (long long)p.split * p.rows_pad * N * 4 : 0,     // split-K partial sums
+      p.split > 1 ? (long long)p.max_tiles * (N / 256) * 4 : 0,      // split-K item counters
   };
   long long o = 0;
-  for (int i = 0; i < 6; ++i) {
+  for (int i = 0; i < 8; ++i) {
     p.off[i] = o;
     o += align256(sz[i]);
   }
@@ -806,7 +826,7 @@ int dsv4_build_fp8_weight_atoms(const uint8_t* scale, int N, int K, uint8_t* ato
 
 long long dsv4_fp8_linear_workspace_bytes(int M, int N, int K) {
   if (!linear_shape_ok(M, N, K)) return -1;
-  return make_linear_plan(M, K).total;
+  return make_linear_plan(M, N, K).total;
 }
 
 int dsv4_fp8_linear(const void* x, int M, int K, const uint8_t* w, const uint8_t* w_atoms, int N, void* y,
@@ -817,7 +837,7 @@ int dsv4_fp8_linear(const void* x, int M, int K, const uint8_t* w, const uint8_t
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15) ||
       (reinterpret_cast<uintptr_t>(y) & 15))
     return DSV4_ERR_ARG;
-  const LinearPlan p = make_linear_plan(M, K);
+  const LinearPlan p = make_linear_plan(M, N, K);
   if (!workspace || workspace_bytes < p.total) return DSV4_ERR_WORKSPACE;
   bind_device(workspace);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -851,8 +871,16 @@ int dsv4_fp8_linear(const void* x, int M, int K, const uint8_t* w, const uint8_t
   g.slot_weight = slot_weight;
   g.out_bf16 = static_cast<__nv_bfloat16*>(y);
   g.out_ld = N;
-  g.k_split = 1;
-  const long long work = (long long)p.max_tiles * g.nb_count;
+  g.k_split = p.split;
+  if (p.split > 1) {
+    g.partial = reinterpret_cast<float*>(ws + p.off[6]);
+    g.part_rows = p.rows_pad;
+    g.part_ld = N;
+    g.item_done = reinterpret_cast<int*>(ws + p.off[7]);
+    if (cudaMemsetAsync(g.item_done, 0, (size_t)p.max_tiles * g.nb_count * 4, st) != cudaSuccess)
+      return DSV4_ERR_CUDA;
+  }
+  const long long work = (long long)p.max_tiles * g.nb_count * p.split;
   const int grid = (int)(work < nsm ? work : nsm);
   return launch_expert_gemm(false, p.block_n, tw, tw, tw, tw, tx, g, grid, st);
 }

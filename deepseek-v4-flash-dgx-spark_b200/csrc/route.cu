@@ -357,15 +357,16 @@ __global__ void __launch_bounds__(256) route_scatter_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// Per-128 act_quant of one row by one warp into a single destination row (the
-// expert forward's identity plan and the plain act_quant entry point).
+// Per-128 act_quant of k tiles [kt_begin, kt_end) of one row by one warp into a
+// single destination row (the expert forward's identity plan, the linear layer
+// and the plain act_quant entry point).
 // ---------------------------------------------------------------------------
 
 template <typename ScaleSink>
 __device__ __forceinline__ void quant_row(const __nv_bfloat16* __restrict__ src, bool valid,
-                                          uint8_t* __restrict__ dst, int KT, int lane,
+                                          uint8_t* __restrict__ dst, int kt_begin, int KT, int lane,
                                           ScaleSink sink) {
-  for (int k0 = 0; k0 < KT; k0 += kQuantGroup) {
+  for (int k0 = kt_begin; k0 < KT; k0 += kQuantGroup) {
     uint2 raw[kQuantGroup];
 #pragma unroll
     for (int g = 0; g < kQuantGroup; ++g) {
@@ -404,10 +405,13 @@ __global__ void __launch_bounds__(256) permute_quant_kernel(
   const int lane = threadIdx.x & 31;
   const int total = *total_rows_ptr;
   const int KT = H / 128;
+  // blockIdx.y takes one share of every row's k tiles (few rows: more warps)
+  const int per = (KT + gridDim.y - 1) / gridDim.y;
+  const int kb = blockIdx.y * per, ke = min(KT, kb + per);
   const int nwarps = (gridDim.x * blockDim.x) >> 5;
   for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < total; row += nwarps) {
     const int t = slot_token[row];
-    quant_row(x + (size_t)(t < 0 ? 0 : t) * H, t >= 0, xq + (size_t)row * H, KT, lane,
+    quant_row(x + (size_t)(t < 0 ? 0 : t) * H, t >= 0, xq + (size_t)row * H, kb, ke, lane,
               [&](int kt, uint32_t s) {
                 if (lane < 4) {
                   const int m1 = lane;
@@ -427,7 +431,7 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const __nv_bfloat16* __r
   const int KT = K / 128;
   const int nwarps = (gridDim.x * blockDim.x) >> 5;
   for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < M; row += nwarps) {
-    quant_row(x + (size_t)row * K, true, q + (size_t)row * K, KT, lane, [&](int kt, uint32_t sc) {
+    quant_row(x + (size_t)row * K, true, q + (size_t)row * K, 0, KT, lane, [&](int kt, uint32_t sc) {
       if (lane == 0) s[(size_t)row * KT + kt] = static_cast<uint8_t>(sc);
     });
   }
@@ -578,7 +582,15 @@ int launch_permute_quant(const void* x, int H, const int* slot_token, const int*
   int grid = (max_rows + warps - 1) / warps;
   grid = grid < num_sms * 8 ? grid : num_sms * 8;
   if (grid < 1) grid = 1;
-  launch_k(permute_quant_kernel, grid, warps * 32, 0, st,
+  // few rows: split each row's k tiles (whole groups of kQuantGroup) over
+  // blockIdx.y, up to about two CTAs per SM
+  const int KT = H / 128;
+  int ky = (2 * num_sms + grid - 1) / grid;
+  const int kmax = (KT + kQuantGroup - 1) / kQuantGroup;
+  ky = ky < kmax ? ky : kmax;
+  if (ky < 1) ky = 1;
+  while (ky > 1 && ((KT + ky - 1) / ky) % kQuantGroup) --ky;
+  launch_k(permute_quant_kernel, dim3(grid, ky), warps * 32, 0, st,
            static_cast<const __nv_bfloat16*>(x), H,
                                                     slot_token, total_rows_ptr, xq, sfb);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;

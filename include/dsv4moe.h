@@ -226,7 +226,11 @@ DSV4_API int dsv4_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* sc
  * (kind::mxf8f6f4, fp32 accumulate).  N % 256 == 0 and K % 512 == 0
  * (DSV4_ERR_UNSUPPORTED otherwise); x, W and y 16-byte aligned.
  * w_atoms: the weight's scales expanded once by dsv4_build_fp8_weight_atoms
- * (dsv4_fp8_weight_atoms_bytes(N, K) bytes) from scale [N/128][K/128]. */
+ * (dsv4_fp8_weight_atoms_bytes(N, K) bytes) from scale [N/128][K/128].
+ * With the split-K setting on (dsv4_set_k_split; off by default) and M <= 64,
+ * the k range is split into 2-8 slices of whole 512-wide groups whose fp32
+ * sums are added in slice order (deterministic); the workspace size follows
+ * the setting in force when it is asked for. */
 DSV4_API long long dsv4_fp8_weight_atoms_bytes(int N, int K);
 DSV4_API int dsv4_build_fp8_weight_atoms(const uint8_t* scale, int N, int K, uint8_t* atoms, void* stream);
 DSV4_API long long dsv4_fp8_linear_workspace_bytes(int M, int N, int K);

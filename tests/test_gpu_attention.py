@@ -40,6 +40,17 @@ def _attn_close(got, ref):
     assert _rel_err(got, ref) <= 5e-2, _rel_err(got, ref)
 
 
+@pytest.fixture
+def auto_split():
+    """The split-K setting at auto for one test, back to off (the default) after."""
+    from spark_b200 import _lib
+
+    lib = _lib.load()
+    _lib.check(lib.dsv4_set_k_split(0), "dsv4_set_k_split")
+    yield
+    _lib.check(lib.dsv4_set_k_split(1), "dsv4_set_k_split")
+
+
 def _case(B, S, N, K, seed, invalid_frac=0.1, empty_query=False):
     g = torch.Generator().manual_seed(seed)
     q = torch.randn(B, S, 64, 512, generator=g).to(torch.bfloat16)
@@ -93,9 +104,17 @@ def test_sparse_attn_out_of_range_index_is_reported_and_skipped(cuda_device):
     _attn_close(out.float().cpu().numpy(), ref)
 
 
-@pytest.mark.parametrize("M,K,N", [(1, 4096, 1024), (37, 4096, 512), (5, 1024, 32768), (200, 8192, 4096),
-                                   (130, 4096, 8192)])
-def test_fp8_linear_matches_the_oracle(cuda_device, M, K, N):
+@pytest.mark.parametrize("M,K,N", [
+    (1, 4096, 1024),      # one row tile, 4 items (k split in 8 under the auto split)
+    (37, 4096, 512),
+    (64, 4096, 1024),     # decode wq_a
+    (16, 3072, 256),      # 6 scale groups (split in 2 under the auto split)
+    (5, 1024, 32768),     # enough items: never split
+    (200, 8192, 4096),
+    (130, 4096, 8192),
+])
+@pytest.mark.parametrize("k_split", [1, 0])
+def test_fp8_linear_matches_the_oracle(cuda_device, M, K, N, k_split):
     from spark_b200 import _lib
     from spark_b200.attention import FP8Linear
 
@@ -108,8 +127,13 @@ def test_fp8_linear_matches_the_oracle(cuda_device, M, K, N):
         lin.scale.view(torch.uint8).copy_(s.to(cuda_device))
     lin.refresh_scale_atoms()
     x = torch.randn(M, K, generator=g).to(torch.bfloat16)
-    y = lin(x.to(cuda_device))
-    torch.cuda.synchronize()
+    lib = _lib.load()
+    _lib.check(lib.dsv4_set_k_split(k_split), "dsv4_set_k_split")
+    try:
+        y = lin(x.to(cuda_device))
+        torch.cuda.synchronize()
+    finally:
+        _lib.check(lib.dsv4_set_k_split(1), "dsv4_set_k_split")
     _lib.raise_on_device_error()
     ref = A.fp8_linear(x.float().numpy(), w.view(torch.uint8).numpy(), s.numpy())
     assert _rel_err(y.float().cpu().numpy(), ref) <= 2e-2
@@ -138,3 +162,22 @@ def test_raw_c_abi_and_torch_op_agree_bit_for_bit(cuda_device):
         _lib.check(lib.dsv4_sparse_attn(_lib.ptr(q), _lib.ptr(kv), _lib.ptr(sink), _lib.ptr(idx), B, S, H, kv.shape[1],
                                         D, idx.shape[-1], 0.05, _lib.ptr(out), _lib.ptr(ws), max(need - 256, 0),
                                         _lib.stream_ptr()), "dsv4_sparse_attn")
+
+
+def test_split_fp8_linear_is_deterministic(cuda_device, auto_split):
+    """Under the auto split a decode-sized linear splits its k range; the
+    slices are added in slice order, so two calls give equal bytes."""
+    from spark_b200 import _lib
+    from spark_b200.attention import FP8Linear
+
+    g = torch.Generator().manual_seed(5)
+    lin = FP8Linear(4096, 1024, device=cuda_device)
+    lin.weight.data.copy_(torch.randn(1024, 4096, generator=g).to(torch.float8_e4m3fn).to(cuda_device))
+    lin.refresh_scale_atoms()
+    # the workspace holds the 8 slices' fp32 partial sums
+    assert int(_lib.load().dsv4_fp8_linear_workspace_bytes(64, 1024, 4096)) >= 8 * 64 * 1024 * 4
+    x = torch.randn(64, 4096, generator=g).to(torch.bfloat16).to(cuda_device)
+    a, b = lin(x), lin(x)
+    torch.cuda.synchronize()
+    _lib.raise_on_device_error()
+    assert torch.equal(a, b)
