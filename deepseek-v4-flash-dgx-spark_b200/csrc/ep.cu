@@ -242,18 +242,70 @@ __global__ void __launch_bounds__(kEpChunk) ep_plan_kernel(
   }
 }
 
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// The call counter in this rank's own buffer.
+__device__ __forceinline__ int* ep_counter(const uint64_t* bases, int rank) {
+  return reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bases[rank]) + kEpEpochOff);
+}
+
+// Source, one warp: tell owner d how many rows / routes arrived from this
+// rank and where their returns go, then raise disp_flag[rank] in d's buffer
+// (release, system scope).  Lane d takes destination d.  epoch <= 0: this
+// call's epoch is the own call counter plus one (stored back).  The caller has
+// made every row store visible at system scope first.
+__device__ __forceinline__ void signal_dispatch(const uint64_t* __restrict__ bases, int rank, int world,
+                                                const int* __restrict__ send_counts,
+                                                const int* __restrict__ dst_base, int epoch) {
+  const int d = threadIdx.x & 31;
+  if (epoch <= 0) {
+    int e = 0;
+    if (d == 0) {
+      int* ctr = ep_counter(bases, rank);
+      e = *ctr + 1;
+      *ctr = e;
+    }
+    epoch = __shfl_sync(0xffffffffu, e, 0);
+  }
+  if (d >= world) return;
+  uint8_t* b = reinterpret_cast<uint8_t*>(bases[d]);
+  int* info = reinterpret_cast<int*>(b + kEpInfoOff) + 4 * rank;
+  info[0] = __ldcg(send_counts + 2 * d);
+  info[1] = __ldcg(send_counts + 2 * d + 1);
+  info[2] = __ldcg(dst_base + 2 * d + 1);
+  __threadfence_system();
+  st_release_sys(reinterpret_cast<int*>(b) + rank, epoch);
+}
+
+// A source with no rows to send (one warp): the counts and offsets are zeros.
+__global__ void ep_signal_dispatch_kernel(const uint64_t* __restrict__ bases, int rank, int world,
+                                          const int* __restrict__ send_counts,
+                                          const int* __restrict__ dst_base, int epoch) {
+  signal_dispatch(bases, rank, world, send_counts, dst_base, epoch);
+}
+
 // Data: one warp per (token, group of quads) quantizes the row once and writes
-// codes + scale bytes into each of its send rows.
+// codes + scale bytes into each of its send rows.  Over peer memory the kernel
+// also publishes them: every thread fences its stores at system scope, each
+// CTA then counts itself done (pack_ctr, zeroed by the dispatch), and the CTA
+// that completes the count raises the owners' flags (signal_dispatch).
 __global__ void __launch_bounds__(256) ep_pack_kernel(const __nv_bfloat16* __restrict__ x, int T,
                                                       int H, int world, long long row_bytes,
                                                       const int* __restrict__ row_pos,
                                                       int qsplit, uint8_t* __restrict__ send,
                                                       const int* __restrict__ dst_base,
-                                                      EpPeerRows peer) {
+                                                      EpPeerRows peer, int* __restrict__ pack_ctr,
+                                                      const int* __restrict__ send_counts, int epoch) {
   const int lane = threadIdx.x & 31;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int t = gw / qsplit, part = gw % qsplit;
-  if (t >= T) return;
   const int KQ = H / 512;
   const int per = (KQ + qsplit - 1) / qsplit;
   const int q0 = part * per, q1 = min(KQ, q0 + per);
@@ -261,12 +313,11 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const __nv_bfloat16* __res
   int np = 0;
 #pragma unroll
   for (int d = 0; d < kEpMaxWorld; ++d) {
-    pos[d] = d < world ? row_pos[(size_t)t * world + d] : -1;
+    pos[d] = (t < T && d < world) ? row_pos[(size_t)t * world + d] : -1;
     np += pos[d] >= 0;
   }
-  if (np == 0) return;
-  const __nv_bfloat16* xrow = x + (size_t)t * H;
-  for (int q = q0; q < q1; q += 2) {
+  const __nv_bfloat16* xrow = x + (size_t)(t < T ? t : 0) * H;
+  for (int q = q0; np > 0 && q < q1; q += 2) {
     uint4 raw[2][2];
 #pragma unroll
     for (int g = 0; g < 2; ++g) {
@@ -294,6 +345,15 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const __nv_bfloat16* __res
       }
     }
   }
+  if (!peer.bases) return;  // host exchange: nothing to publish
+  __shared__ int s_last;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(pack_ctr, 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence_system();  // every CTA's rows (and the plan kernel's row tails) before the flags
+  if (threadIdx.x < 32) signal_dispatch(peer.bases, peer.rank, world, send_counts, dst_base, epoch);
 }
 
 // Receiver: routing of the T_own + R local rows.  Rows t < T_own are this
@@ -366,47 +426,6 @@ __global__ void __launch_bounds__(256) ep_return_gather_kernel(
 // ---------------------------------------------------------------------------
 // peer-memory exchange: signals, bounded waits, unpack and return over NVLink
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void st_release_sys(int* p, int v) {
-  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ int ld_acquire_sys(const int* p) {
-  int v;
-  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// The call counter in this rank's own buffer.
-__device__ __forceinline__ int* ep_counter(const uint64_t* bases, int rank) {
-  return reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bases[rank]) + kEpEpochOff);
-}
-
-// Source: after its rows are in every owner's buffer (previous launch), tell
-// owner d how many rows / routes arrived and where their returns go, then
-// raise disp_flag[rank] there.  One lane per destination.  epoch <= 0: this
-// call's epoch is the own call counter plus one (stored back).
-__global__ void ep_signal_dispatch_kernel(const uint64_t* __restrict__ bases, int rank, int world,
-                                          const int* __restrict__ send_counts,
-                                          const int* __restrict__ dst_base, int epoch) {
-  const int d = threadIdx.x;
-  if (epoch <= 0) {
-    int e = 0;
-    if (d == 0) {
-      int* ctr = ep_counter(bases, rank);
-      e = *ctr + 1;
-      *ctr = e;
-    }
-    epoch = __shfl_sync(0xffffffffu, e, 0);
-  }
-  if (d >= world) return;
-  uint8_t* b = reinterpret_cast<uint8_t*>(bases[d]);
-  int* info = reinterpret_cast<int*>(b + kEpInfoOff) + 4 * rank;
-  info[0] = send_counts[2 * d];
-  info[1] = send_counts[2 * d + 1];
-  info[2] = dst_base[2 * d + 1];
-  __threadfence_system();
-  st_release_sys(reinterpret_cast<int*>(b) + rank, epoch);
-}
-
 // Owner: every route row is in its source's return region (previous launch);
 // raise ret_flag[rank] in every rank's buffer.
 __global__ void ep_signal_return_kernel(const uint64_t* __restrict__ bases, int rank, int world,
@@ -551,12 +570,10 @@ int launch_ep_dispatch(const void* x, const int64_t* indices, const float* weigh
   int qsplit = (int)((8LL * num_sms * 8 + T - 1) / T);  // about 8 warps per SM slot
   qsplit = qsplit < 1 ? 1 : (qsplit > KQ ? KQ : qsplit);
   const long long warps = (long long)T * qsplit;
+  // over peer memory the pack kernel's last CTA also raises the owners' flags
   launch_k(ep_pack_kernel, (unsigned)((warps + 7) / 8), 256, 0, st,
            static_cast<const __nv_bfloat16*>(x), T, H, world, rb, row_pos, qsplit, send,
-           (const int*)dst_base, peer);
-  if (peer_bases)
-    launch_k(ep_signal_dispatch_kernel, 1, 32, 0, st, peer_bases, rank, world,
-             (const int*)send_counts, (const int*)dst_base, epoch);
+           (const int*)dst_base, peer, ctrl + 2, (const int*)send_counts, epoch);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
 

@@ -21,6 +21,7 @@ goes through libdsv4moe.so; nothing here computes on the CPU.
 from __future__ import annotations
 
 import ctypes
+import os
 from dataclasses import dataclass
 
 import torch
@@ -59,6 +60,12 @@ class ModelArgs:
 # ---------------------------------------------------------------------------
 # packed expert block (scripts/build_packed_expert_layout.py:76-86)
 # ---------------------------------------------------------------------------
+# MoE.forward replays a captured CUDA graph per token count up to this many
+# tokens (decode batches); DSV4_CUDA_GRAPHS=0 keeps every call eager.
+GRAPH_MAX_TOKENS = 1024
+GRAPH_MAX_ENTRIES = 8
+_GRAPHS_ON = os.environ.get("DSV4_CUDA_GRAPHS", "1") != "0"
+
 PACKED_ORDER = ("w1.scale", "w2.scale", "w3.scale", "w1.weight", "w2.weight", "w3.weight")
 
 
@@ -415,6 +422,7 @@ class MoE(nn.Module):
         from .ep import PeerExchange
 
         old = getattr(self, "peer_exchange", None)
+        self.reset_graphs()
         if old is not None:
             old.close()
         self.peer_exchange = PeerExchange(self, cap_tokens, group=self.group)
@@ -487,10 +495,81 @@ class MoE(nn.Module):
                                tokens=x2.shape[0])
         else:
             tel.count_routing(x2.shape[0], x2.shape[0] * self.n_activated_experts)
-        if self.world == 1:
+        if self._graph_ok(x2, routing, tel):
+            y = self._graph_forward(x2)
+        elif self.world == 1:
             y = self.forward_tokens(x2, routing=routing)
         else:
             from .ep import ep_moe_forward
 
             y = ep_moe_forward(self, x2, routing=routing)
         return y.type_as(x).view(shape)
+
+    # ------------------------------------------------------------ graphs
+    def _graph_ok(self, x2, routing, tel) -> bool:
+        """Graph replay applies to decode-sized calls whose routing the layer
+        computes itself, with no route trace, on one rank or over peer memory
+        (the host-collective exchange needs the host between its steps), and
+        not while the caller is capturing a graph of its own."""
+        return (_GRAPHS_ON and routing is None and tel.route_trace_path is None
+                and 0 < x2.shape[0] <= GRAPH_MAX_TOKENS
+                and (self.world == 1 or getattr(self, "peer_exchange", None) is not None)
+                and not torch.cuda.is_current_stream_capturing())
+
+    def _graph_key(self) -> tuple:
+        """Every address a captured layer holds: a change of any recaptures."""
+        sh = self.shared_experts
+        ex = getattr(self, "peer_exchange", None)
+        return (self.gate.weight.data_ptr(), ptr(self.gate.bias), self.arena.buffer.data_ptr(),
+                self.arena.sf.data_ptr(), self.expert_slot.data_ptr(), sh.w1.weight.data_ptr(),
+                sh.w2.weight.data_ptr(), sh.w3.weight.data_ptr(), sh.scale_atoms.data_ptr(),
+                ex.buf.value if ex is not None else 0)
+
+    def _graph_body(self, x2: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return self.forward_tokens(x2)
+        from .ep import ep_forward_peer
+
+        return ep_forward_peer(self.peer_exchange, x2)
+
+    def _graph_forward(self, x2: torch.Tensor) -> torch.Tensor:
+        """The layer as a replayed CUDA graph, one per token count.  A new
+        token count is captured (nothing runs while capturing) and then
+        replayed, so every call, the first included, is exactly one layer
+        call: expert-parallel ranks stay in step whatever their own counts.
+        Under expert parallelism the exchange's poisoning check and error-word
+        copy run on the host around each replay, as around an eager call."""
+        graphs = self.__dict__.setdefault("_graphs", {})
+        T = x2.shape[0]
+        key = self._graph_key()
+        entry = graphs.get(T)
+        if entry is not None and entry[3] != key:
+            del graphs[T]
+            entry = None
+        ex = getattr(self, "peer_exchange", None) if self.world > 1 else None
+        if ex is not None:
+            ex.check_poisoned()
+        if entry is None:
+            while len(graphs) >= GRAPH_MAX_ENTRIES:
+                graphs.pop(next(iter(graphs)))
+            if ex is not None:
+                ex.workspace(T)  # sized outside the capture, shared with eager calls
+            static_x = x2.clone()
+            graph = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream(device=x2.device)
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.graph(graph, stream=side):
+                static_y = self._graph_body(static_x)
+            torch.cuda.current_stream().wait_stream(side)
+            entry = (graph, static_x, static_y, key)
+            graphs[T] = entry
+        else:
+            entry[1].copy_(x2)
+        entry[0].replay()
+        if ex is not None:
+            ex.note_call_end()
+        return entry[2].clone()
+
+    def reset_graphs(self) -> None:
+        """Drop the captured graphs (they are recaptured on the next calls)."""
+        self.__dict__.pop("_graphs", None)

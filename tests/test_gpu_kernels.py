@@ -339,6 +339,35 @@ def test_moe_module_forward_shape_and_dtype(cuda_device):
     assert w.shape == (6, cfg.topk) and idx.dtype == torch.int64
 
 
+def test_module_forward_graph_replay_equals_the_eager_layer(cuda_device):
+    """MoE.forward replays a captured graph per token count: every call,
+    the capturing one included, equals the eager C ABI layer bit for bit; a
+    second token count gets its own graph; a replaced weight tensor (a new
+    address) is recaptured."""
+    from spark_b200 import _lib
+    from spark_b200.synthetic import CONFIGS, build_moe, make_layer
+
+    cfg = CONFIGS["decode"].with_tokens(64)
+    layer = make_layer(cfg, seed=11, device="cpu")
+    moe = build_moe(layer, device=cuda_device)
+    g = torch.Generator().manual_seed(12)
+    for T in (64, 64, 7, 64, 7):
+        x = (torch.randn(T, cfg.dim, generator=g) * 0.5).to(torch.bfloat16).to(cuda_device)
+        y = moe(x.view(1, T, cfg.dim)).view(T, cfg.dim)
+        ref = moe.forward_tokens(x)
+        torch.cuda.synchronize()
+        assert torch.equal(y, ref), T
+    assert sorted(moe._graphs) == [7, 64]
+    first = moe._graphs[64][0]
+    with torch.no_grad():
+        moe.gate.weight = torch.nn.Parameter(moe.gate.weight.detach().clone() * 0.5, requires_grad=False)
+    x = (torch.randn(64, cfg.dim, generator=g) * 0.5).to(torch.bfloat16).to(cuda_device)
+    y = moe(x.view(1, 64, cfg.dim)).view(64, cfg.dim)
+    assert moe._graphs[64][0] is not first
+    assert torch.equal(y, moe.forward_tokens(x))
+    _lib.raise_on_device_error()
+
+
 def test_prefill_layer_full_size_routing_and_sampled_rows(cuda_device):
     """T=8192 with the Zipf(1.2)-tilted gate: routing checked on every token
     (bit-exact on the device's logits, counts = bincount), outputs checked on a
