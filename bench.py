@@ -892,6 +892,7 @@ def _sweep(args, local):
         out[f"{wl}_T{T}"] = entry
         del moe, layer, ws, y
         torch.cuda.empty_cache()
+    out["prefill_T8192_fp4act"] = _prefill_fp4(args, dev, flush)
     out.update(_materializer(args, dev, flush))
     out["upload_32_experts"] = _upload_rate(args, dev)
     out["attention"] = _attention(args, dev, flush)
@@ -1012,6 +1013,95 @@ def _prefill_roofline(moe, layer, ws, y, flush, cfg, T):
             "peak_fp4": round(4 * bf16, 1), "frac_fp4": round(achieved / (4 * bf16), 4),
             "kernel": "expert_gemm_kernel (GEMM1 + GEMM2), kind::mxf8f6f4 (e4m3 x e2m1, FP8 rate)",
             "peak_source": f"{src} bf16 x2 (FP8) / x4 (FP4), nominal dense ratios"}
+
+
+def _prefill_fp4(args, dev, flush, T=8192, sample=16):
+    """The prefill layer in the opt-in FP4-activation mode
+    (dsv4_set_fp4_activations): the routed experts' w1 | w3 as kind::mxf4
+    products on FP4 activations, everything else as in the default layer.
+    Time: the graph-replayed layer (median of 10, L2 flushed between), and the
+    expert GEMMs' stage time against their mixed roofline (routed w1 | w3
+    FLOPs at the FP4 rate, shared w1 | w3 and every w2 at the FP8 rate, both
+    scaled from the measured bf16 peak).  Outside the timings: the first
+    `sample` tokens against the oracle run in the same mode (the bar) and
+    against the default e4m3 oracle (how far the mode moves the layer)."""
+    import numpy as np
+    import torch
+
+    from oracle import moe_oracle as O
+    from spark_b200 import _lib
+    from spark_b200.synthetic import CONFIGS, build_moe, make_layer
+
+    lib = _lib.load()
+    _lib.check(lib.dsv4_set_fp4_activations(1), "dsv4_set_fp4_activations")
+    try:
+        cfg = CONFIGS["prefill"].with_tokens(T)
+        layer = make_layer(cfg, seed=args.seed + 7, device=dev)
+        moe = build_moe(layer, device=dev)
+        d = moe.layer_desc()
+        offs = (ctypes.c_longlong * 21)()
+        _lib.check(lib.dsv4_moe_workspace_layout(ctypes.byref(d), T, offs, 21), "dsv4_moe_workspace_layout")
+        if offs[20] != 1:
+            return {"error": "the FP4-activation mode is not in force for this layout"}
+        ws = torch.empty(moe.workspace_bytes(T), dtype=torch.uint8, device=dev)
+        y = torch.empty_like(layer["x"])
+        ms = _graph_ms(lambda: moe.forward_tokens(layer["x"], workspace=ws, out=y), flush)
+        # stage times of the expert GEMMs (library events on the launching stream)
+        lib.dsv4_profile_enable(1)
+        buf = (ctypes.c_float * 6)()
+        gemm = []
+        for _ in range(5):
+            flush.fill_(1)
+            moe.forward_tokens(layer["x"], workspace=ws, out=y)
+            torch.cuda.synchronize()
+            lib.dsv4_profile_read(buf, 6)
+            gemm.append(buf[3] + buf[4])
+        lib.dsv4_profile_enable(0)
+        gemm_ms = statistics.median(gemm)
+        _lib.raise_on_device_error()
+        k, H, I = cfg.topk, cfg.dim, cfg.inter
+        w_dev = ws[offs[1]:offs[1] + T * k * 4].view(torch.float32).view(T, k)
+        i_dev = ws[offs[2]:offs[2] + T * k * 8].view(torch.int64).view(T, k)
+        routes = int((i_dev >= 0).sum())
+        f_fp4 = 2.0 * routes * 2 * H * I               # routed w1 | w3
+        f_fp8 = 2.0 * T * 2 * H * I + 2.0 * (routes + T) * H * I   # shared w1 | w3, every w2
+        peaks, src = _peaks()
+        bf16 = peaks.get("bf16_tflops", 1590.0)
+        ideal_ms = (f_fp4 / (4 * bf16 * 1e12) + f_fp8 / (2 * bf16 * 1e12)) * 1e3
+        # parity on sampled tokens, outside the timings
+        xs, ys = layer["x"][:sample], y[:sample]
+        ws_, is_ = w_dev[:sample].cpu().numpy(), i_dev[:sample].cpu().numpy()
+        experts = sorted(set(int(e) for e in is_.reshape(-1).tolist()))
+        mw = O.MoEWeights(
+            gate_w=None, gate_bias=None,
+            experts={e: O.expert_from_block(layer["blocks"][e].cpu().numpy(), H, I) for e in experts},
+            shared=O.shared_from_tensors({kk: v.cpu().numpy() for kk, v in layer["shared"].items()}),
+            topk=k, route_scale=cfg.route_scale, swiglu_limit=cfg.swiglu_limit)
+        xn, yn = xs.float().cpu().numpy(), ys.float().cpu().numpy().astype(np.float64)
+        workers = min(16, os.cpu_count() or 1)
+        r4 = O.moe_forward(xn, mw, routing=(ws_, is_), workers=workers, fp4_act=True)[0].astype(np.float64)
+        r8 = O.moe_forward(xn, mw, routing=(ws_, is_), workers=workers)[0].astype(np.float64)
+
+        def rel(a, b, rms=False):
+            den = np.sqrt(np.mean(b ** 2)) + 1e-30
+            return float((np.sqrt(np.mean((a - b) ** 2)) if rms else np.max(np.abs(a - b))) / den)
+
+        return {
+            "tokens": T, "ms": round(ms, 4), "tokens_per_s": round(T / (ms * 1e-3), 1), "cuda_graph": True,
+            "gemm_ms": round(gemm_ms, 4),
+            "roofline": {"bound": "tensor", "algorithmic_flops_fp4": f_fp4, "algorithmic_flops_fp8": f_fp8,
+                         "achieved": round((f_fp4 + f_fp8) / (gemm_ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
+                         "ideal_ms": round(ideal_ms, 4), "frac": round(ideal_ms / gemm_ms, 4),
+                         "peak_source": f"{src} bf16 {bf16} x4 (FP4) / x2 (FP8), nominal dense ratios"},
+            "parity": {"checked_tokens": sample, "max_err_vs_fp4_oracle": round(rel(yn, r4), 6), "tol": 2e-2,
+                       "ok": bool(rel(yn, r4) <= 2e-2),
+                       "deviation_from_e4m3_layer": {"max_of_rms": round(rel(yn, r8), 4),
+                                                     "rms_of_rms": round(rel(yn, r8, rms=True), 4)}},
+            "numerics": "routed w1 | w3 on fp4_act_quant(x, 32) activations (e2m1, per-32 ue8m0); "
+                        "the reference's layer uses act_quant(x, 128) e4m3"}
+    finally:
+        _lib.check(lib.dsv4_set_fp4_activations(0), "dsv4_set_fp4_activations")
+        torch.cuda.empty_cache()
 
 
 def _materializer(args, dev, flush):

@@ -111,7 +111,8 @@ struct Plan {
   int T, E, k, H, I, S, block_n, max_rows, max_tiles;
   int split1, split2;  // split-K slices of GEMM1 / GEMM2 (1 = none)
   int part_rows;       // compact rows of the split-K partial sums
-  long long off[21];
+  bool fp4;            // routed GEMM1 on FP4 activations (dsv4_set_fp4_activations)
+  long long off[23];
   long long total;
 };
 
@@ -151,6 +152,20 @@ static int k_split_setting() {
   if (v < 0) {
     v = env_int("DSV4_KSPLIT", 1, 0, 64);
     g_k_split_setting.store(v, std::memory_order_relaxed);
+  }
+  return v;
+}
+
+// FP4 activations for the routed experts' GEMM1 (opt-in: 0 = off, the
+// default, matching the reference's e4m3 act_quant; 1 = on).  From
+// DSV4_FP4_ACT on first use, or dsv4_set_fp4_activations.
+static std::atomic<int> g_fp4_act_setting{-1};
+
+static int fp4_act_setting() {
+  int v = g_fp4_act_setting.load(std::memory_order_relaxed);
+  if (v < 0) {
+    v = env_int("DSV4_FP4_ACT", 0, 0, 1);
+    g_fp4_act_setting.store(v, std::memory_order_relaxed);
   }
   return v;
 }
@@ -216,9 +231,12 @@ static Plan make_plan(const dsv4_moe_layer* L, int T, int E_local = -1) {
   p.split1 = choose_k_split(T, p.k, p.E, p.block_n, nb1, p.H / 128, nsm);
   p.split2 = choose_k_split(T, p.k, p.E, p.block_n, nb2, p.I / 128, nsm);
   p.part_rows = T * p.k + T * p.S;
+  // single-GPU layer only; the CTA-pair form and split-K keep e4m3 activations
+  p.fp4 = E_local < 0 && L->arena != nullptr && fp4_act_setting() == 1 && p.block_n != 256 && p.H % 256 == 0;
+  if (p.fp4) p.split1 = 1;
   const int smax = p.split1 > p.split2 ? p.split1 : p.split2;
   const long long part_ld = (long long)(nb1 * 256 > nb2 * 256 ? nb1 * 256 : nb2 * 256);
-  long long sz[21] = {
+  long long sz[23] = {
       (long long)T * (p.E > p.k ? p.E : p.k) * 4,  // logits (expert parallel: return rows)
       (long long)T * p.k * 4,                 // weights
       (long long)T * p.k * 8,                 // indices
@@ -242,9 +260,11 @@ static Plan make_plan(const dsv4_moe_layer* L, int T, int E_local = -1) {
       16,                                     // plan control words
       smax > 1 ? (long long)smax * p.part_rows * part_ld * 4 : 0,  // split-K partial sums
       smax > 1 ? (long long)p.max_tiles * (nb1 + nb2) * 4 : 0,     // split-K item counters
+      p.fp4 ? (long long)p.max_rows * (p.H / 2) : 0,                // FP4 activation codes
+      p.fp4 ? atom_groups * (p.H / 128) * 512 : 0,                  // their per-32 scale atoms
   };
   long long o = 0;
-  for (int i = 0; i < 21; ++i) {
+  for (int i = 0; i < 23; ++i) {
     p.off[i] = o;
     o += align256(sz[i]);
   }
@@ -301,7 +321,8 @@ static int run_expert_gemms(const dsv4_moe_layer* L, const int4* tiles, const in
                             const float* slot_weight, const uint8_t* xq, const uint8_t* xsf,
                             uint8_t* hq, uint8_t* hsf, __nv_bfloat16* out_bf16, int out_ld,
                             int max_rows, int max_tiles, int block_n, const int* expert_slot,
-                            int n_routed, int nsm, cudaStream_t st, const SplitK& sk = SplitK()) {
+                            int n_routed, int nsm, cudaStream_t st, const SplitK& sk = SplitK(),
+                            const uint8_t* xq4 = nullptr, const uint8_t* xsf4 = nullptr) {
   const int H = L->hidden, I = L->inter;
   const bool has_shared = L->shared_w1 != nullptr;
   const bool has_routed = L->arena != nullptr;
@@ -374,6 +395,30 @@ static int run_expert_gemms(const dsv4_moe_layer* L, const int4* tiles, const in
     if (work < clusters) clusters = (int)(work > 0 ? work : 1);
     if ((rc = launch_expert_gemm_pair(true, pm, g1, 0, sc >> 8, 0, sc >> 8, clusters, st)))
       return rc;
+  } else if (xq4 && has_routed) {
+    // FP4 activations: the routed items on kind::mxf4 (packed w1 / w3 maps,
+    // 256-wide k tiles, per-32 activation atoms), then the shared expert's
+    // items on the e4m3 kernel
+    CUtensorMap p0, p1, bx;
+    if ((rc = make_tmap_fp4_packed_arena(&p0, L->arena + w1_off, H, I, L->n_slots, L->slot_stride, gemm_l2promo())))
+      return rc;
+    if ((rc = make_tmap_fp4_packed_arena(&p1, L->arena + w3_off, H, I, L->n_slots, L->slot_stride, gemm_l2promo())))
+      return rc;
+    if ((rc = make_tmap_u8(&bx, xq4, H / 2, max_rows, block_n))) return rc;
+    GemmArgs g4 = g1;
+    g4.kt_count = H / 256;
+    g4.sfb = xsf4;
+    g4.k_split = 1;
+    g4.seg_filter = 1;
+    const long long work1 = (long long)max_tiles * g1.nb_count;
+    const int grid1 = (int)(work1 < nsm ? work1 : nsm);
+    if ((rc = launch_expert_gemm_fp4(block_n, p0, p1, bx, g4, grid1, st))) return rc;
+    if (has_shared) {
+      GemmArgs gs = g1;
+      gs.k_split = 1;
+      gs.seg_filter = 2;
+      if ((rc = launch_expert_gemm(true, block_n, a0, a1, s0, s1, b, gs, grid1, st))) return rc;
+    }
   } else {
     const long long work1 = (long long)max_tiles * g1.nb_count * g1.k_split;
     const int grid1 = (int)(work1 < nsm ? work1 : nsm);
@@ -469,6 +514,21 @@ extern "C" {
 
 int dsv4_version(void) { return 1; }
 
+int dsv4_set_fp4_activations(int on) {
+  if (on != 0 && on != 1) return DSV4_ERR_ARG;
+  g_fp4_act_setting.store(on, std::memory_order_relaxed);
+  return DSV4_OK;
+}
+
+int dsv4_fp4_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* s, void* stream) {
+  if (M < 0 || K <= 0 || K % 32) return DSV4_ERR_ARG;
+  if (M == 0) return DSV4_OK;
+  if (!x || !q || !s || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(q) & 15))
+    return DSV4_ERR_ARG;
+  bind_device(q);
+  return launch_fp4_act_quant(x, M, K, q, s, num_sms(), static_cast<cudaStream_t>(stream));
+}
+
 int dsv4_set_k_split(int slices) {
   if (slices < 0 || slices > 64) return DSV4_ERR_ARG;
   g_k_split_setting.store(slices, std::memory_order_relaxed);
@@ -559,6 +619,7 @@ int dsv4_moe_workspace_layout(const dsv4_moe_layer* L, int T, long long* out, in
     out[18] = p.split1;
     out[19] = p.split2;
   }
+  if (n_out > 20) out[20] = p.fp4 ? 1 : 0;
   return DSV4_OK;
 }
 
@@ -685,10 +746,15 @@ int dsv4_moe_forward(const dsv4_moe_layer* L, const void* x, int T, void* y,
                                  chunk_base, ctrl, route_slot, slot_token, slot_weight, xq, xsf,
                                  nsm, st)))
     return rc;
+  uint8_t* xq4 = p.fp4 ? ws + p.off[21] : nullptr;
+  uint8_t* xsf4 = p.fp4 ? ws + p.off[22] : nullptr;
+  if (p.fp4 && (rc = launch_fp4_permute_quant(x, T, H, slot_token, seg_start + (E + p.S), p.max_rows, xq4,
+                                              xsf4, nsm, st)))
+    return rc;
   stage_mark(3, st);
 
   if ((rc = run_expert_gemms(L, tiles, n_tiles, slot_weight, xq, xsf, hq, hsf, O, H, p.max_rows,
-                             p.max_tiles, p.block_n, L->expert_slot, L->n_routed, nsm, st, sk)))
+                             p.max_tiles, p.block_n, L->expert_slot, L->n_routed, nsm, st, sk, xq4, xsf4)))
     return rc;
   rc = launch_combine(O, H, route_slot, ri, T, k, p.S ? seg_start + E : nullptr, y, st);
   stage_mark(6, st);

@@ -8,6 +8,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp4.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -290,6 +291,29 @@ __device__ __forceinline__ void tc_mma_mxf8f6f4(uint32_t d_tmem, uint64_t adesc,
       : "memory");
 }
 
+// D(tmem) (+)= A(smem) x B(smem)^T, both e2m1 packed two per byte (K = 64 per
+// instruction, 32 bytes of each row), two ue8m0 scales per row per instruction
+// (scale_vec::2X: the scale-factor id 0 or 2 picks bytes {id, id+1} of the
+// 32-bit TMEM word, the first for k 0..31 of the instruction).
+__device__ __forceinline__ void tc_mma_mxf4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.scale_vec::2X [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::
+          "r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// Instruction descriptor for kind::mxf4: A and B e2m1 (format 1 in this kind),
+// K-major, fp32 accumulate, ue8m0 scales (bit 23), dense K = 64 (bit 31 = 0),
+// M = 128; sf ids 0 or 2 (bits 29-30 for A, 4-5 for B).
+__host__ __device__ constexpr uint32_t idesc_mxf4(uint32_t n, uint32_t a_sf_id, uint32_t b_sf_id) {
+  return (b_sf_id << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | (1u << 23) | ((128u >> 4) << 24) |
+         (a_sf_id << 29);
+}
+
 // D(tmem) (+)= A(smem) x B(smem)^T, bf16 inputs, fp32 accumulate.
 __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                            uint32_t idesc, uint32_t accumulate) {
@@ -494,6 +518,46 @@ __device__ __forceinline__ int act_scale_exp(float amax) {
 
 __device__ __forceinline__ float exp2i(int e) {  // exact 2^e for e in [-126, 127]
   return __int_as_float((e + 127) << 23);
+}
+
+// FP4 activations (the official fp4_act_quant(x, 32)): per block of 32 values
+// amax = max(|x|, 1e-4), s = 2^ceil(log2(amax * fp32(1/6))), codes =
+// e2m1(x / s) rounded to nearest even and saturated (cvt.rn.satfinite), two
+// per byte with element 2i in the low nibble.  Returns s's exponent; `packed`
+// gets the 16 code bytes of the 32 values v (already in fp32).
+__device__ __forceinline__ int fp4_block_quant(const float (&v)[32], uint4& packed) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  amax = fmaxf(amax, 1e-4f);
+  const int e = ceil_log2_exact(__fmul_rn(amax, 1.0f / 6.0f));
+  const float inv = exp2i(-e);
+  uint32_t w[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int i = 8 * j + 2 * b;
+      const uint32_t byte = __nv_cvt_float2_to_fp4x2(make_float2(v[i] * inv, v[i + 1] * inv), __NV_E2M1,
+                                                     cudaRoundNearest);
+      word |= (byte & 0xFFu) << (8 * b);
+    }
+    w[j] = word;
+  }
+  packed = make_uint4(w[0], w[1], w[2], w[3]);
+  return e;
+}
+
+// 32 bf16 values (64 bytes, 16-byte aligned) -> fp32
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 r = *reinterpret_cast<const uint4*>(src + 8 * q);
+    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&r);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[8 * q + i] = __bfloat162float(b[i]);
+  }
 }
 
 }  // namespace dsv4

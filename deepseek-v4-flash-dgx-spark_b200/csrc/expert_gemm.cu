@@ -36,32 +36,41 @@ __host__ __device__ constexpr int pow2_at_least(int v) {
   return p;
 }
 
-template <int BM, bool GATED>
+// FP4A: GEMM1 on FP4 activations (kind::mxf4).  A k tile is then 256 values,
+// still 128 bytes per row for both operands (two e2m1 codes per byte), and
+// each stage carries its own scale atoms: two 128-wide windows of the
+// activation atoms and of each weight half (3 KB).
+template <int BM, bool GATED, bool FP4A = false>
 struct GemmCfg {
-  static constexpr int A_BYTES = BM * 128;       // activation rows of one 128-wide k tile
+  static constexpr int A_BYTES = BM * 128;       // activation rows of one k tile
   static constexpr int B_HALF = 128 * 128;       // one 128-row weight box in smem
   static constexpr int B_BYTES = 2 * B_HALF;     // N = 256 weight rows
   static constexpr int TILE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int SF_STAGE = FP4A ? 3 * 1024 : 0;
   // scale atoms of a group of four k tiles, loaded with the group's first
   // tile into one of two ring slots: [act 512][weight half 0: 4 x 512][half 1: 4 x 512].
   // A slot is refilled 8 k tiles after its last use, which the producer's
   // stage wait already covers while STAGES <= 8.
   static constexpr int SF_GROUP = 512 + 2 * 2048;
-  static constexpr int SF_RING = 2 * SF_GROUP;
-  static constexpr int STAGE_BYTES = TILE_BYTES;
+  static constexpr int SF_RING = FP4A ? 0 : 2 * SF_GROUP;
+  static constexpr int STAGE_BYTES = TILE_BYTES + SF_STAGE;
   static constexpr int CTRL_BYTES = 256;
   // the whole 227 KB a CTA may hold: decode is bound by the weight bytes in
   // flight per SM, and an e2m1 box takes twice its global bytes in smem
   static constexpr int SMEM_MAX = 232448;
   static constexpr int STAGES0 = (SMEM_MAX - 1024 - CTRL_BYTES - SF_RING) / STAGE_BYTES;
+  static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte alignment");
   static constexpr int STAGES = STAGES0 > 8 ? 8 : STAGES0;
   static constexpr int ACC_COLS = 256;
   // TMEM scale columns, two sets used by alternate k-tile groups: activation
-  // scales 4 columns, weight scales 4 k tiles x 8 columns (256 rows)
+  // scales 4 columns, weight scales 4 k tiles x 8 columns (256 rows).  FP4A:
+  // two sets used by alternate k tiles, each activation 2 windows x 4 columns
+  // then weights 2 windows x 8 columns (24 columns from SFA_COL + 24 * set).
   static constexpr int SFA_COL = 256;
   static constexpr int SFB_COL = 264;
   static constexpr int TMEM_COLS = 512;
   static constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + SF_RING + CTRL_BYTES;
+  static_assert(!FP4A || GATED, "FP4 activations are GEMM1's");
   static_assert(A_BYTES % 1024 == 0, "tiles must keep 1024-byte alignment");
   // the M = 128 MMA reads 128 rows (16 KB) from the A base; they must stay in the stage
   static_assert(128 * 128 <= TILE_BYTES, "A window leaves the stage");
@@ -99,8 +108,10 @@ struct ItemInfo {
   const uint8_t* sfb1;
 };
 
+// KW: 128-wide k windows of a weight row block's scale atoms (= the k tiles of
+// the e4m3-activation kernel, twice them with FP4 activations).
 template <bool GATED>
-__device__ __forceinline__ ItemInfo decode_item(const GemmArgs& a, int w, int NB, int KT) {
+__device__ __forceinline__ ItemInfo decode_item(const GemmArgs& a, int w, int NB, int KW) {
   ItemInfo it;
   const int4 tl = a.tiles[w / NB];
   it.jb = w % NB;
@@ -112,13 +123,13 @@ __device__ __forceinline__ ItemInfo decode_item(const GemmArgs& a, int w, int NB
   const uint8_t* s1 = it.shared ? a.sf_shared1 : base + a.sf_off1;
   if (GATED) {  // w1 rows jb*128.. on top of the same w3 rows
     it.r0 = it.r1 = it.jb * 128;
-    it.sfb0 = s0 + (size_t)it.jb * KT * 512;
-    it.sfb1 = s1 + (size_t)it.jb * KT * 512;
+    it.sfb0 = s0 + (size_t)it.jb * KW * 512;
+    it.sfb1 = s1 + (size_t)it.jb * KW * 512;
   } else {      // 256 consecutive w2 rows
     it.r0 = it.jb * 256;
     it.r1 = it.r0 + 128;
-    it.sfb0 = s0 + (size_t)(2 * it.jb) * KT * 512;
-    it.sfb1 = s0 + (size_t)(2 * it.jb + 1) * KT * 512;
+    it.sfb0 = s0 + (size_t)(2 * it.jb) * KW * 512;
+    it.sfb1 = s0 + (size_t)(2 * it.jb + 1) * KW * 512;
   }
   return it;
 }
@@ -126,7 +137,12 @@ __device__ __forceinline__ ItemInfo decode_item(const GemmArgs& a, int w, int NB
 // TMA producer of the grouped expert GEMMs (one elected thread): per work
 // item and 128-wide k tile, the activation box, the two 128-row weight boxes
 // and, on the first k tile of each group of four, the group's scale atoms.
-template <class C, bool GATED>
+// True when an item of tile `shared` is outside args.seg_filter's segments.
+__device__ __forceinline__ bool filtered_out(const GemmArgs& a, bool shared) {
+  return a.seg_filter != 0 && shared != (a.seg_filter == 2);
+}
+
+template <class C, bool GATED, bool FP4A = false>
 __device__ __forceinline__ void gemm_produce(const CUtensorMap* tmW0p, const CUtensorMap* tmW1p,
                                              const CUtensorMap* tmS0p, const CUtensorMap* tmS1p,
                                              const CUtensorMap* tmXp, const GemmArgs& args,
@@ -137,14 +153,19 @@ __device__ __forceinline__ void gemm_produce(const CUtensorMap* tmW0p, const CUt
   uint32_t phase = 0;
   int sf_slot = 1;  // ring slot of the current k-tile group (flips at each group)
   const int S = args.k_split, KTS = KT / S;  // k-range slices per item, k tiles per slice
+  const int KW = FP4A ? 2 * KT : KT;         // 128-wide scale windows per row block
   ItemInfo cur, nxt;
-  if ((int)blockIdx.x < total) cur = decode_item<GATED>(args, blockIdx.x / S, NB, KT);
+  if ((int)blockIdx.x < total) cur = decode_item<GATED>(args, blockIdx.x / S, NB, KW);
   // work units are (item, slice); slices start on a group of four k tiles, so
   // the scale-atom ring flips at the same k tiles as without a split
   for (int w = blockIdx.x; w < total && !*abort_flag; w += step) {
     // the next unit's descriptor loads are issued now and used one unit
     // later, so their latency hides behind this unit's k loop
-    if (w + step < total) nxt = decode_item<GATED>(args, (w + step) / S, NB, KT);
+    if (w + step < total) nxt = decode_item<GATED>(args, (w + step) / S, NB, KW);
+    if (filtered_out(args, cur.shared)) {
+      cur = nxt;
+      continue;
+    }
     const size_t g0 = (size_t)(cur.row0 >> 5);
     // transaction bytes count what the TMA reads from global memory: an e2m1
     // box is 8 KB there even though it spreads to 16 KB (16U4_ALIGN16B) in smem
@@ -155,7 +176,26 @@ __device__ __forceinline__ void gemm_produce(const CUtensorMap* tmW0p, const CUt
         *abort_flag = 1;
         break;
       }
-      uint8_t* st = tile_base + (size_t)stage * C::TILE_BYTES;
+      uint8_t* st = tile_base + (size_t)stage * C::STAGE_BYTES;
+      if constexpr (FP4A) {
+        // packed boxes are as many bytes in global memory as in smem; the
+        // stage's scale atoms: activation windows 2kt, 2kt+1, then each
+        // weight half's
+        mbar_arrive_expect_tx(&full[stage], C::A_BYTES + 2u * C::B_HALF + 3072u);
+        tma_load_2d(st, tmXp, &full[stage], kt * 128, cur.row0);
+        uint8_t* b = st + C::A_BYTES;
+        tma_load_3d(b, tmW0p, &full[stage], kt * 128, cur.r0, cur.slot);
+        tma_load_3d(b + C::B_HALF, tmW1p, &full[stage], kt * 128, cur.r1, cur.slot);
+        uint8_t* sfs = st + C::TILE_BYTES;
+        bulk_load(sfs, args.sfb + (g0 * KW + 2 * kt) * 512, 1024, &full[stage]);
+        bulk_load(sfs + 1024, cur.sfb0 + (size_t)(2 * kt) * 512, 1024, &full[stage]);
+        bulk_load(sfs + 2048, cur.sfb1 + (size_t)(2 * kt) * 512, 1024, &full[stage]);
+        if (++stage == C::STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+        continue;
+      }
       // the first k tile of each group of four carries the group's scale atoms
       const bool sf_tile = (kt & 3) == 0;
       if (sf_tile) sf_slot ^= 1;
@@ -318,19 +358,19 @@ __device__ __forceinline__ void split_epilogue(const GemmArgs& args, uint32_t ta
   }
 }
 
-template <int BM, bool GATED>
+template <int BM, bool GATED, bool FP4A = false>
 __global__ void __launch_bounds__(192, 1)
     expert_gemm_kernel(const __grid_constant__ CUtensorMap tmW0,
                        const __grid_constant__ CUtensorMap tmW1,
                        const __grid_constant__ CUtensorMap tmS0,
                        const __grid_constant__ CUtensorMap tmS1,
                        const __grid_constant__ CUtensorMap tmX, const GemmArgs args) {
-  using C = GemmCfg<BM, GATED>;
+  using C = GemmCfg<BM, GATED, FP4A>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* tile_base = smem;
-  uint8_t* sf_base = smem + (size_t)C::STAGES * C::TILE_BYTES;
+  uint8_t* sf_base = smem + (size_t)C::STAGES * C::STAGE_BYTES;
   uint8_t* ctrl = sf_base + C::SF_RING;
   uint64_t* full = reinterpret_cast<uint64_t*>(ctrl);
   uint64_t* empty = full + C::STAGES;
@@ -379,8 +419,8 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0)
-      gemm_produce<C, GATED>(&tmW0, &tmW1, &tmS0, &tmS1, &tmX, args, tile_base, sf_base, full, empty,
-                             abort_flag, NB, KT, KT4, total, step);
+      gemm_produce<C, GATED, FP4A>(&tmW0, &tmW1, &tmS0, &tmS1, &tmX, args, tile_base, sf_base, full, empty,
+                                   abort_flag, NB, KT, KT4, total, step);
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -388,6 +428,7 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0;
       uint32_t aphase = 0;
       int sf_slot = 1;  // follows the producer's ring slot
+      uint32_t sf_set = 0;  // FP4A: TMEM scale column set of the next k tile
       const uint32_t sfa_t = tmem + C::SFA_COL;
       const uint32_t sfb_t = tmem + C::SFB_COL;
       int4 tl_next = make_int4(0, 0, 0, 0);
@@ -395,6 +436,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int w = blockIdx.x; w < total && !*abort_flag; w += step) {
         const int4 tl = tl_next;
         if (w + step < total) tl_next = args.tiles[(w + step) / S / NB];
+        if (filtered_out(args, tl.x >= args.n_routed)) continue;
         const int kt0 = (w % S) * KTS;
         const uint32_t b_fmt = tl.x >= args.n_routed ? 0u : 5u;  // e4m3 shared, e2m1 routed
         if (!mbar_wait(acc_empty, aphase ^ 1, DSV4_DEVERR_TIMEOUT_MMA)) {
@@ -409,7 +451,35 @@ __global__ void __launch_bounds__(192, 1)
             break;
           }
           tc_fence_after();
-          const uint8_t* st = tile_base + (size_t)stage * C::TILE_BYTES;
+          const uint8_t* st = tile_base + (size_t)stage * C::STAGE_BYTES;
+          if constexpr (FP4A) {
+            // the stage's atoms into the column set the previous k tile's
+            // MMAs are not reading; K = 64 per MMA: window kk / 2, scale
+            // bytes {0,1} or {2,3} of it
+            const uint8_t* sfs = st + C::TILE_BYTES;
+            const uint32_t sfa_k = sfa_t + 24 * sf_set, sfb_k = sfa_k + 8;
+            tc_cp_sf(sfa_k, sdesc_sf(smem_u32(sfs)));
+            tc_cp_sf(sfa_k + 4, sdesc_sf(smem_u32(sfs + 512)));
+            tc_cp_sf(sfb_k, sdesc_sf(smem_u32(sfs + 1024)));       // w1 rows, window 0
+            tc_cp_sf(sfb_k + 8, sdesc_sf(smem_u32(sfs + 1536)));   // w1 rows, window 1
+            tc_cp_sf(sfb_k + 4, sdesc_sf(smem_u32(sfs + 2048)));   // w3 rows, window 0
+            tc_cp_sf(sfb_k + 12, sdesc_sf(smem_u32(sfs + 2560)));  // w3 rows, window 1
+            const uint64_t adesc = sdesc_k_sw128(smem_u32(st));
+            const uint64_t bdesc = sdesc_k_sw128(smem_u32(st + C::A_BYTES));
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint32_t id = (kk & 1) * 2;
+              tc_mma_mxf4(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc_mxf4(256, id, id), sfa_k + 4 * (kk >> 1),
+                          sfb_k + 8 * (kk >> 1), (kt > kt0 || kk > 0) ? 1u : 0u);
+            }
+            sf_set ^= 1;
+            tc_commit(&empty[stage]);
+            if (++stage == C::STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+            continue;
+          }
           // one burst of scale copies per four k tiles, into the column set the
           // previous group's MMAs are not reading
           if ((kt & 3) == 0) sf_slot ^= 1;
@@ -464,6 +534,7 @@ __global__ void __launch_bounds__(192, 1)
     for (int w = blockIdx.x; w < total; w += step) {
       const int item = w / S;
       const int4 tl = args.tiles[item / NB];
+      if (filtered_out(args, tl.x >= args.n_routed)) continue;
       const int jb = item % NB;
       const int row0 = tl.y, nrows = tl.z;
       // epi_abort is written only by epilogue warps and read between two
@@ -616,6 +687,29 @@ int make_tmap_fp4_arena(CUtensorMap* m, const void* base, int K, int rows, int s
   return r == CUDA_SUCCESS ? DSV4_OK : DSV4_ERR_CUDA;
 }
 
+// FP4 e2m1 weights of every arena slot read as packed bytes (two codes per
+// byte, for kind::mxf4): dims {K/2 bytes, rows, slots}, box {128 bytes = 256
+// values, 128 rows, 1}.
+int make_tmap_fp4_packed_arena(CUtensorMap* m, const void* base, int K, int rows, int slots,
+                               long long slot_stride, int l2_promotion) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return DSV4_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (slot_stride & 15) || (K % 256)) return DSV4_ERR_ARG;
+  cuuint64_t dims[3] = {(cuuint64_t)(K / 2), (cuuint64_t)rows, (cuuint64_t)slots};
+  cuuint64_t strides[2] = {(cuuint64_t)(K / 2), (cuuint64_t)slot_stride};
+  cuuint32_t box[3] = {128, 128, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  const CUtensorMapL2promotion promo =
+      l2_promotion >= 256 ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B
+      : l2_promotion >= 128 ? CU_TENSOR_MAP_L2_PROMOTION_L2_128B
+      : l2_promotion >= 64  ? CU_TENSOR_MAP_L2_PROMOTION_L2_64B
+                            : CU_TENSOR_MAP_L2_PROMOTION_NONE;
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, promo,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? DSV4_OK : DSV4_ERR_CUDA;
+}
+
 // 8-bit row-major matrix [rows][K] (e4m3 weights or activations), box {128, box_rows}.
 int make_tmap_u8(CUtensorMap* m, const void* base, int K, int rows, int box_rows) {
   EncodeTiledFn enc = get_encode_fn();
@@ -657,6 +751,27 @@ static int launch_one(const CUtensorMap& a0, const CUtensorMap& a1, const CUtens
   launch_k(expert_gemm_kernel<BM, GATED>, grid, 192, C::SMEM_BYTES, st,
            a0, a1, s0, s1, b, args);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
+}
+
+template <int BM>
+static int launch_one_fp4(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b, const GemmArgs& args,
+                          int grid, cudaStream_t st) {
+  using C = GemmCfg<BM, true, true>;
+  if (ensure_smem_attr(reinterpret_cast<const void*>(expert_gemm_kernel<BM, true, true>), (int)C::SMEM_BYTES))
+    return DSV4_ERR_CUDA;
+  launch_k(expert_gemm_kernel<BM, true, true>, grid, 192, C::SMEM_BYTES, st, a0, a1, a0, a1, b, args);
+  return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
+}
+
+int launch_expert_gemm_fp4(int block_n, const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b,
+                           const GemmArgs& args, int grid, cudaStream_t st) {
+  if (args.seg_filter != 1 || args.k_split != 1) return DSV4_ERR_ARG;  // routed items, unsplit
+  switch (block_n) {
+    case 32: return launch_one_fp4<32>(a0, a1, b, args, grid, st);
+    case 64: return launch_one_fp4<64>(a0, a1, b, args, grid, st);
+    case 128: return launch_one_fp4<128>(a0, a1, b, args, grid, st);
+    default: return DSV4_ERR_ARG;
+  }
 }
 
 int launch_expert_gemm(bool gated, int block_n, const CUtensorMap& a0, const CUtensorMap& a1,

@@ -34,6 +34,9 @@ struct GemmArgs {
   int part_rows;          // compact rows per slice (>= every valid route row)
   int part_ld;            // floats per compact row: nb_count * 256
   int* item_done;         // [n_tiles * nb_count] slices finished, zeroed by the route plan
+  // 0: every segment; 1: routed segments only; 2: the shared segment only
+  // (an item of another segment is skipped by all warps alike)
+  int seg_filter;
 };
 
 int launch_gate_logits(const void* x, const void* w, int w_is_fp32, int T, int H, int E,
@@ -68,6 +71,9 @@ int launch_single_segment_plan(int T, int seg, int block_n, int rows_pad, const 
                                int* total_rows, cudaStream_t st);
 int launch_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* s, int num_sms,
                      cudaStream_t st);
+int launch_fp4_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* s, int num_sms, cudaStream_t st);
+int launch_fp4_permute_quant(const void* x, int T, int H, const int* slot_token, const int* total_rows_ptr,
+                             int max_rows, uint8_t* xq4, uint8_t* atoms, int num_sms, cudaStream_t st);
 // expert parallelism (ep.cu)
 long long ep_row_bytes(int H, int k);
 long long ep_dispatch_workspace(int T, int world);
@@ -113,6 +119,8 @@ int launch_build_sf_fp8(const uint8_t* scale, int rows, int K, uint8_t* atoms, i
 int make_tmap_fp4_arena(CUtensorMap* m, const void* base, int K, int rows, int slots,
                         long long slot_stride, int l2_promotion);
 int make_tmap_u8(CUtensorMap* m, const void* base, int K, int rows, int box_rows);
+int make_tmap_fp4_packed_arena(CUtensorMap* m, const void* base, int K, int rows, int slots,
+                               long long slot_stride, int l2_promotion);
 struct PairMaps;
 int make_tmap_atoms(CUtensorMap* m, const void* base, long long bytes, int box_rows);
 int pair_clusters_resident(bool gated);
@@ -123,5 +131,10 @@ int launch_expert_gemm_pair(bool gated, const PairMaps& maps, const GemmArgs& ar
 int launch_expert_gemm(bool gated, int block_n, const CUtensorMap& a0, const CUtensorMap& a1,
                        const CUtensorMap& s0, const CUtensorMap& s1, const CUtensorMap& b,
                        const GemmArgs& args, int grid, cudaStream_t st);
+// GEMM1 of the routed experts on FP4 activations (kind::mxf4): a0 / a1 packed
+// w1 / w3 arena maps, b the packed activation rows; args.kt_count = H / 256,
+// args.sfb the per-32 activation atoms.
+int launch_expert_gemm_fp4(int block_n, const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b,
+                           const GemmArgs& args, int grid, cudaStream_t st);
 
 }  // namespace dsv4

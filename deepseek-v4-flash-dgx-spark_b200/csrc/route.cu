@@ -438,6 +438,59 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const __nv_bfloat16* __r
 }
 
 // ---------------------------------------------------------------------------
+// FP4 activations (fp4_block_quant): one thread per 32-value block.
+// fp4_act_quant_kernel: plain rows -> packed codes [M][K/2] + scale bytes
+// [M][K/32] (the official fp4_act_quant's outputs).
+// fp4_permute_quant_kernel: plan slot rows (token slot_token[row], -1 = a
+// padding row: zero codes) -> packed codes [rows][H/2] and per-32 scale atoms
+// for the tensor core: atom (g, w) holds rows 32g .. 32g+127 for the 128-wide
+// k window w, row r / block b of the window at byte (r%32)*16 + ((r/32)-g)*4 + b
+// (each row written to its four overlapping atoms, as the per-128 atoms are).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) fp4_act_quant_kernel(const __nv_bfloat16* __restrict__ x, int M, int K,
+                                                            uint8_t* __restrict__ q, uint8_t* __restrict__ s) {
+  const int nb = K / 32;
+  const long long n = (long long)M * nb;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int row = (int)(i / nb), b = (int)(i % nb);
+    float v[32];
+    load_bf16x32(x + (size_t)row * K + 32 * b, v);
+    uint4 packed;
+    const int e = fp4_block_quant(v, packed);
+    *reinterpret_cast<uint4*>(q + (size_t)row * (K / 2) + 16 * b) = packed;
+    s[(size_t)row * nb + b] = static_cast<uint8_t>(e + 127);
+  }
+}
+
+__global__ void __launch_bounds__(256) fp4_permute_quant_kernel(
+    const __nv_bfloat16* __restrict__ x, int T, int H, const int* __restrict__ slot_token,
+    const int* __restrict__ total_rows_ptr, int max_rows, uint8_t* __restrict__ xq4,
+    uint8_t* __restrict__ atoms) {
+  const int nb = H / 32, KW = H / 128;
+  const int total = min(*total_rows_ptr, max_rows);
+  const long long n = (long long)total * nb;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int row = (int)(i / nb), b = (int)(i % nb);
+    const int t = slot_token[row];
+    float v[32];
+    if (t >= 0 && t < T) {  // anything else (padding, a failed plan's leftovers) quantizes zeros
+      load_bf16x32(x + (size_t)t * H + 32 * b, v);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = 0.f;
+    }
+    uint4 packed;
+    const int e = fp4_block_quant(v, packed);
+    *reinterpret_cast<uint4*>(xq4 + (size_t)row * (H / 2) + 16 * b) = packed;
+    const int w = b >> 2, g = row >> 5;
+#pragma unroll
+    for (int m1 = 0; m1 < 4; ++m1)
+      if (g - m1 >= 0)
+        atoms[((size_t)(g - m1) * KW + w) * 512 + (row & 31) * 16 + m1 * 4 + (b & 3)] = static_cast<uint8_t>(e + 127);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Combine: y[t] = bf16( sum over t's routes in ascending expert id of O[slot]
 // (fp32) + O[shared slot] ).  Routing weights were applied inside the expert
 // (before w2), so this is a plain ordered sum.  One CTA per token, one thread
@@ -614,6 +667,26 @@ int launch_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* s, int nu
   if (grid < 1) return DSV4_OK;
   launch_k(act_quant_kernel, grid, warps * 32, 0, st,
            static_cast<const __nv_bfloat16*>(x), M, K, q, s);
+  return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
+}
+
+int launch_fp4_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* s, int num_sms, cudaStream_t st) {
+  const long long n = (long long)M * (K / 32);
+  if (n <= 0) return DSV4_OK;
+  long long grid = (n + 255) / 256;
+  if (grid > 8LL * num_sms) grid = 8LL * num_sms;
+  launch_k(fp4_act_quant_kernel, (unsigned)grid, 256, 0, st, static_cast<const __nv_bfloat16*>(x), M, K, q, s);
+  return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
+}
+
+int launch_fp4_permute_quant(const void* x, int T, int H, const int* slot_token, const int* total_rows_ptr,
+                             int max_rows, uint8_t* xq4, uint8_t* atoms, int num_sms, cudaStream_t st) {
+  const long long n = (long long)max_rows * (H / 32);
+  if (n <= 0) return DSV4_OK;
+  long long grid = (n + 255) / 256;
+  if (grid > 8LL * num_sms) grid = 8LL * num_sms;
+  launch_k(fp4_permute_quant_kernel, (unsigned)grid, 256, 0, st, static_cast<const __nv_bfloat16*>(x), T, H,
+           slot_token, total_rows_ptr, max_rows, xq4, atoms);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
 

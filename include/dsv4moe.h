@@ -67,6 +67,17 @@ DSV4_API const char* dsv4_status_string(int status);
  * GEMMs.  It also changes dsv4_moe_workspace_bytes and the EP workspace
  * sizes: set it before sizing workspaces, not while calls are in flight. */
 DSV4_API int dsv4_set_k_split(int slices);
+/* Opt-in FP4 activations for the routed experts' GEMM1 (no counterpart in the
+ * reference, whose layer quantizes activations to e4m3 per 128): on = 1 makes
+ * dsv4_moe_forward quantize each routed row with the official fp4_act_quant
+ * semantics (dsv4_fp4_act_quant) and run w1 | w3 as kind::mxf4 products
+ * (e2m1 x e2m1, per-32 ue8m0 scales: the FP4 tensor rate, twice the FP8 one).
+ * The shared expert, GEMM2 and the expert-parallel entry points keep e4m3
+ * activations.  This changes the layer's numerics (FP4 activations); 0 (the
+ * default, or DSV4_FP4_ACT=0) is the reference's arithmetic.  It changes
+ * dsv4_moe_workspace_bytes: set it before sizing workspaces.
+ * dsv4_moe_workspace_layout's out[20] says whether a layout uses it. */
+DSV4_API int dsv4_set_fp4_activations(int on);
 /* Synchronises the device, returns the first device-side error code (0 if
  * none) in *code, and clears it when clear != 0. */
 DSV4_API int dsv4_device_error(int clear, int* code);
@@ -215,6 +226,15 @@ DSV4_API int dsv4_gate_route_hash(const void* x, const void* w, int w_is_fp32, c
 /* Official kernel.act_quant(x, 128, "ue8m0") (scripts/smoke_official_kernels.py:
  * 44-49): bf16 [M,K] -> e4m3 codes [M,K] + ue8m0 scales [M,K/128]. */
 DSV4_API int dsv4_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* scale, void* stream);
+
+/* Official kernel.fp4_act_quant(x, 32) (scripts/smoke_official_kernels.py:
+ * 32-34; results float4_e2m1fn_x2 codes + float8_e8m0fnu scales,
+ * docs/experiments/016-native-kernel-smoke.md:50): bf16 [M,K] -> packed e2m1
+ * codes [M,K/2] (element 2i in the low nibble) + ue8m0 scales [M,K/32].  Per
+ * 32 values: amax = max(|x|, 1e-4), s = 2^ceil(log2(amax * fp32(1/6))),
+ * codes = e2m1(x / s) rounded to nearest even.  K % 32 == 0; x and q 16-byte
+ * aligned. */
+DSV4_API int dsv4_fp4_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* scale, void* stream);
 
 /* ---- attention block: dense FP8 linear layers ---------------------------
  * The official linear(x, W) for an FP8 weight (act_quant(x, 128, "ue8m0") ->

@@ -185,6 +185,47 @@ def act_quant(x: np.ndarray, block: int = 128) -> tuple[np.ndarray, np.ndarray]:
     return q.reshape(M, K), (e + 127).astype(np.uint8)
 
 
+# e2m1 magnitudes by code, and the rounding boundaries between neighbouring
+# codes: a magnitude exactly on a boundary rounds to the even code (down at
+# 0.25, 1.25, 2.5, 5; up at 0.75, 1.75, 3.5); above 5 it saturates to 6.
+_E2M1_DOWN_TIES = np.array([0.25, 1.25, 2.5, 5.0], np.float32)
+_E2M1_UP_TIES = np.array([0.75, 1.75, 3.5], np.float32)
+_INV_E2M1_MAX = np.float32(1.0 / 6.0)
+
+
+def f32_to_e2m1_codes(v: np.ndarray) -> np.ndarray:
+    """fp32 -> 4-bit e2m1 codes (sign in bit 3), round to nearest even,
+    saturating at +-6 (cvt.rn.satfinite semantics)."""
+    v = np.asarray(v, np.float32)
+    a = np.abs(v)
+    code = (a[..., None] > _E2M1_DOWN_TIES).sum(-1) + (a[..., None] >= _E2M1_UP_TIES).sum(-1)
+    return (code.astype(np.uint8) | (np.signbit(v).astype(np.uint8) << 3)).astype(np.uint8)
+
+
+def fp4_act_quant(x: np.ndarray, block: int = 32) -> tuple[np.ndarray, np.ndarray]:
+    """The official ``fp4_act_quant(x, 32)`` (scripts/smoke_official_kernels.py:
+    32-34; result types torch.float4_e2m1fn_x2 codes and float8_e8m0fnu scales,
+    docs/experiments/016-native-kernel-smoke.md:50), restated with the
+    conventions of ``act_quant``: per block of 32, amax = max(|x|, 1e-4),
+    s = 2^ceil(log2(amax * fp32(1/6))), q = e2m1(x / s) with round to nearest
+    even; codes packed two per byte, element 2i in the low nibble.
+    Returns (packed [M, K/2] uint8, scale bytes [M, K/block] uint8)."""
+    x = np.asarray(x, dtype=np.float32)
+    M, K = x.shape
+    assert K % block == 0 and block % 2 == 0
+    xb = x.reshape(M, K // block, block)
+    amax = np.maximum(np.max(np.abs(xb), axis=-1), np.float32(1e-4))
+    e = ceil_log2_exact((amax * _INV_E2M1_MAX).astype(np.float32))
+    codes = f32_to_e2m1_codes(np.ldexp(xb, -e[..., None]).astype(np.float32)).reshape(M, K)
+    packed = (codes[:, 0::2] | (codes[:, 1::2] << 4)).astype(np.uint8)
+    return packed, (e + 127).astype(np.uint8)
+
+
+def fp4_act_dequant(packed: np.ndarray, s: np.ndarray, block: int = 32) -> np.ndarray:
+    vals = unpack_e2m1(packed)
+    return (vals * np.repeat(e8m0_to_f32(s), block, axis=1)).astype(np.float32)
+
+
 def act_dequant(q: np.ndarray, s: np.ndarray, block: int = 128) -> np.ndarray:
     vals = decode_e4m3(q)
     return (vals * np.repeat(e8m0_to_f32(s), block, axis=1)).astype(np.float32)
@@ -361,11 +402,18 @@ def silu(x: np.ndarray) -> np.ndarray:
 
 
 def expert_forward(x_bf16: np.ndarray, ew: ExpertWeights, route_w: np.ndarray | None,
-                   swiglu_limit: float, dense=None) -> np.ndarray:
+                   swiglu_limit: float, dense=None, fp4_act: bool = False) -> np.ndarray:
     """SwiGLU expert.  g = w1(x), u = w3(x) (bf16 outputs); if swiglu_limit > 0:
     u = clamp(u, -limit, limit), g = min(g, limit); h = silu(g) * u, times the
     routing weight when given (applied before w2, in fp32); h is cast to bf16
-    and fed through w2.  Returns bf16 values as fp32 [n, H]."""
+    and fed through w2.  Returns bf16 values as fp32 [n, H].
+
+    fp4_act: x is quantized by fp4_act_quant (e2m1, per-32 scales) instead of
+    act_quant for w1 and w3 (the library's opt-in FP4-activation mode); the
+    products stay exact in float64 (e2m1 x e2m1 with power-of-two scales)."""
+    if fp4_act:
+        q, s = fp4_act_quant(x_bf16)
+        return expert_forward_dequant(fp4_act_dequant(q, s), ew, route_w, swiglu_limit, dense)
     q, s = act_quant(x_bf16)
     return expert_forward_dequant(act_dequant(q, s), ew, route_w, swiglu_limit, dense)
 
@@ -417,14 +465,19 @@ def combine(T: int, H: int, indices: np.ndarray, expert_out: dict, shared_out: n
     return round_bf16(y)
 
 
-def moe_forward(x_bf16: np.ndarray, mw: MoEWeights, routing=None, dense_cache=None, workers: int = 1):
+def moe_forward(x_bf16: np.ndarray, mw: MoEWeights, routing=None, dense_cache=None, workers: int = 1,
+                fp4_act: bool = False):
     """Full layer.  ``routing`` = (weights, indices) overrides the gate (used to
     check the expert math on the device's own routing).  Returns
     (y bf16-as-fp32 [T,H], weights, indices, per-route outputs dict).
 
     ``workers`` > 1 evaluates the experts in a thread pool (the weight decode
     and the float64 products release the GIL); each expert's output is the
-    same either way and the combine always sums in ascending expert id."""
+    same either way and the combine always sums in ascending expert id.
+
+    ``fp4_act``: the routed experts take FP4 activations for w1 / w3 (see
+    ``expert_forward``); the shared expert keeps act_quant, as the library's
+    FP4-activation mode does."""
     T, H = x_bf16.shape
     if routing is None:
         wts, idx, _ = gate_forward(x_bf16, mw.gate_w, mw.gate_bias, mw.topk, mw.route_scale)
@@ -434,7 +487,8 @@ def moe_forward(x_bf16: np.ndarray, mw: MoEWeights, routing=None, dense_cache=No
     def one(e):
         rows, top = np.nonzero(idx == e)  # torch.where order: row-major
         dense = dense_cache(e) if dense_cache is not None else None
-        return e, (rows, expert_forward(x_bf16[rows], mw.experts[e], wts[rows, top], mw.swiglu_limit, dense))
+        return e, (rows, expert_forward(x_bf16[rows], mw.experts[e], wts[rows, top], mw.swiglu_limit, dense,
+                                        fp4_act=fp4_act))
 
     active = [int(e) for e in np.unique(idx)]
     if workers > 1 and len(active) > 1:
