@@ -160,6 +160,9 @@ static int k_split_setting() {
 // default, matching the reference's e4m3 act_quant; 1 = on).  From
 // DSV4_FP4_ACT on first use, or dsv4_set_fp4_activations.
 static std::atomic<int> g_fp4_act_setting{-1};
+// bumped by every setter: a captured graph records the kernels of the settings
+// in force, so callers that cache graphs compare it
+static std::atomic<long long> g_settings_generation{0};
 
 static int fp4_act_setting() {
   int v = g_fp4_act_setting.load(std::memory_order_relaxed);
@@ -517,6 +520,7 @@ int dsv4_version(void) { return 1; }
 int dsv4_set_fp4_activations(int on) {
   if (on != 0 && on != 1) return DSV4_ERR_ARG;
   g_fp4_act_setting.store(on, std::memory_order_relaxed);
+  g_settings_generation.fetch_add(1, std::memory_order_relaxed);
   return DSV4_OK;
 }
 
@@ -532,8 +536,11 @@ int dsv4_fp4_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* s, void
 int dsv4_set_k_split(int slices) {
   if (slices < 0 || slices > 64) return DSV4_ERR_ARG;
   g_k_split_setting.store(slices, std::memory_order_relaxed);
+  g_settings_generation.fetch_add(1, std::memory_order_relaxed);
   return DSV4_OK;
 }
+
+long long dsv4_settings_generation(void) { return g_settings_generation.load(std::memory_order_relaxed); }
 
 long long dsv4_kernel_launches(void) { return g_kernel_launches.load(std::memory_order_relaxed); }
 

@@ -252,6 +252,23 @@ std::tuple<at::Tensor, at::Tensor> act_quant(const at::Tensor& x) {
   return {q, s};
 }
 
+// The official kernel.fp4_act_quant(x, 32): packed e2m1 codes [M, K/2] (two
+// per byte, element 2i in the low nibble) and ue8m0 scale bytes [M, K/32].
+std::tuple<at::Tensor, at::Tensor> fp4_act_quant(const at::Tensor& x) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16, "x must be bfloat16");
+  const int64_t K = x.size(-1);
+  TORCH_CHECK(K % 32 == 0, "the last dimension must be a multiple of 32");
+  c10::cuda::CUDAGuard guard(x.device());
+  const at::Tensor x2 = x.reshape({-1, K});
+  at::Tensor q = at::empty({x2.size(0), K / 2}, x2.options().dtype(at::kByte));
+  at::Tensor s = at::empty({x2.size(0), K / 32}, x2.options().dtype(at::kByte));
+  check_status(dsv4_fp4_act_quant(x2.data_ptr(), static_cast<int>(x2.size(0)), static_cast<int>(K),
+                                  q.data_ptr<uint8_t>(), s.data_ptr<uint8_t>(), stream_of(x2)),
+               "dsv4_fp4_act_quant");
+  return {q, s};
+}
+
 // ---------------------------------------------------------- attention block
 // The official kernel.sparse_attn(q, kv, attn_sink, topk_idxs, softmax_scale)
 // (spark_runtime/lazy_official_runtime.py:1016-1049 swaps in a Python fallback).
@@ -508,6 +525,7 @@ TORCH_LIBRARY(dsv4moe, m) {
   m.def("gate_logits(Tensor x, Tensor weight) -> Tensor");
   m.def("gate_topk(Tensor logits, Tensor? bias, int topk, float route_scale) -> (Tensor, Tensor)");
   m.def("act_quant(Tensor x) -> (Tensor, Tensor)");
+  m.def("fp4_act_quant(Tensor x) -> (Tensor, Tensor)");
   m.def("materialize(Tensor slab, Tensor src_off, Tensor dst_slot, Tensor(a!)? arena, int slot_stride, "
         "Tensor(b!)? arena_sf, int sf_slot_stride, Tensor(c!)? bf16_out, int bf16_slot_stride, int hidden, "
         "int inter) -> int");
@@ -543,6 +561,7 @@ TORCH_LIBRARY_IMPL(dsv4moe, CUDA, m) {
   m.impl("gate_logits", &gate_logits);
   m.impl("gate_topk", &gate_topk);
   m.impl("act_quant", &act_quant);
+  m.impl("fp4_act_quant", &fp4_act_quant);
   m.impl("materialize", &materialize);
   m.impl("build_scale_atoms", &build_scale_atoms);
   m.impl("build_shared_scale_atoms", &build_shared_scale_atoms);

@@ -517,10 +517,11 @@ class MoE(nn.Module):
                 and not torch.cuda.is_current_stream_capturing())
 
     def _graph_key(self) -> tuple:
-        """Every address a captured layer holds: a change of any recaptures."""
+        """Every address a captured layer holds, and the library's settings
+        generation (split-K, FP4 activations): a change of any recaptures."""
         sh = self.shared_experts
         ex = getattr(self, "peer_exchange", None)
-        return (self.gate.weight.data_ptr(), ptr(self.gate.bias), self.arena.buffer.data_ptr(),
+        return (_lib.load().dsv4_settings_generation(), self.gate.weight.data_ptr(), ptr(self.gate.bias), self.arena.buffer.data_ptr(),
                 self.arena.sf.data_ptr(), self.expert_slot.data_ptr(), sh.w1.weight.data_ptr(),
                 sh.w2.weight.data_ptr(), sh.w3.weight.data_ptr(), sh.scale_atoms.data_ptr(),
                 ex.buf.value if ex is not None else 0)
@@ -569,6 +570,14 @@ class MoE(nn.Module):
         if ex is not None:
             ex.note_call_end()
         return entry[2].clone()
+
+    @staticmethod
+    def set_fp4_activations(on: bool) -> None:
+        """Opt-in FP4 activations for the routed experts' w1 | w3
+        (``dsv4_set_fp4_activations``): the FP4 tensor rate at prefill, at the
+        cost of the layer's numerics (the reference quantizes to e4m3).
+        Process-wide; set it before sizing workspaces."""
+        _lib.check(_lib.load().dsv4_set_fp4_activations(1 if on else 0), "dsv4_set_fp4_activations")
 
     def reset_graphs(self) -> None:
         """Drop the captured graphs (they are recaptured on the next calls)."""

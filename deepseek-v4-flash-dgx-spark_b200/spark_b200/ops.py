@@ -92,6 +92,12 @@ def _register_fakes() -> None:
         M = x.numel() // K
         return x.new_empty((M, K), dtype=torch.uint8), x.new_empty((M, K // 128), dtype=torch.uint8)
 
+    @fake("fp4_act_quant")
+    def _(x):
+        K = x.shape[-1]
+        M = x.numel() // K
+        return x.new_empty((M, K // 2), dtype=torch.uint8), x.new_empty((M, K // 32), dtype=torch.uint8)
+
     @fake("ep_dispatch_p2p")
     def _(x, indices, weights, n_routed, world, rank, peer_bases, cap, epoch):
         return x.new_empty((max(x.shape[0], 1), indices.shape[1]), dtype=torch.int32)

@@ -78,6 +78,10 @@ DSV4_API int dsv4_set_k_split(int slices);
  * dsv4_moe_workspace_bytes: set it before sizing workspaces.
  * dsv4_moe_workspace_layout's out[20] says whether a layout uses it. */
 DSV4_API int dsv4_set_fp4_activations(int on);
+/* A counter that every call of dsv4_set_k_split / dsv4_set_fp4_activations
+ * advances: a caller that captured CUDA graphs of the layer recaptures when it
+ * changes (the settings choose the kernels a graph holds). */
+DSV4_API long long dsv4_settings_generation(void);
 /* Synchronises the device, returns the first device-side error code (0 if
  * none) in *code, and clears it when clear != 0. */
 DSV4_API int dsv4_device_error(int clear, int* code);

@@ -69,6 +69,10 @@ def test_fp4_act_quant_bit_exact(cuda_device):
     qo, so = O.fp4_act_quant(x.float().numpy())
     assert np.array_equal(s.cpu().numpy(), so)
     assert np.array_equal(q.cpu().numpy(), qo)
+    from spark_b200 import ops
+
+    q2, s2 = ops.load().fp4_act_quant(xd)  # the torch op: the same call
+    assert torch.equal(q2, q) and torch.equal(s2, s)
 
 
 @pytest.mark.parametrize("name,T", [("decode", 64), ("decode", 1000), ("cpu_ref", 300)])
@@ -106,3 +110,28 @@ def test_fp4_activation_layer_matches_the_fp4_oracle(cuda_device, fp4_mode, name
     y8 = O.moe_forward(xs, mw, routing=(w_gpu, i_gpu), workers=_WORKERS)[0]
     print(f"\n{name} T={T}: vs FP4 oracle max {err:.4f}, vs e4m3 oracle max {_rel_err(got, y8):.4f} "
           f"rms {_rms_err(got, y8):.4f} (of output RMS)")
+
+
+def test_module_graphs_follow_the_fp4_setting(cuda_device):
+    """MoE.forward's cached graphs hold the kernels of the settings in force:
+    switching the FP4 mode recaptures, so each call equals the eager layer of
+    the current setting."""
+    from spark_b200 import _lib
+    from spark_b200.moe import MoE
+    from spark_b200.synthetic import CONFIGS, build_moe, make_layer
+
+    cfg = CONFIGS["decode"].with_tokens(32)
+    layer = make_layer(cfg, seed=5, device="cpu")
+    moe = build_moe(layer, device=cuda_device)
+    x = layer["x"].to(cuda_device)
+    try:
+        for on in (False, True, False):
+            MoE.set_fp4_activations(on)
+            y = moe(x.view(1, 32, -1)).view(32, -1)
+            assert torch.equal(y, moe.forward_tokens(x)), on
+        y8 = moe(x.view(1, 32, -1)).view(32, -1)
+        MoE.set_fp4_activations(True)
+        assert not torch.equal(moe(x.view(1, 32, -1)).view(32, -1), y8)
+    finally:
+        MoE.set_fp4_activations(False)
+    _lib.raise_on_device_error()

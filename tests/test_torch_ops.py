@@ -12,7 +12,7 @@ import torch
 OPS = ["moe_forward", "moe_forward_out", "moe_workspace_bytes", "expert_forward", "gate_route", "gate_logits",
        "gate_topk", "act_quant", "materialize", "build_scale_atoms", "build_shared_scale_atoms", "ep_dispatch",
        "ep_expert_forward", "ep_combine", "ep_dispatch_p2p", "ep_expert_forward_p2p", "ep_combine_p2p",
-       "read_into", "sparse_attn", "build_fp8_weight_atoms", "fp8_linear"]
+       "read_into", "sparse_attn", "build_fp8_weight_atoms", "fp8_linear", "fp4_act_quant"]
 
 
 @pytest.fixture(scope="module")
@@ -45,6 +45,8 @@ def test_fake_kernels_give_output_shapes_on_meta(dsv4):
     assert w.shape == (T, k) and idx.dtype == torch.int64 and logits.shape == (T, E)
     q, s = dsv4.act_quant(x)
     assert q.shape == (T, H) and s.shape == (T, H // 128) and q.dtype == torch.uint8
+    q4, s4 = dsv4.fp4_act_quant(x)
+    assert q4.shape == (T, H // 2) and s4.shape == (T, H // 32) and q4.dtype == torch.uint8
     assert dsv4.gate_logits(x, layer[0]).shape == (T, E)
     assert dsv4.expert_forward(x, 0, None, layer, dims, [1.0, 0.0]).shape == (T, H)
     assert ops.OPS_LIB.name == "libdsv4moe_torch.so"
