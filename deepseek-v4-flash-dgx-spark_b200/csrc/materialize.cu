@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(256) build_sf_fp8_kernel(const uint8_t* __rest
   }
 }
 
-constexpr int kDecodeGroupsPerThread = 8;
+constexpr int kDecodeWordsPerThread = 8;
 
 // bf16 bits of the two e2m1 codes of byte v (low nibble first) at scale 1.
 __device__ __forceinline__ uint32_t e2m1_pair_bf16_bits(uint32_t v) {
@@ -109,14 +109,48 @@ __device__ __forceinline__ uint32_t e2m1_pair_bf16_bits(uint32_t v) {
   return out;
 }
 
+// 8 e2m1 codes (one 32-bit word) at ue8m0 scale byte s -> 8 bf16 (16 bytes).
+__device__ __forceinline__ uint4 decode_word(uint32_t cw, int s, const uint32_t* lut) {
+  uint32_t pk[4];
+  if (s >= 16 && s <= 239) {
+    const uint32_t d = (uint32_t)((s - 127) << 7) & 0xFFFFu;
+    const uint32_t dpair = d | (d << 16);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t x = lut[(cw >> (8 * i)) & 0xFF];
+      const uint32_t nz = __vcmpne2(x & 0x7FFF7FFFu, 0u);  // +-0 keeps its exponent
+      pk[i] = __vadd2(x, dpair & nz);
+    }
+  } else {
+    const float sc = exp2i(s - 127);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float v[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t c = (cw >> (8 * i + 4 * h)) & 0xF;
+        // e2m1: exponent bits 2..1, mantissa bit 0; subnormal when exponent = 0
+        const uint32_t ex = (c >> 1) & 3, m = c & 1;
+        const float mag = ex == 0 ? 0.5f * (float)m : exp2i((int)ex - 1) * (1.0f + 0.5f * (float)m);
+        v[h] = (c & 8) ? -mag * sc : mag * sc;
+      }
+      const __nv_bfloat162 p = __floats2bfloat162_rn(v[0], v[1]);
+      pk[i] = *reinterpret_cast<const uint32_t*>(&p);
+    }
+  }
+  return make_uint4(pk[0], pk[1], pk[2], pk[3]);
+}
+
 // Exact bf16 decode of the three fp4 weights of n experts:
 // out + dst_slot[i] * out_slot_stride + {w1, w2, w3} as [rows, K] bf16.
 // blockIdx.y = expert * 3 + weight (packed order w1, w2, w3).  One thread
-// decodes one ue8m0 scale group: 32 codes (16 bytes, coalesced), one scale
-// byte, 64 bytes of bf16 out.  e2m1 x 2^(s-127) is exact in bf16; for
-// 16 <= s <= 239 every nonzero result is a normal bf16, so the product is the
-// scale-1 bit pattern (a 256-entry byte -> bf16x2 table) with s - 127 added to
-// both exponent fields; other scale bytes take the float path.
+// decodes one 32-bit code word (8 codes, a quarter of a ue8m0 scale group)
+// into 16 bytes of bf16: a warp reads 128 contiguous bytes and writes 512, so
+// every store instruction fills whole sectors; each thread keeps
+// kDecodeWordsPerThread words in flight.  e2m1 x 2^(s-127) is exact in bf16;
+// for 16 <= s <= 239 every nonzero result is a normal bf16, so the product is
+// the scale-1 bit pattern (a 256-entry byte -> bf16x2 table) with s - 127
+// added to both exponent fields; other scale bytes take the float path.
 __global__ void __launch_bounds__(256) decode_bf16_kernel(
     const uint8_t* __restrict__ src, const long long* __restrict__ src_off,
     const int* __restrict__ dst_slot, int hidden, int inter, __nv_bfloat16* __restrict__ out,
@@ -127,60 +161,32 @@ __global__ void __launch_bounds__(256) decode_bf16_kernel(
   const int b = blockIdx.y / 3, wsel = blockIdx.y % 3;
   const long long w_elems = (long long)inter * hidden;
   const long long groups = w_elems / 32;  // scale groups of one weight (= its scale bytes)
+  const long long words = w_elems / 8;    // 32-bit code words of one weight
   if (src_off[b] & 15) {
     if (blockIdx.x == 0 && threadIdx.x == 0) record_error(DSV4_DEVERR_MISALIGNED);
     return;
   }
   const uint8_t* blk = src + src_off[b];
   const uint8_t* scale = blk + (long long)wsel * groups;
-  const uint4* codes = reinterpret_cast<const uint4*>(blk + 3 * groups + (long long)wsel * (w_elems / 2));
-  uint4* o = reinterpret_cast<uint4*>(out + (long long)dst_slot[b] * out_slot_stride +
-                                      (long long)wsel * w_elems);
-  // short CTAs (kDecodeGroupsPerThread strided groups per thread) so the many
-  // CTAs of a launch balance over the SMs without a long partial last wave
-#pragma unroll 2
-  for (int j = 0; j < kDecodeGroupsPerThread; ++j) {
-    const long long g = ((long long)blockIdx.x * kDecodeGroupsPerThread + j) * blockDim.x + threadIdx.x;
-    if (g >= groups) break;
-    const int s = __ldcs(scale + g);
-    const uint4 c4 = __ldcs(codes + g);
-    const uint32_t cw[4] = {c4.x, c4.y, c4.z, c4.w};
-    if (s >= 16 && s <= 239) {
-      const uint32_t d = (uint32_t)((s - 127) << 7) & 0xFFFFu;
-      const uint32_t dpair = d | (d << 16);
+  const uint32_t* codes = reinterpret_cast<const uint32_t*>(blk + 3 * groups + (long long)wsel * (w_elems / 2));
+  uint4* o = reinterpret_cast<uint4*>(out + (long long)dst_slot[b] * out_slot_stride + (long long)wsel * w_elems);
+  const long long w0 = (long long)blockIdx.x * kDecodeWordsPerThread * blockDim.x + threadIdx.x;
+  uint32_t cw[kDecodeWordsPerThread];
+  int sc[kDecodeWordsPerThread];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint32_t pk[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint32_t x = lut[(cw[q] >> (8 * i)) & 0xFF];
-          const uint32_t nz = __vcmpne2(x & 0x7FFF7FFFu, 0u);  // +-0 keeps its exponent
-          pk[i] = __vadd2(x, dpair & nz);
-        }
-        __stcs(o + 4 * g + q, make_uint4(pk[0], pk[1], pk[2], pk[3]));
-      }
-    } else {
-      const float sc = exp2i(s - 127);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint32_t pk[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float v[2];
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const uint32_t c = (cw[q] >> (8 * i + 4 * h)) & 0xF;
-            // e2m1: exponent bits 2..1, mantissa bit 0; subnormal when exponent = 0
-            const uint32_t ex = (c >> 1) & 3, m = c & 1;
-            const float mag = ex == 0 ? 0.5f * (float)m : exp2i((int)ex - 1) * (1.0f + 0.5f * (float)m);
-            v[h] = (c & 8) ? -mag * sc : mag * sc;
-          }
-          const __nv_bfloat162 p = __floats2bfloat162_rn(v[0], v[1]);
-          pk[i] = *reinterpret_cast<const uint32_t*>(&p);
-        }
-        __stcs(o + 4 * g + q, make_uint4(pk[0], pk[1], pk[2], pk[3]));
-      }
+  for (int u = 0; u < kDecodeWordsPerThread; ++u) {
+    const long long w = w0 + (long long)u * blockDim.x;
+    cw[u] = 0;
+    sc[u] = 127;
+    if (w < words) {
+      cw[u] = __ldcs(codes + w);
+      sc[u] = scale[w >> 2];
     }
+  }
+#pragma unroll
+  for (int u = 0; u < kDecodeWordsPerThread; ++u) {
+    const long long w = w0 + (long long)u * blockDim.x;
+    if (w < words) __stcs(o + w, decode_word(cw[u], sc[u], lut));
   }
 }
 
@@ -211,8 +217,8 @@ int launch_materialize(const uint8_t* slab, const long long* src_off, const int*
   }
   if (bf16_out) {
     if (3LL * n > 65535) return DSV4_ERR_UNSUPPORTED;
-    const long long per_cta = 256LL * kDecodeGroupsPerThread;
-    const dim3 grid((unsigned)(((long long)inter * hidden / 32 + per_cta - 1) / per_cta), 3 * n);
+    const long long per_cta = 256LL * kDecodeWordsPerThread;
+    const dim3 grid((unsigned)(((long long)inter * hidden / 8 + per_cta - 1) / per_cta), 3 * n);
     count_launch();
     decode_bf16_kernel<<<grid, 256, 0, st>>>(slab, src_off, dst_slot, hidden, inter,
                                              static_cast<__nv_bfloat16*>(bf16_out),
