@@ -173,6 +173,21 @@ static int fp4_act_setting() {
   return v;
 }
 
+// The fused decode routing kernel (route_small_fused_kernel) for batches of
+// up to 8 tokens: off by default (measured no faster than the three separate
+// kernels inside a CUDA graph, slower at 8 tokens); DSV4_FUSED_ROUTE=1 or
+// dsv4_set_fused_routing(1) turns it on.
+static std::atomic<int> g_fused_route_setting{-1};
+
+static bool small_route_fused_enabled() {
+  int v = g_fused_route_setting.load(std::memory_order_relaxed);
+  if (v < 0) {
+    v = env_int("DSV4_FUSED_ROUTE", 0, 0, 1);
+    g_fused_route_setting.store(v, std::memory_order_relaxed);
+  }
+  return v == 1;
+}
+
 static int choose_k_split(int T, int k, int E, int block_n, int nb, int kt, int nsm) {
   const int groups = kt / 4;
   const int setting = k_split_setting();
@@ -517,6 +532,13 @@ extern "C" {
 
 int dsv4_version(void) { return 1; }
 
+int dsv4_set_fused_routing(int on) {
+  if (on != 0 && on != 1) return DSV4_ERR_ARG;
+  g_fused_route_setting.store(on, std::memory_order_relaxed);
+  g_settings_generation.fetch_add(1, std::memory_order_relaxed);
+  return DSV4_OK;
+}
+
 int dsv4_set_fp4_activations(int on) {
   if (on != 0 && on != 1) return DSV4_ERR_ARG;
   g_fp4_act_setting.store(on, std::memory_order_relaxed);
@@ -730,29 +752,49 @@ int dsv4_moe_forward(const dsv4_moe_layer* L, const void* x, int T, void* y,
 
   const float* rw = routing_weights;
   const int64_t* ri = routing_indices;
-  stage_mark(0, st);
-  if (!rw) {
-    if ((rc = gate_route(x, L->gate_w, L->gate_w_fp32, L->gate_bias, T, H, E, k, L->route_scale,
-                         logits, weights, indices, reinterpret_cast<float*>(ws + p.off[15]),
-                         p.off[16] - p.off[15], nsm, st)))
-      return rc;
-    rw = weights;
-    ri = indices;
-  }
-  stage_mark(1, st);
   int* chunk_cnt = reinterpret_cast<int*>(ws + p.off[16]);
   int* chunk_base = reinterpret_cast<int*>(ws + p.off[17]);
   int* ctrl = reinterpret_cast<int*>(ws + p.off[18]);
   const SplitK sk = plan_split(p, ws);
-  if ((rc = launch_route_plan(ri, T, k, E, 0, p.S ? T : 0, p.block_n, p.max_rows, p.max_tiles,
-                              chunk_cnt, chunk_base, ctrl, counts, seg_start, tiles, n_tiles,
-                              slot_token, slot_weight, st, sk.done1, split_counters(p))))
-    return rc;
-  stage_mark(2, st);
-  if ((rc = launch_route_scatter(x, T, nullptr, 0, ri, rw, T, k, E, H, p.S ? T : 0, seg_start,
-                                 chunk_base, ctrl, route_slot, slot_token, slot_weight, xq, xsf,
-                                 nsm, st)))
-    return rc;
+  float* partials = reinterpret_cast<float*>(ws + p.off[15]);
+  const long long partials_bytes = p.off[16] - p.off[15];
+  stage_mark(0, st);
+  // decode batches of up to 8 tokens with the tensor-core gate: the gate's
+  // split-K partial logits, then top-k + route plan + scatter in one kernel
+  const long long fused_need = gate_partials_bytes(T, H, E, nsm, true, true);
+  if (!rw && T <= 8 && tc_gate_ok(x, L->gate_w, L->gate_w_fp32, H, E) && fused_need > 0 &&
+      partials_bytes >= fused_need && small_route_fused_enabled()) {
+    int bm, ks;
+    gate_gemm_split_shape(T, H, E, nsm, &bm, &ks);
+    if ((rc = launch_gate_gemm_partials(x, L->gate_w, T, H, E, partials, nsm, st))) return rc;
+    stage_mark(1, st);
+    if ((rc = launch_route_small_fused(partials, ks, logits, L->gate_bias, T, E, k, L->route_scale, weights,
+                                       indices, x, H, p.S ? T : 0, p.block_n, p.max_rows, p.max_tiles, chunk_base,
+                                       counts, seg_start, tiles, n_tiles, slot_token, slot_weight, ctrl, sk.done1,
+                                       split_counters(p), route_slot, xq, xsf, st)))
+      return rc;
+    rw = weights;
+    ri = indices;
+    stage_mark(2, st);
+  } else {
+    if (!rw) {
+      if ((rc = gate_route(x, L->gate_w, L->gate_w_fp32, L->gate_bias, T, H, E, k, L->route_scale,
+                           logits, weights, indices, partials, partials_bytes, nsm, st)))
+        return rc;
+      rw = weights;
+      ri = indices;
+    }
+    stage_mark(1, st);
+    if ((rc = launch_route_plan(ri, T, k, E, 0, p.S ? T : 0, p.block_n, p.max_rows, p.max_tiles,
+                                chunk_cnt, chunk_base, ctrl, counts, seg_start, tiles, n_tiles,
+                                slot_token, slot_weight, st, sk.done1, split_counters(p))))
+      return rc;
+    stage_mark(2, st);
+    if ((rc = launch_route_scatter(x, T, nullptr, 0, ri, rw, T, k, E, H, p.S ? T : 0, seg_start,
+                                   chunk_base, ctrl, route_slot, slot_token, slot_weight, xq, xsf,
+                                   nsm, st)))
+      return rc;
+  }
   uint8_t* xq4 = p.fp4 ? ws + p.off[21] : nullptr;
   uint8_t* xsf4 = p.fp4 ? ws + p.off[22] : nullptr;
   if (p.fp4 && (rc = launch_fp4_permute_quant(x, T, H, slot_token, seg_start + (E + p.S), p.max_rows, xq4,

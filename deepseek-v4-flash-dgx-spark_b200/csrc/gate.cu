@@ -130,66 +130,28 @@ constexpr int kMaxExpertsPerLane = 16;  // E <= 512
 constexpr int kMaxTopk = 8;
 constexpr int kSliceBatch = 8;  // split-K slices loaded together
 
-// With nsplit > 1, `logits` holds nsplit partial slices [nsplit][T][E] that are
-// summed in slice order (fp32) and the sums are written to logits_out.
-__global__ void __launch_bounds__(512) gate_topk_kernel(const float* __restrict__ logits,
-                                                        int nsplit, float* __restrict__ logits_out,
-                                                        const float* __restrict__ bias, int T,
-                                                        int E, int k, float route_scale,
-                                                        float* __restrict__ weights,
-                                                        int64_t* __restrict__ indices,
-                                                        const int64_t* __restrict__ hash_table,
-                                                        const int64_t* __restrict__ input_ids,
-                                                        long long vocab) {
-  // One CTA per token, one thread per expert: each thread sums its expert's
-  // split-K slices in slice order (loads issued kSliceBatch at a time so they
-  // are in flight together), then warp 0 selects the top k from shared memory.
-  __shared__ float s_score[kMaxExpertsPerLane * 32], s_sel[kMaxExpertsPerLane * 32];
-  const int t = blockIdx.x;
-  const int lane = threadIdx.x & 31;
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    const float* src = logits + (size_t)t * E + e;
-    const size_t slice = (size_t)T * E;
-    float lg = src[0];
-    for (int sl0 = 1; sl0 < nsplit; sl0 += kSliceBatch) {
-      float v[kSliceBatch];
+// The logit at src from nsplit split-K partial slices `slice` floats apart,
+// summed in slice order in fp32 (loads issued kSliceBatch at a time).
+__device__ __forceinline__ float sum_slices(const float* src, int nsplit, size_t slice) {
+  float lg = src[0];
+  for (int sl0 = 1; sl0 < nsplit; sl0 += kSliceBatch) {
+    float v[kSliceBatch];
 #pragma unroll
-      for (int j = 0; j < kSliceBatch; ++j) v[j] = sl0 + j < nsplit ? src[(size_t)(sl0 + j) * slice] : 0.f;
+    for (int j = 0; j < kSliceBatch; ++j) v[j] = sl0 + j < nsplit ? src[(size_t)(sl0 + j) * slice] : 0.f;
 #pragma unroll
-      for (int j = 0; j < kSliceBatch; ++j)
-        if (sl0 + j < nsplit) lg = __fadd_rn(lg, v[j]);
-    }
-    if (logits_out) logits_out[(size_t)t * E + e] = lg;
-    const float s = sigmoid_canonical(lg);
-    s_score[e] = s;
-    s_sel[e] = bias ? __fadd_rn(s, bias[e]) : s;
+    for (int j = 0; j < kSliceBatch; ++j)
+      if (sl0 + j < nsplit) lg = __fadd_rn(lg, v[j]);
   }
-  __syncthreads();
-  if (threadIdx.x >= 32) return;
-  if (hash_table) {
-    // hash-routed layer: the experts are the table row of the token id (rank
-    // order of the row), the weights their scores renormalised in that order
-    const long long id = input_ids[t];
-    int e = -1;
-    if (lane < k) {
-      if (id >= 0 && id < vocab) {
-        const int64_t v = hash_table[id * k + lane];
-        if (v >= 0 && v < E) e = static_cast<int>(v);
-      }
-      if (e < 0) record_error(DSV4_DEVERR_BAD_INDEX);
-    }
-    const float w = e >= 0 ? s_score[e] : 0.f;
-    float total = 0.f;
-    for (int r = 0; r < k; ++r) {
-      const float wr = __shfl_sync(0xffffffffu, w, r);
-      total = (r == 0) ? wr : __fadd_rn(total, wr);
-    }
-    if (lane < k) {
-      weights[(size_t)t * k + lane] = e >= 0 ? __fmul_rn(__fdiv_rn(w, total), route_scale) : 0.f;
-      indices[(size_t)t * k + lane] = e;
-    }
-    return;
-  }
+  return lg;
+}
+
+// Top-k of one token by one warp, from its sigmoid scores (s_score) and
+// selection values (s_sel = score + bias) in shared memory: k rounds of a warp
+// arg-max on s_sel, ties to the lower expert id; lane r < k gets the rank-r
+// expert and its weight (its score over the sum of the k picked scores, summed
+// in rank order, times route_scale).
+__device__ __forceinline__ void warp_topk(const float* s_score, const float* s_sel, int E, int k,
+                                          float route_scale, int lane, float* w_out, int* e_out) {
   float score[kMaxExpertsPerLane], sel[kMaxExpertsPerLane];
   const int per = (E + 31) / 32;
 #pragma unroll
@@ -244,11 +206,68 @@ __global__ void __launch_bounds__(512) gate_topk_kernel(const float* __restrict_
       my_e = best_e;
     }
   }
+  float w = 0.f;
+  if (lane < k) w = __fmul_rn(__fdiv_rn(my_w, total), route_scale);
+  *w_out = w;
+  *e_out = my_e;
+}
+
+// With nsplit > 1, `logits` holds nsplit partial slices [nsplit][T][E] that are
+// summed in slice order (fp32) and the sums are written to logits_out.
+__global__ void __launch_bounds__(512) gate_topk_kernel(const float* __restrict__ logits,
+                                                        int nsplit, float* __restrict__ logits_out,
+                                                        const float* __restrict__ bias, int T,
+                                                        int E, int k, float route_scale,
+                                                        float* __restrict__ weights,
+                                                        int64_t* __restrict__ indices,
+                                                        const int64_t* __restrict__ hash_table,
+                                                        const int64_t* __restrict__ input_ids,
+                                                        long long vocab) {
+  // One CTA per token, one thread per expert: each thread sums its expert's
+  // split-K slices in slice order (loads issued kSliceBatch at a time so they
+  // are in flight together), then warp 0 selects the top k from shared memory.
+  __shared__ float s_score[kMaxExpertsPerLane * 32], s_sel[kMaxExpertsPerLane * 32];
+  const int t = blockIdx.x;
+  const int lane = threadIdx.x & 31;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const float lg = sum_slices(logits + (size_t)t * E + e, nsplit, (size_t)T * E);
+    if (logits_out) logits_out[(size_t)t * E + e] = lg;
+    const float s = sigmoid_canonical(lg);
+    s_score[e] = s;
+    s_sel[e] = bias ? __fadd_rn(s, bias[e]) : s;
+  }
+  __syncthreads();
+  if (threadIdx.x >= 32) return;
+  if (hash_table) {
+    // hash-routed layer: the experts are the table row of the token id (rank
+    // order of the row), the weights their scores renormalised in that order
+    const long long id = input_ids[t];
+    int e = -1;
+    if (lane < k) {
+      if (id >= 0 && id < vocab) {
+        const int64_t v = hash_table[id * k + lane];
+        if (v >= 0 && v < E) e = static_cast<int>(v);
+      }
+      if (e < 0) record_error(DSV4_DEVERR_BAD_INDEX);
+    }
+    const float w = e >= 0 ? s_score[e] : 0.f;
+    float total = 0.f;
+    for (int r = 0; r < k; ++r) {
+      const float wr = __shfl_sync(0xffffffffu, w, r);
+      total = (r == 0) ? wr : __fadd_rn(total, wr);
+    }
+    if (lane < k) {
+      weights[(size_t)t * k + lane] = e >= 0 ? __fmul_rn(__fdiv_rn(w, total), route_scale) : 0.f;
+      indices[(size_t)t * k + lane] = e;
+    }
+    return;
+  }
+  float w;
+  int e;
+  warp_topk(s_score, s_sel, E, k, route_scale, lane, &w, &e);
   if (lane < k) {
-    float w = __fdiv_rn(my_w, total);
-    w = __fmul_rn(w, route_scale);
     weights[(size_t)t * k + lane] = w;
-    indices[(size_t)t * k + lane] = my_e;
+    indices[(size_t)t * k + lane] = e;
   }
 }
 

@@ -71,6 +71,14 @@ int launch_single_segment_plan(int T, int seg, int block_n, int rows_pad, const 
                                int* total_rows, cudaStream_t st);
 int launch_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* s, int num_sms,
                      cudaStream_t st);
+// Decode batches (T <= 8): gate top-k from split-K partial logits + route plan
+// + scatter/act_quant in one launch.
+int launch_route_small_fused(const float* partials, int nsplit, float* logits_out, const float* bias, int T, int E,
+                             int k, float route_scale, float* weights, int64_t* indices, const void* x, int H,
+                             int shared_rows, int block_n, int max_rows, int max_tiles, int* chunk_base, int* counts,
+                             int* seg_start, int4* tiles, int* n_tiles, int* slot_token, float* slot_weight,
+                             int* ctrl, int* zero_ptr, int n_zero, int* route_slot, uint8_t* xq, uint8_t* sfb,
+                             cudaStream_t st);
 int launch_fp4_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* s, int num_sms, cudaStream_t st);
 int launch_fp4_permute_quant(const void* x, int T, int H, const int* slot_token, const int* total_rows_ptr,
                              int max_rows, uint8_t* xq4, uint8_t* atoms, int num_sms, cudaStream_t st);

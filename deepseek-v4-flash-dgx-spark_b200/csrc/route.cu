@@ -357,6 +357,132 @@ __global__ void __launch_bounds__(256) route_scatter_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// Decode batches of at most kFusedMaxTokens tokens: the gate's top-k (from the
+// split-K partial logits), the route plan and the scatter + act_quant in one
+// CTA, with the same results as gate_topk_kernel + route_plan_small_kernel +
+// route_scatter_kernel (one chunk): the three launches and their round trips
+// through global memory become one.
+// ---------------------------------------------------------------------------
+constexpr int kFusedMaxTokens = 8;
+constexpr int kFusedMaxExperts = 512;
+
+__global__ void __launch_bounds__(512) route_small_fused_kernel(
+    const float* __restrict__ partials, int nsplit, float* __restrict__ logits_out, const float* __restrict__ bias,
+    int T, int E, int k, float route_scale, float* __restrict__ weights, int64_t* __restrict__ indices,
+    const __nv_bfloat16* __restrict__ x, int H, int shared_rows, int block_n, int max_rows, int max_tiles,
+    int* __restrict__ chunk_base, int* __restrict__ counts, int* __restrict__ seg_start, int4* __restrict__ tiles,
+    int* __restrict__ n_tiles, int* __restrict__ slot_token, float* __restrict__ slot_weight,
+    int* __restrict__ ctrl, int* __restrict__ zero_ptr, int n_zero, int* __restrict__ route_slot,
+    uint8_t* __restrict__ xq, uint8_t* __restrict__ sfb) {
+  __shared__ float s_score[kFusedMaxTokens * kFusedMaxExperts], s_sel[kFusedMaxTokens * kFusedMaxExperts];
+  __shared__ int cnt[kFusedMaxExperts];
+  __shared__ int s_cnt[kMaxSegments], s_start[kMaxSegments + 1], s_tbase[kMaxSegments + 1];
+  __shared__ int s_e[kFusedMaxTokens * kMaxK];
+  __shared__ float s_w[kFusedMaxTokens * kMaxK];
+  __shared__ int s_slot[kFusedMaxTokens][kMaxK + 1];
+  __shared__ int s_bad;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) s_bad = 0;
+  // scores of every (token, expert): a thread takes kFusedPairs pairs a
+  // block apart and keeps all their slice loads in flight together; each
+  // logit still adds its slices in slice order (as sum_slices does)
+  constexpr int kFusedPairs = 4;
+  const size_t slice = (size_t)T * E;
+  const int n_pairs = T * E;
+  for (int i0 = tid; i0 < n_pairs; i0 += blockDim.x * kFusedPairs) {
+    float acc[kFusedPairs];
+#pragma unroll
+    for (int p = 0; p < kFusedPairs; ++p) {
+      const int i = i0 + p * blockDim.x;
+      acc[p] = i < n_pairs ? partials[i] : 0.f;
+    }
+    for (int sl0 = 1; sl0 < nsplit; sl0 += kSliceBatch) {
+      float v[kFusedPairs][kSliceBatch];
+#pragma unroll
+      for (int p = 0; p < kFusedPairs; ++p) {
+        const int i = i0 + p * blockDim.x;
+#pragma unroll
+        for (int j = 0; j < kSliceBatch; ++j)
+          v[p][j] = (i < n_pairs && sl0 + j < nsplit) ? partials[i + (size_t)(sl0 + j) * slice] : 0.f;
+      }
+#pragma unroll
+      for (int p = 0; p < kFusedPairs; ++p)
+#pragma unroll
+        for (int j = 0; j < kSliceBatch; ++j)
+          if (sl0 + j < nsplit) acc[p] = __fadd_rn(acc[p], v[p][j]);
+    }
+#pragma unroll
+    for (int p = 0; p < kFusedPairs; ++p) {
+      const int i = i0 + p * blockDim.x;
+      if (i >= n_pairs) continue;
+      const int t = i / E, e = i % E;
+      logits_out[i] = acc[p];
+      const float sc = sigmoid_canonical(acc[p]);
+      s_score[t * kFusedMaxExperts + e] = sc;
+      s_sel[t * kFusedMaxExperts + e] = bias ? __fadd_rn(sc, bias[e]) : sc;
+    }
+  }
+  for (int e = tid; e < E; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  // top-k: warp t takes token t
+  if (warp < T) {
+    float w;
+    int e;
+    warp_topk(s_score + warp * kFusedMaxExperts, s_sel + warp * kFusedMaxExperts, E, k, route_scale, lane, &w, &e);
+    if (lane < k) {
+      weights[(size_t)warp * k + lane] = w;
+      indices[(size_t)warp * k + lane] = e;
+      s_e[warp * k + lane] = e;
+      s_w[warp * k + lane] = w;
+      if (e >= 0 && e < E)
+        atomicAdd(&cnt[e], 1);
+      else
+        s_bad = 1;  // no finite selection value (NaN logits): the plan fails as the separate kernels' does
+    }
+  }
+  __syncthreads();
+  // plan (one chunk: every chunk offset is 0)
+  for (int e = tid; e < E; e += blockDim.x) {
+    chunk_base[e] = 0;
+    s_cnt[e] = cnt[e];
+  }
+  if (tid == 0) s_cnt[E] = shared_rows;
+  plan_layout(s_cnt, s_start, s_tbase, E + 1, block_n, max_rows, max_tiles, s_bad, counts, seg_start, tiles,
+              n_tiles, slot_token, slot_weight, ctrl, zero_ptr, n_zero);
+  __syncthreads();
+  if (__ldcg(ctrl + 2)) return;
+  // slots: route i of expert e goes to seg_start[e] + (its rank among e's routes, in route order)
+  const int nr = T * k;
+  if (tid < nr) {
+    const int e = s_e[tid];
+    int rank = 0;
+    for (int j = 0; j < tid; ++j) rank += s_e[j] == e;
+    const int slot = s_start[e] + rank;
+    slot_token[slot] = tid / k;
+    slot_weight[slot] = s_w[tid];
+    route_slot[tid] = slot;
+    s_slot[tid / k][tid % k] = slot;
+  }
+  if (tid < T) {
+    int slot = -1;
+    if (tid < shared_rows) {
+      slot = s_start[E] + tid;
+      slot_token[slot] = tid;
+      slot_weight[slot] = 1.0f;
+    }
+    s_slot[tid][k] = slot;
+  }
+  __syncthreads();
+  // quantize every token once and write its k + 1 rows: warps take (token,
+  // pair of 512-wide quads) units
+  const int KT = H / 128, KQ = KT / 4, units_per_token = (KQ + 1) / 2;
+  for (int u = warp; u < T * units_per_token; u += blockDim.x / 32) {
+    const int t = u / units_per_token, q0 = (u % units_per_token) * 2;
+    scatter_row(x + (size_t)t * H, nullptr, q0, min(KQ, q0 + 2), KT, H, s_slot[t], k + 1, lane, xq, sfb);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Per-128 act_quant of k tiles [kt_begin, kt_end) of one row by one warp into a
 // single destination row (the expert forward's identity plan, the linear layer
 // and the plain act_quant entry point).
@@ -606,6 +732,21 @@ int launch_route_plan(const int64_t* indices, int T, int k, int E, int allow_ski
                                                 max_rows, max_tiles, chunk_base, counts, seg_start,
                                                 tiles, n_tiles, slot_token, slot_weight, ctrl, zero_ptr,
                                                 n_zero);
+  return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
+}
+
+int launch_route_small_fused(const float* partials, int nsplit, float* logits_out, const float* bias, int T, int E,
+                             int k, float route_scale, float* weights, int64_t* indices, const void* x, int H,
+                             int shared_rows, int block_n, int max_rows, int max_tiles, int* chunk_base, int* counts,
+                             int* seg_start, int4* tiles, int* n_tiles, int* slot_token, float* slot_weight,
+                             int* ctrl, int* zero_ptr, int n_zero, int* route_slot, uint8_t* xq, uint8_t* sfb,
+                             cudaStream_t st) {
+  if (T <= 0 || T > kFusedMaxTokens || k > kMaxK || E > kFusedMaxExperts || E + 1 > kMaxSegments || H % 512)
+    return DSV4_ERR_ARG;
+  launch_k(route_small_fused_kernel, 1, 512, 0, st, partials, nsplit, logits_out, bias, T, E, k, route_scale,
+           weights, indices, static_cast<const __nv_bfloat16*>(x), H, shared_rows, block_n, max_rows, max_tiles,
+           chunk_base, counts, seg_start, tiles, n_tiles, slot_token, slot_weight, ctrl, zero_ptr, n_zero,
+           route_slot, xq, sfb);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
 

@@ -82,6 +82,7 @@ _SIGNATURES = {
     "dsv4_set_k_split": (c_int, [c_int]),
     "dsv4_set_fp4_activations": (c_int, [c_int]),
     "dsv4_settings_generation": (c_ll, []),
+    "dsv4_set_fused_routing": (c_int, [c_int]),
     "dsv4_fp4_act_quant": (c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_vp]),
     "dsv4_fp8_weight_atoms_bytes": (c_ll, [c_int, c_int]),
     "dsv4_build_fp8_weight_atoms": (c_int, [c_vp, c_int, c_int, c_vp, c_vp]),

@@ -78,7 +78,13 @@ DSV4_API int dsv4_set_k_split(int slices);
  * dsv4_moe_workspace_bytes: set it before sizing workspaces.
  * dsv4_moe_workspace_layout's out[20] says whether a layout uses it. */
 DSV4_API int dsv4_set_fp4_activations(int on);
-/* A counter that every call of dsv4_set_k_split / dsv4_set_fp4_activations
+/* Decode batches of at most 8 tokens with the tensor-core gate: run the
+ * gate's top-k, the route plan and the scatter as one kernel (1) instead of
+ * three (0, the default).  Bit-identical results; measured no faster inside a
+ * CUDA graph.  No counterpart in the reference. */
+DSV4_API int dsv4_set_fused_routing(int on);
+/* A counter that every call of dsv4_set_k_split / dsv4_set_fp4_activations /
+ * dsv4_set_fused_routing
  * advances: a caller that captured CUDA graphs of the layer recaptures when it
  * changes (the settings choose the kernels a graph holds). */
 DSV4_API long long dsv4_settings_generation(void);

@@ -339,6 +339,57 @@ def test_moe_module_forward_shape_and_dtype(cuda_device):
     assert w.shape == (6, cfg.topk) and idx.dtype == torch.int64
 
 
+@pytest.mark.parametrize("T", [1, 3, 8])
+def test_fused_small_batch_routing_equals_the_separate_kernels(cuda_device, T):
+    """With dsv4_set_fused_routing(1), at T <= 8 the layer's own gate runs as
+    split-K partials + one fused top-k / plan / scatter kernel.  Fed its
+    routing back (which takes the separate plan and scatter kernels), the
+    layer gives the same bits: output, counts, segments, tiles, every route's
+    slot and the quantized rows."""
+    from spark_b200.synthetic import CONFIGS, build_moe, make_layer
+
+    cfg = CONFIGS["decode"].with_tokens(T)
+    layer = make_layer(cfg, seed=40 + T, device="cpu")
+    moe = build_moe(layer, device=cuda_device)
+    x = layer["x"].to(cuda_device)
+    nb = moe.workspace_bytes(T)
+    ws1 = torch.zeros(nb, dtype=torch.uint8, device=cuda_device)
+    ws2 = torch.zeros(nb, dtype=torch.uint8, device=cuda_device)
+    L = _lib()
+    L.check(L.load().dsv4_set_fused_routing(1), "dsv4_set_fused_routing")
+    try:
+        y1 = moe.forward_tokens(x, workspace=ws1)
+        torch.cuda.synchronize()
+    finally:
+        L.check(L.load().dsv4_set_fused_routing(0), "dsv4_set_fused_routing")
+    offs = _layer_ws(moe, T)
+    k, E, H = cfg.topk, cfg.n_routed, cfg.dim
+    w = ws1[offs[1]:offs[1] + T * k * 4].view(torch.float32).view(T, k).clone()
+    i = ws1[offs[2]:offs[2] + T * k * 8].view(torch.int64).view(T, k).clone()
+    y2 = moe.forward_tokens(x, routing=(w, i), workspace=ws2)
+    torch.cuda.synchronize()
+    _no_device_error()
+    assert torch.equal(y1, y2)
+
+    def ints(ws, o, n):
+        return ws[offs[o]:offs[o] + 4 * n].view(torch.int32).cpu().numpy()
+
+    for o, n in ((3, E + 1), (4, E + 2), (5, 1), (6, T * k)):
+        assert np.array_equal(ints(ws1, o, n), ints(ws2, o, n)), o
+    rows = int(ints(ws1, 4, E + 2)[E + 1])
+    assert np.array_equal(ints(ws1, 7, rows), ints(ws2, 7, rows))
+    nt = int(ints(ws1, 5, 1)[0])
+    assert np.array_equal(ints(ws1, 9, 4 * nt), ints(ws2, 9, 4 * nt))
+    tok = ints(ws1, 7, rows)
+    valid = np.nonzero(tok >= 0)[0]
+    xq1 = ws1[offs[10]:offs[10] + rows * H].view(rows, H).cpu().numpy()
+    xq2 = ws2[offs[10]:offs[10] + rows * H].view(rows, H).cpu().numpy()
+    assert np.array_equal(xq1[valid], xq2[valid])
+    y_ref = O.moe_forward(layer["x"].float().numpy(), _oracle_weights(layer, sorted(set(i.cpu().reshape(-1).tolist()))),
+                          routing=(w.cpu().numpy(), i.cpu().numpy()), workers=_WORKERS)[0]
+    assert _rel_err(_bf16_np(y1), y_ref) <= TOL
+
+
 def test_module_forward_graph_replay_equals_the_eager_layer(cuda_device):
     """MoE.forward replays a captured graph per token count: every call,
     the capturing one included, equals the eager C ABI layer bit for bit; a
