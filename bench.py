@@ -1017,12 +1017,12 @@ def _prefill_roofline(moe, layer, ws, y, flush, cfg, T):
 
 def _prefill_fp4(args, dev, flush, T=8192, sample=16):
     """The prefill layer in the opt-in FP4-activation mode
-    (dsv4_set_fp4_activations): the routed experts' w1 | w3 as kind::mxf4
-    products on FP4 activations, everything else as in the default layer.
-    Time: the graph-replayed layer (median of 10, L2 flushed between), and the
-    expert GEMMs' stage time against their mixed roofline (routed w1 | w3
-    FLOPs at the FP4 rate, shared w1 | w3 and every w2 at the FP8 rate, both
-    scaled from the measured bf16 peak).  Outside the timings: the first
+    (dsv4_set_fp4_activations): the routed experts' w1 | w3 and w2 as
+    kind::mxf4 products on FP4 activations (x and h quantized per 32), the
+    shared expert as in the default layer.  Time: the graph-replayed layer
+    (median of 10, L2 flushed between), and the expert GEMMs' stage time
+    against their mixed roofline (routed FLOPs at the FP4 rate, the shared
+    expert's at the FP8 rate, both scaled from the measured bf16 peak).  Outside the timings: the first
     `sample` tokens against the oracle run in the same mode (the bar) and
     against the default e4m3 oracle (how far the mode moves the layer)."""
     import numpy as np
@@ -1063,8 +1063,8 @@ def _prefill_fp4(args, dev, flush, T=8192, sample=16):
         w_dev = ws[offs[1]:offs[1] + T * k * 4].view(torch.float32).view(T, k)
         i_dev = ws[offs[2]:offs[2] + T * k * 8].view(torch.int64).view(T, k)
         routes = int((i_dev >= 0).sum())
-        f_fp4 = 2.0 * routes * 2 * H * I               # routed w1 | w3
-        f_fp8 = 2.0 * T * 2 * H * I + 2.0 * (routes + T) * H * I   # shared w1 | w3, every w2
+        f_fp4 = 2.0 * routes * 3 * H * I               # routed w1 | w3 and w2
+        f_fp8 = 2.0 * T * 3 * H * I                    # the shared expert
         peaks, src = _peaks()
         bf16 = peaks.get("bf16_tflops", 1590.0)
         ideal_ms = (f_fp4 / (4 * bf16 * 1e12) + f_fp8 / (2 * bf16 * 1e12)) * 1e3
@@ -1097,8 +1097,8 @@ def _prefill_fp4(args, dev, flush, T=8192, sample=16):
                        "ok": bool(rel(yn, r4) <= 2e-2),
                        "deviation_from_e4m3_layer": {"max_of_rms": round(rel(yn, r8), 4),
                                                      "rms_of_rms": round(rel(yn, r8, rms=True), 4)}},
-            "numerics": "routed w1 | w3 on fp4_act_quant(x, 32) activations (e2m1, per-32 ue8m0); "
-                        "the reference's layer uses act_quant(x, 128) e4m3"}
+            "numerics": "routed experts on fp4_act_quant(., 32) activations (x before w1 | w3, h before w2; e2m1, "
+                        "per-32 ue8m0); the reference's layer uses act_quant(., 128) e4m3"}
     finally:
         _lib.check(lib.dsv4_set_fp4_activations(0), "dsv4_set_fp4_activations")
         torch.cuda.empty_cache()

@@ -112,7 +112,7 @@ struct Plan {
   int split1, split2;  // split-K slices of GEMM1 / GEMM2 (1 = none)
   int part_rows;       // compact rows of the split-K partial sums
   bool fp4;            // routed GEMM1 on FP4 activations (dsv4_set_fp4_activations)
-  long long off[23];
+  long long off[25];
   long long total;
 };
 
@@ -250,11 +250,12 @@ static Plan make_plan(const dsv4_moe_layer* L, int T, int E_local = -1) {
   p.split2 = choose_k_split(T, p.k, p.E, p.block_n, nb2, p.I / 128, nsm);
   p.part_rows = T * p.k + T * p.S;
   // single-GPU layer only; the CTA-pair form and split-K keep e4m3 activations
-  p.fp4 = E_local < 0 && L->arena != nullptr && fp4_act_setting() == 1 && p.block_n != 256 && p.H % 256 == 0;
-  if (p.fp4) p.split1 = 1;
+  p.fp4 = E_local < 0 && L->arena != nullptr && fp4_act_setting() == 1 && p.block_n != 256 && p.H % 256 == 0 &&
+          p.I % 256 == 0;
+  if (p.fp4) p.split1 = p.split2 = 1;
   const int smax = p.split1 > p.split2 ? p.split1 : p.split2;
   const long long part_ld = (long long)(nb1 * 256 > nb2 * 256 ? nb1 * 256 : nb2 * 256);
-  long long sz[23] = {
+  long long sz[25] = {
       (long long)T * (p.E > p.k ? p.E : p.k) * 4,  // logits (expert parallel: return rows)
       (long long)T * p.k * 4,                 // weights
       (long long)T * p.k * 8,                 // indices
@@ -280,9 +281,11 @@ static Plan make_plan(const dsv4_moe_layer* L, int T, int E_local = -1) {
       smax > 1 ? (long long)p.max_tiles * (nb1 + nb2) * 4 : 0,     // split-K item counters
       p.fp4 ? (long long)p.max_rows * (p.H / 2) : 0,                // FP4 activation codes
       p.fp4 ? atom_groups * (p.H / 128) * 512 : 0,                  // their per-32 scale atoms
+      p.fp4 ? (long long)p.max_rows * (p.I / 2) : 0,                // FP4 h codes
+      p.fp4 ? atom_groups * (p.I / 128) * 512 : 0,                  // their per-32 scale atoms
   };
   long long o = 0;
-  for (int i = 0; i < 23; ++i) {
+  for (int i = 0; i < 25; ++i) {
     p.off[i] = o;
     o += align256(sz[i]);
   }
@@ -340,7 +343,11 @@ static int run_expert_gemms(const dsv4_moe_layer* L, const int4* tiles, const in
                             uint8_t* hq, uint8_t* hsf, __nv_bfloat16* out_bf16, int out_ld,
                             int max_rows, int max_tiles, int block_n, const int* expert_slot,
                             int n_routed, int nsm, cudaStream_t st, const SplitK& sk = SplitK(),
-                            const uint8_t* xq4 = nullptr, const uint8_t* xsf4 = nullptr) {
+                            const uint8_t* xq4 = nullptr, const uint8_t* xsf4 = nullptr,
+                            uint8_t* hq4 = nullptr, uint8_t* hsf4 = nullptr) {
+  // xq4 != nullptr (FP4-activation mode): the routed experts' rows take FP4
+  // activations through both GEMMs (x -> xq4 before GEMM1, h -> hq4 in GEMM1's
+  // epilogue); the shared expert's rows keep e4m3 (xq -> hq) on the e4m3 kernel.
   const int H = L->hidden, I = L->inter;
   const bool has_shared = L->shared_w1 != nullptr;
   const bool has_routed = L->arena != nullptr;
@@ -426,11 +433,13 @@ static int run_expert_gemms(const dsv4_moe_layer* L, const int4* tiles, const in
     GemmArgs g4 = g1;
     g4.kt_count = H / 256;
     g4.sfb = xsf4;
+    g4.out_q = hq4;
+    g4.out_sf = hsf4;
     g4.k_split = 1;
     g4.seg_filter = 1;
     const long long work1 = (long long)max_tiles * g1.nb_count;
     const int grid1 = (int)(work1 < nsm ? work1 : nsm);
-    if ((rc = launch_expert_gemm_fp4(block_n, p0, p1, bx, g4, grid1, st))) return rc;
+    if ((rc = launch_expert_gemm_fp4(true, block_n, p0, p1, bx, g4, grid1, st))) return rc;
     if (has_shared) {
       GemmArgs gs = g1;
       gs.k_split = 1;
@@ -483,6 +492,27 @@ static int run_expert_gemms(const dsv4_moe_layer* L, const int4* tiles, const in
     if (work < clusters2) clusters2 = (int)(work > 0 ? work : 1);
     rc = launch_expert_gemm_pair(false, pm, g2, (2 * sc) >> 8, (2 * sc) >> 8, (2 * sc) >> 8,
                                  (2 * sc) >> 8, clusters2, st);
+  } else if (xq4 && has_routed) {
+    // FP4 activations: the routed items on kind::mxf4 over hq4, then the
+    // shared expert's items on the e4m3 kernel over hq
+    CUtensorMap p2, bh;
+    if ((rc = make_tmap_fp4_packed_arena(&p2, L->arena + w2_off, I, H, L->n_slots, L->slot_stride, gemm_l2promo())))
+      return rc;
+    if ((rc = make_tmap_u8(&bh, hq4, I / 2, max_rows, block_n))) return rc;
+    GemmArgs g5 = g2;
+    g5.kt_count = I / 256;
+    g5.sfb = hsf4;
+    g5.k_split = 1;
+    g5.seg_filter = 1;
+    const long long work2 = (long long)max_tiles * g2.nb_count;
+    const int grid2 = (int)(work2 < nsm ? work2 : nsm);
+    if ((rc = launch_expert_gemm_fp4(false, block_n, p2, p2, bh, g5, grid2, st))) return rc;
+    if (has_shared) {
+      GemmArgs gs = g2;
+      gs.k_split = 1;
+      gs.seg_filter = 2;
+      rc = launch_expert_gemm(false, block_n, a0, a0, s0, s0, b, gs, grid2, st);
+    }
   } else {
     const long long work2 = (long long)max_tiles * g2.nb_count * g2.k_split;
     const int grid2 = (int)(work2 < nsm ? work2 : nsm);
@@ -802,8 +832,11 @@ int dsv4_moe_forward(const dsv4_moe_layer* L, const void* x, int T, void* y,
     return rc;
   stage_mark(3, st);
 
+  uint8_t* hq4 = p.fp4 ? ws + p.off[23] : nullptr;
+  uint8_t* hsf4 = p.fp4 ? ws + p.off[24] : nullptr;
   if ((rc = run_expert_gemms(L, tiles, n_tiles, slot_weight, xq, xsf, hq, hsf, O, H, p.max_rows,
-                             p.max_tiles, p.block_n, L->expert_slot, L->n_routed, nsm, st, sk, xq4, xsf4)))
+                             p.max_tiles, p.block_n, L->expert_slot, L->n_routed, nsm, st, sk, xq4, xsf4, hq4,
+                             hsf4)))
     return rc;
   rc = launch_combine(O, H, route_slot, ri, T, k, p.S ? seg_start + E : nullptr, y, st);
   stage_mark(6, st);

@@ -70,7 +70,6 @@ struct GemmCfg {
   static constexpr int SFB_COL = 264;
   static constexpr int TMEM_COLS = 512;
   static constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + SF_RING + CTRL_BYTES;
-  static_assert(!FP4A || GATED, "FP4 activations are GEMM1's");
   static_assert(A_BYTES % 1024 == 0, "tiles must keep 1024-byte alignment");
   // the M = 128 MMA reads 128 rows (16 KB) from the A base; they must stay in the stage
   static_assert(128 * 128 <= TILE_BYTES, "A window leaves the stage");
@@ -185,7 +184,7 @@ __device__ __forceinline__ void gemm_produce(const CUtensorMap* tmW0p, const CUt
         tma_load_2d(st, tmXp, &full[stage], kt * 128, cur.row0);
         uint8_t* b = st + C::A_BYTES;
         tma_load_3d(b, tmW0p, &full[stage], kt * 128, cur.r0, cur.slot);
-        tma_load_3d(b + C::B_HALF, tmW1p, &full[stage], kt * 128, cur.r1, cur.slot);
+        tma_load_3d(b + C::B_HALF, GATED ? tmW1p : tmW0p, &full[stage], kt * 128, cur.r1, cur.slot);
         uint8_t* sfs = st + C::TILE_BYTES;
         bulk_load(sfs, args.sfb + (g0 * KW + 2 * kt) * 512, 1024, &full[stage]);
         bulk_load(sfs + 1024, cur.sfb0 + (size_t)(2 * kt) * 512, 1024, &full[stage]);
@@ -460,10 +459,10 @@ __global__ void __launch_bounds__(192, 1)
             const uint32_t sfa_k = sfa_t + 24 * sf_set, sfb_k = sfa_k + 8;
             tc_cp_sf(sfa_k, sdesc_sf(smem_u32(sfs)));
             tc_cp_sf(sfa_k + 4, sdesc_sf(smem_u32(sfs + 512)));
-            tc_cp_sf(sfb_k, sdesc_sf(smem_u32(sfs + 1024)));       // w1 rows, window 0
-            tc_cp_sf(sfb_k + 8, sdesc_sf(smem_u32(sfs + 1536)));   // w1 rows, window 1
-            tc_cp_sf(sfb_k + 4, sdesc_sf(smem_u32(sfs + 2048)));   // w3 rows, window 0
-            tc_cp_sf(sfb_k + 12, sdesc_sf(smem_u32(sfs + 2560)));  // w3 rows, window 1
+            tc_cp_sf(sfb_k, sdesc_sf(smem_u32(sfs + 1024)));       // weight rows 0-127 (w1), window 0
+            tc_cp_sf(sfb_k + 8, sdesc_sf(smem_u32(sfs + 1536)));   // rows 0-127, window 1
+            tc_cp_sf(sfb_k + 4, sdesc_sf(smem_u32(sfs + 2048)));   // rows 128-255 (w3), window 0
+            tc_cp_sf(sfb_k + 12, sdesc_sf(smem_u32(sfs + 2560)));  // rows 128-255, window 1
             const uint64_t adesc = sdesc_k_sw128(smem_u32(st));
             const uint64_t bdesc = sdesc_k_sw128(smem_u32(st + C::A_BYTES));
 #pragma unroll
@@ -610,21 +609,44 @@ __global__ void __launch_bounds__(192, 1)
             amax = fmaxf(amax, fabsf(hv));
             pk[j] = __float_as_uint(hv);
           }
-          const int e = act_scale_exp(amax);
-          const float inv = exp2i(-e);
-          uint8_t* dst = args.out_q + (size_t)row * args.out_ld + jb * 128;
+          if constexpr (FP4A) {
+            // FP4 h for the FP4 GEMM2: four 32-value blocks (fp4_act_quant
+            // semantics), 64 packed bytes per row of this 128-wide window jb,
+            // scale bytes into the per-32 atoms of window jb
+            (void)amax;
+            uint8_t* dst = args.out_q + (size_t)row * (args.out_ld / 2) + jb * 64;
+            const int KW = args.out_ld >> 7, g = row >> 5;
 #pragma unroll
-          for (int v = 0; v < 8; ++v) {
-            uint32_t wds[4];
+            for (int blk = 0; blk < 4; ++blk) {
+              float v32[32];
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              const float* f = reinterpret_cast<const float*>(&pk[16 * v + 4 * t]);
-              wds[t] = e4m3x4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv);
+              for (int i = 0; i < 32; ++i) v32[i] = __uint_as_float(pk[32 * blk + i]);
+              uint4 packed;
+              const int e4 = fp4_block_quant(v32, packed);
+              *reinterpret_cast<uint4*>(dst + 16 * blk) = packed;
+#pragma unroll
+              for (int m1 = 0; m1 < 4; ++m1)
+                if (g - m1 >= 0)
+                  args.out_sf[((size_t)(g - m1) * KW + jb) * 512 + (row & 31) * 16 + m1 * 4 + blk] =
+                      static_cast<uint8_t>(e4 + 127);
             }
-            *reinterpret_cast<uint4*>(dst + 16 * v) = make_uint4(wds[0], wds[1], wds[2], wds[3]);
+          } else {
+            const int e = act_scale_exp(amax);
+            const float inv = exp2i(-e);
+            uint8_t* dst = args.out_q + (size_t)row * args.out_ld + jb * 128;
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              uint32_t wds[4];
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                const float* f = reinterpret_cast<const float*>(&pk[16 * v + 4 * t]);
+                wds[t] = e4m3x4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv);
+              }
+              *reinterpret_cast<uint4*>(dst + 16 * v) = make_uint4(wds[0], wds[1], wds[2], wds[3]);
+            }
+            write_row_scale(args.out_sf, row, jb, (args.out_ld >> 7) >> 2,
+                            static_cast<uint8_t>(e + 127));
           }
-          write_row_scale(args.out_sf, row, jb, (args.out_ld >> 7) >> 2,
-                          static_cast<uint8_t>(e + 127));
         } else {
           uint4* dst = reinterpret_cast<uint4*>(args.out_bf16 + (size_t)row * args.out_ld + jb * 256);
 #pragma unroll
@@ -753,23 +775,31 @@ static int launch_one(const CUtensorMap& a0, const CUtensorMap& a1, const CUtens
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
 
-template <int BM>
+template <int BM, bool GATED>
 static int launch_one_fp4(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b, const GemmArgs& args,
                           int grid, cudaStream_t st) {
-  using C = GemmCfg<BM, true, true>;
-  if (ensure_smem_attr(reinterpret_cast<const void*>(expert_gemm_kernel<BM, true, true>), (int)C::SMEM_BYTES))
+  using C = GemmCfg<BM, GATED, true>;
+  if (ensure_smem_attr(reinterpret_cast<const void*>(expert_gemm_kernel<BM, GATED, true>), (int)C::SMEM_BYTES))
     return DSV4_ERR_CUDA;
-  launch_k(expert_gemm_kernel<BM, true, true>, grid, 192, C::SMEM_BYTES, st, a0, a1, a0, a1, b, args);
+  launch_k(expert_gemm_kernel<BM, GATED, true>, grid, 192, C::SMEM_BYTES, st, a0, a1, a0, a1, b, args);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
 
-int launch_expert_gemm_fp4(int block_n, const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b,
-                           const GemmArgs& args, int grid, cudaStream_t st) {
+int launch_expert_gemm_fp4(bool gated, int block_n, const CUtensorMap& a0, const CUtensorMap& a1,
+                           const CUtensorMap& b, const GemmArgs& args, int grid, cudaStream_t st) {
   if (args.seg_filter != 1 || args.k_split != 1) return DSV4_ERR_ARG;  // routed items, unsplit
+  if (gated) {
+    switch (block_n) {
+      case 32: return launch_one_fp4<32, true>(a0, a1, b, args, grid, st);
+      case 64: return launch_one_fp4<64, true>(a0, a1, b, args, grid, st);
+      case 128: return launch_one_fp4<128, true>(a0, a1, b, args, grid, st);
+      default: return DSV4_ERR_ARG;
+    }
+  }
   switch (block_n) {
-    case 32: return launch_one_fp4<32>(a0, a1, b, args, grid, st);
-    case 64: return launch_one_fp4<64>(a0, a1, b, args, grid, st);
-    case 128: return launch_one_fp4<128>(a0, a1, b, args, grid, st);
+    case 32: return launch_one_fp4<32, false>(a0, a1, b, args, grid, st);
+    case 64: return launch_one_fp4<64, false>(a0, a1, b, args, grid, st);
+    case 128: return launch_one_fp4<128, false>(a0, a1, b, args, grid, st);
     default: return DSV4_ERR_ARG;
   }
 }

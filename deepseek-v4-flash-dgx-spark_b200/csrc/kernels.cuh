@@ -139,10 +139,12 @@ int launch_expert_gemm_pair(bool gated, const PairMaps& maps, const GemmArgs& ar
 int launch_expert_gemm(bool gated, int block_n, const CUtensorMap& a0, const CUtensorMap& a1,
                        const CUtensorMap& s0, const CUtensorMap& s1, const CUtensorMap& b,
                        const GemmArgs& args, int grid, cudaStream_t st);
-// GEMM1 of the routed experts on FP4 activations (kind::mxf4): a0 / a1 packed
-// w1 / w3 arena maps, b the packed activation rows; args.kt_count = H / 256,
-// args.sfb the per-32 activation atoms.
-int launch_expert_gemm_fp4(int block_n, const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b,
-                           const GemmArgs& args, int grid, cudaStream_t st);
+// The routed experts' GEMMs on FP4 activations (kind::mxf4): gated = GEMM1
+// (a0 / a1 packed w1 / w3 arena maps; its epilogue writes FP4 h: packed codes
+// [rows][out_ld/2] + per-32 atoms), else GEMM2 (a0 the packed w2 map);
+// b the packed activation rows, args.kt_count = K / 256, args.sfb the per-32
+// activation atoms.
+int launch_expert_gemm_fp4(bool gated, int block_n, const CUtensorMap& a0, const CUtensorMap& a1,
+                           const CUtensorMap& b, const GemmArgs& args, int grid, cudaStream_t st);
 
 }  // namespace dsv4

@@ -408,20 +408,22 @@ def expert_forward(x_bf16: np.ndarray, ew: ExpertWeights, route_w: np.ndarray | 
     routing weight when given (applied before w2, in fp32); h is cast to bf16
     and fed through w2.  Returns bf16 values as fp32 [n, H].
 
-    fp4_act: x is quantized by fp4_act_quant (e2m1, per-32 scales) instead of
-    act_quant for w1 and w3 (the library's opt-in FP4-activation mode); the
-    products stay exact in float64 (e2m1 x e2m1 with power-of-two scales)."""
+    fp4_act: x and h are quantized by fp4_act_quant (e2m1, per-32 scales)
+    instead of act_quant for w1 / w3 and for w2 (the library's opt-in
+    FP4-activation mode); the products stay exact in float64 (e2m1 x e2m1
+    with power-of-two scales)."""
     if fp4_act:
         q, s = fp4_act_quant(x_bf16)
-        return expert_forward_dequant(fp4_act_dequant(q, s), ew, route_w, swiglu_limit, dense)
+        return expert_forward_dequant(fp4_act_dequant(q, s), ew, route_w, swiglu_limit, dense, fp4_h=True)
     q, s = act_quant(x_bf16)
     return expert_forward_dequant(act_dequant(q, s), ew, route_w, swiglu_limit, dense)
 
 
 def expert_forward_dequant(a: np.ndarray, ew: ExpertWeights, route_w: np.ndarray | None,
-                           swiglu_limit: float, dense=None) -> np.ndarray:
+                           swiglu_limit: float, dense=None, fp4_h: bool = False) -> np.ndarray:
     """``expert_forward`` from the dequantized act_quant of its input (the form
-    in which an expert-parallel rank receives the rows)."""
+    in which an expert-parallel rank receives the rows).  fp4_h: h goes through
+    fp4_act_quant (per 32) instead of act_quant before w2."""
     w1, w2, w3 = dense if dense is not None else ew.dense()
     g = dequant_linear(a, w1)
     u = dequant_linear(a, w3)
@@ -432,6 +434,9 @@ def expert_forward_dequant(a: np.ndarray, ew: ExpertWeights, route_w: np.ndarray
     h = (silu(g) * u).astype(np.float32)
     if route_w is not None:
         h = (h * np.asarray(route_w, np.float32).reshape(-1, 1)).astype(np.float32)
+    if fp4_h:
+        q, s = fp4_act_quant(round_bf16(h))
+        return dequant_linear(fp4_act_dequant(q, s), w2)
     return quantized_linear(round_bf16(h), w2)
 
 

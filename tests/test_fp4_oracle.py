@@ -1,7 +1,7 @@
 """The oracle's restatement of the official fp4_act_quant(x, 32) (CPU):
 e2m1 rounding to nearest even with saturation, the per-32 power-of-two scale,
-nibble packing, and the FP4-activation expert against a dense float64
-reference of the same quantized operands."""
+nibble packing, and the FP4-activation expert (x and h quantized per 32)
+against a dense float64 reference of the same quantized operands."""
 
 import numpy as np
 
@@ -47,7 +47,7 @@ def test_fp4_activation_expert_against_dense_reference():
     w1, w2, w3 = (g.standard_normal(s).astype(np.float32) * 0.05 for s in ((I, H), (H, I), (I, H)))
     q, s = O.fp4_act_quant(x)
     a = O.fp4_act_dequant(q, s)
-    ref = O.expert_forward_dequant(a, None, None, 0.0, dense=(w1, w2, w3))
+    ref = O.expert_forward_dequant(a, None, None, 0.0, dense=(w1, w2, w3), fp4_h=True)
     got = O.expert_forward(x, None, None, 0.0, dense=(w1, w2, w3), fp4_act=True)
     assert np.array_equal(got, ref)
     assert not np.array_equal(got, O.expert_forward(x, None, None, 0.0, dense=(w1, w2, w3)))

@@ -2,9 +2,9 @@
 
 * dsv4_fp4_act_quant is bit-exact against the oracle's restatement of the
   official fp4_act_quant(x, 32) (codes and scale bytes), edge cases included.
-* With dsv4_set_fp4_activations(1) the layer's routed GEMM1 runs as kind::mxf4
-  products on FP4 activations; the output matches the oracle run in the same
-  mode (FP4 activations for the routed experts' w1 / w3, e4m3 elsewhere) within
+* With dsv4_set_fp4_activations(1) the routed experts' GEMMs run as kind::mxf4
+  products on FP4 activations (x before w1 / w3, h before w2); the output
+  matches the oracle run in the same mode (the shared expert on e4m3) within
   the layer bar, at every tile size (32 / 64 / 128 rows).  How far the mode
   moves the layer from the reference's e4m3 arithmetic is reported beside it.
 """
