@@ -827,8 +827,7 @@ int dsv4_moe_forward(const dsv4_moe_layer* L, const void* x, int T, void* y,
   }
   uint8_t* xq4 = p.fp4 ? ws + p.off[21] : nullptr;
   uint8_t* xsf4 = p.fp4 ? ws + p.off[22] : nullptr;
-  if (p.fp4 && (rc = launch_fp4_permute_quant(x, T, H, slot_token, seg_start + (E + p.S), p.max_rows, xq4,
-                                              xsf4, nsm, st)))
+  if (p.fp4 && (rc = launch_fp4_scatter_quant(x, T, H, k, route_slot, p.max_rows, xq4, xsf4, nsm, st)))
     return rc;
   stage_mark(3, st);
 

@@ -80,8 +80,8 @@ int launch_route_small_fused(const float* partials, int nsplit, float* logits_ou
                              int* ctrl, int* zero_ptr, int n_zero, int* route_slot, uint8_t* xq, uint8_t* sfb,
                              cudaStream_t st);
 int launch_fp4_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* s, int num_sms, cudaStream_t st);
-int launch_fp4_permute_quant(const void* x, int T, int H, const int* slot_token, const int* total_rows_ptr,
-                             int max_rows, uint8_t* xq4, uint8_t* atoms, int num_sms, cudaStream_t st);
+int launch_fp4_scatter_quant(const void* x, int T, int H, int k, const int* route_slot, int max_rows, uint8_t* xq4,
+                             uint8_t* atoms, int num_sms, cudaStream_t st);
 // expert parallelism (ep.cu)
 long long ep_row_bytes(int H, int k);
 long long ep_dispatch_workspace(int T, int world);

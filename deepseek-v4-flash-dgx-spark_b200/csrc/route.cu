@@ -567,11 +567,15 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const __nv_bfloat16* __r
 // FP4 activations (fp4_block_quant): one thread per 32-value block.
 // fp4_act_quant_kernel: plain rows -> packed codes [M][K/2] + scale bytes
 // [M][K/32] (the official fp4_act_quant's outputs).
-// fp4_permute_quant_kernel: plan slot rows (token slot_token[row], -1 = a
-// padding row: zero codes) -> packed codes [rows][H/2] and per-32 scale atoms
-// for the tensor core: atom (g, w) holds rows 32g .. 32g+127 for the 128-wide
-// k window w, row r / block b of the window at byte (r%32)*16 + ((r/32)-g)*4 + b
-// (each row written to its four overlapping atoms, as the per-128 atoms are).
+// fp4_scatter_quant_kernel: the layer's routed rows -> packed codes
+// [rows][H/2] and per-32 scale atoms for the tensor core: atom (g, w) holds
+// rows 32g .. 32g+127 for the 128-wide k window w, row r / block b of the
+// window at byte (r%32)*16 + ((r/32)-g)*4 + b (each row written to its four
+// overlapping atoms, as the per-128 atoms are).  Each token's block is
+// quantized once and written to the token's routed slots (route_slot [T][k],
+// -1 = skipped); the shared expert's rows keep e4m3 and get none.  Padding
+// rows are left unwritten: a row of A reaches only its own accumulator lane,
+// and the epilogue never stores those lanes.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) fp4_act_quant_kernel(const __nv_bfloat16* __restrict__ x, int M, int K,
                                                             uint8_t* __restrict__ q, uint8_t* __restrict__ s) {
@@ -588,33 +592,30 @@ __global__ void __launch_bounds__(256) fp4_act_quant_kernel(const __nv_bfloat16*
   }
 }
 
-__global__ void __launch_bounds__(256) fp4_permute_quant_kernel(
-    const __nv_bfloat16* __restrict__ x, int T, int H, const int* __restrict__ slot_token,
-    const int* __restrict__ total_rows_ptr, int max_rows, uint8_t* __restrict__ xq4,
-    uint8_t* __restrict__ atoms) {
+__global__ void __launch_bounds__(256) fp4_scatter_quant_kernel(
+    const __nv_bfloat16* __restrict__ x, int T, int H, int k, const int* __restrict__ route_slot, int max_rows,
+    uint8_t* __restrict__ xq4, uint8_t* __restrict__ atoms) {
   const int nb = H / 32, KW = H / 128;
-  const int total = min(*total_rows_ptr, max_rows);
-  const long long n = (long long)total * nb;
+  const long long n = (long long)T * nb;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const int row = (int)(i / nb), b = (int)(i % nb);
-    const int t = slot_token[row];
+    const int t = (int)(i / nb), b = (int)(i % nb);
     float v[32];
-    if (t >= 0 && t < T) {  // anything else (padding, a failed plan's leftovers) quantizes zeros
-      load_bf16x32(x + (size_t)t * H + 32 * b, v);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = 0.f;
-    }
+    load_bf16x32(x + (size_t)t * H + 32 * b, v);
     uint4 packed;
-    const int e = fp4_block_quant(v, packed);
-    *reinterpret_cast<uint4*>(xq4 + (size_t)row * (H / 2) + 16 * b) = packed;
-    const int w = b >> 2, g = row >> 5;
+    const uint8_t sbyte = static_cast<uint8_t>(fp4_block_quant(v, packed) + 127);
+    const int w = b >> 2;
+    for (int j = 0; j < k; ++j) {
+      const int row = route_slot[(size_t)t * k + j];
+      if (row < 0 || row >= max_rows) continue;
+      *reinterpret_cast<uint4*>(xq4 + (size_t)row * (H / 2) + 16 * b) = packed;
+      const int g = row >> 5;
 #pragma unroll
-    for (int m1 = 0; m1 < 4; ++m1)
-      if (g - m1 >= 0)
-        atoms[((size_t)(g - m1) * KW + w) * 512 + (row & 31) * 16 + m1 * 4 + (b & 3)] = static_cast<uint8_t>(e + 127);
+      for (int m1 = 0; m1 < 4; ++m1)
+        if (g - m1 >= 0) atoms[((size_t)(g - m1) * KW + w) * 512 + (row & 31) * 16 + m1 * 4 + (b & 3)] = sbyte;
+    }
   }
 }
+
 
 // ---------------------------------------------------------------------------
 // Combine: y[t] = bf16( sum over t's routes in ascending expert id of O[slot]
@@ -820,16 +821,17 @@ int launch_fp4_act_quant(const void* x, int M, int K, uint8_t* q, uint8_t* s, in
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
 
-int launch_fp4_permute_quant(const void* x, int T, int H, const int* slot_token, const int* total_rows_ptr,
-                             int max_rows, uint8_t* xq4, uint8_t* atoms, int num_sms, cudaStream_t st) {
-  const long long n = (long long)max_rows * (H / 32);
+int launch_fp4_scatter_quant(const void* x, int T, int H, int k, const int* route_slot, int max_rows, uint8_t* xq4,
+                             uint8_t* atoms, int num_sms, cudaStream_t st) {
+  const long long n = (long long)T * (H / 32);
   if (n <= 0) return DSV4_OK;
   long long grid = (n + 255) / 256;
   if (grid > 8LL * num_sms) grid = 8LL * num_sms;
-  launch_k(fp4_permute_quant_kernel, (unsigned)grid, 256, 0, st, static_cast<const __nv_bfloat16*>(x), T, H,
-           slot_token, total_rows_ptr, max_rows, xq4, atoms);
+  launch_k(fp4_scatter_quant_kernel, (unsigned)grid, 256, 0, st, static_cast<const __nv_bfloat16*>(x), T, H, k,
+           route_slot, max_rows, xq4, atoms);
   return cudaGetLastError() == cudaSuccess ? DSV4_OK : DSV4_ERR_CUDA;
 }
+
 
 int launch_combine(const void* O, int H, const int* route_slot, const int64_t* indices, int T,
                    int k, const int* shared_base, void* y, cudaStream_t st, const void* O_shared) {
