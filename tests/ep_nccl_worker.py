@@ -33,8 +33,11 @@ def main() -> int:
         if os.environ.get("EP_MODE", "nccl") == "peer":
             ep.enable_peer_exchange(64)
         ok = True
-        for step in range(2):  # the second call reuses the exchange buffers
-            n = ((64, 37), (5, 64))[step][rank % 2]
+        # the second call reuses the exchange buffers; over peer memory
+        # MoE.forward captures a graph per token count, and the third call
+        # replays the graphs of the first (the ranks' counts differ)
+        for step in range(3):
+            n = ((64, 37), (5, 64), (64, 37))[step][rank % 2]
             g = torch.Generator().manual_seed(1000 + 10 * step + rank)
             x = torch.randn(1, n, cfg.dim, generator=g).to(torch.bfloat16).to(dev)
             y = ep(x)
