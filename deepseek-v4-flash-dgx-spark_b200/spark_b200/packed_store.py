@@ -29,6 +29,7 @@ import json
 import os
 import threading
 import time
+from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass
 from pathlib import Path
 from typing import Any
@@ -136,6 +137,9 @@ class _Staging:
         return buf[:size]
 
 
+_READ_PIECE = 4 << 20  # bytes per pread piece of a block
+
+
 class PackedExpertStore:
     def __init__(self, layout_path: Path):
         self.layout_path = Path(layout_path)
@@ -155,6 +159,11 @@ class PackedExpertStore:
         self._fd_of_file: list[int | None] = [None] * len(self.index.files)
         self._plans: dict[tuple[int, tuple[str, ...]], NativeExpertCopyPlan] = {}
         self._upload: dict[tuple[str, int], dict[str, Any]] = {}  # per device: pinned + device rings
+        # blocks are pread in pieces of at most _READ_PIECE bytes by this many
+        # threads at once (each piece is one native call that releases the
+        # GIL); DSV4_READ_THREADS overrides
+        self.read_threads = max(1, int(os.environ.get("DSV4_READ_THREADS", min(8, os.cpu_count() or 1))))
+        self._read_pool: ThreadPoolExecutor | None = None
 
     @classmethod
     def from_env(cls) -> "PackedExpertStore | None":
@@ -162,6 +171,9 @@ class PackedExpertStore:
         return cls(Path(path)) if path else None
 
     def close(self) -> None:
+        if self._read_pool is not None:
+            self._read_pool.shutdown(wait=True)
+            self._read_pool = None
         with self._fd_lock:
             for i, fd in enumerate(self._fd_of_file):
                 if fd is not None:
@@ -250,17 +262,29 @@ class PackedExpertStore:
 
     # --------------------------------------------------------- B200 bulk path
     def _pread_rows(self, rows: np.ndarray, dst: torch.Tensor, dst_off: np.ndarray) -> int:
-        """pread the blocks of index ``rows`` into ``dst`` at ``dst_off``; raises
-        on a short read.  Returns the bytes read."""
-        total = 0
+        """pread the blocks of index ``rows`` into ``dst`` at ``dst_off`` in
+        pieces of at most _READ_PIECE bytes, up to ``read_threads`` pieces at
+        once (positional reads of distinct ranges into distinct destinations);
+        raises on a short read.  Returns the bytes read."""
+        jobs = []
         for r, o in zip(rows.tolist(), dst_off.tolist()):
-            size = int(self.index.nbytes[r])
-            fd = self._descriptor(int(self.index.file_id[r]))
-            got = self._native_module.read_into(fd, dst[o:o + size], size, int(self.index.offset[r]))
+            size, fd, offset = int(self.index.nbytes[r]), self._descriptor(int(self.index.file_id[r])), int(
+                self.index.offset[r])
+            for p0 in range(0, size, _READ_PIECE):
+                jobs.append((min(_READ_PIECE, size - p0), fd, offset + p0, int(o) + p0))
+
+        def one(job) -> int:
+            size, fd, offset, o = job
+            got = self._native_module.read_into(fd, dst[o:o + size], size, offset)
             if got != size:
                 raise RuntimeError("short packed expert read")
-            total += size
-        return total
+            return size
+
+        if len(jobs) > 1 and self.read_threads > 1:
+            if self._read_pool is None:
+                self._read_pool = ThreadPoolExecutor(max_workers=self.read_threads)
+            return sum(self._read_pool.map(one, jobs))
+        return sum(one(j) for j in jobs)
 
     def read_blocks(self, layer_id: int, experts: list[int]) -> tuple[torch.Tensor, list[int], float]:
         """All blocks of ``experts`` in one (pinned when CUDA is present) host

@@ -100,6 +100,38 @@ def test_loader_mirror_materializes_reference_bytes(layer):
         store.close()
 
 
+def test_threaded_block_reads_give_the_same_bytes(layer):
+    """read_blocks preads up to read_threads blocks at once; the buffer equals
+    a one-thread read byte for byte, and a short read still raises."""
+    from spark_b200.packed_store import PackedExpertStore, write_packed_layout
+
+    cfg = layer["cfg"]
+    with tempfile.TemporaryDirectory() as tmp:
+        write_packed_layout(Path(tmp), {3: {e: layer["blocks"][e].numpy() for e in range(cfg.n_routed)}},
+                            cfg.dim, cfg.inter)
+        experts = list(range(cfg.n_routed))[::-1]
+        bufs = []
+        for threads in (1, 4):
+            store = PackedExpertStore(Path(tmp) / "layout.json")
+            store.read_threads = threads
+            buf, offs, _ = store.read_blocks(3, experts)
+            bufs.append((buf.clone(), offs))
+            store.close()
+        assert bufs[0][1] == bufs[1][1] and torch.equal(bufs[0][0], bufs[1][0])
+        for e, o in zip(experts, bufs[1][1]):
+            blk = layer["blocks"][e].numpy().reshape(-1)
+            assert np.array_equal(bufs[1][0][o:o + blk.size].numpy(), blk)
+        # truncate the slab: the threaded read reports the short read
+        slab = next(Path(tmp).glob("*.bin"))
+        with open(slab, "r+b") as f:
+            f.truncate(slab.stat().st_size // 2)
+        store = PackedExpertStore(Path(tmp) / "layout.json")
+        store.read_threads = 4
+        with pytest.raises(RuntimeError, match="short packed expert read"):
+            store.read_blocks(3, experts)
+        store.close()
+
+
 def test_loader_mirror_error_messages():
     from spark_b200 import native_packed_loader as npl
 
