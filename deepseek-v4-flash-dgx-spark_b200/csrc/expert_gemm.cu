@@ -380,6 +380,7 @@ __global__ void __launch_bounds__(192, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* epi_abort = abort_flag + 1;
   volatile int* split_last = epi_abort + 1;  // this CTA finished the item's last slice
+  volatile int* epi_dry = split_last + 1;    // [4] per epilogue warp: its next pass is the dry one
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -392,6 +393,7 @@ __global__ void __launch_bounds__(192, 1)
     mbar_init(final_bar, 1);
     *abort_flag = 0;
     *epi_abort = 0;
+    for (int i = 0; i < 4; ++i) epi_dry[i] = 1;
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -399,7 +401,12 @@ __global__ void __launch_bounds__(192, 1)
     tmem_relinquish();
   }
   if (warp == 0 && lane == 0) {
+    // every map a first k tile may need: its descriptor fetch is otherwise
+    // in series with that tile's loads
     tma_prefetch_desc(&tmW0);
+    tma_prefetch_desc(&tmW1);
+    tma_prefetch_desc(&tmS0);
+    tma_prefetch_desc(&tmS1);
     tma_prefetch_desc(&tmX);
   }
   tc_fence_before();
@@ -425,7 +432,9 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t aphase = 0;
+      // acc_empty's first phase is the epilogue's dry pass (below), so the
+      // first item waits for it to have read TMEM
+      uint32_t aphase = 1;
       int sf_slot = 1;  // follows the producer's ring slot
       uint32_t sf_set = 0;  // FP4A: TMEM scale column set of the next k tile
       const uint32_t sfa_t = tmem + C::SFA_COL;
@@ -530,15 +539,38 @@ __global__ void __launch_bounds__(192, 1)
     uint32_t aphase = 0;
     const float lim = args.swiglu_limit;
     const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
-    for (int w = blockIdx.x; w < total; w += step) {
-      const int item = w / S;
+    // The first pass is dry: the CTA's first item again, on whatever TMEM
+    // holds before any MMA, without waiting for the accumulator.  It runs the
+    // epilogue's instructions once while that item's MMAs are still
+    // microseconds off, so that the real passes do not fetch them cold (the
+    // unrolled GEMM1 arithmetic is thousands of instructions, and a decode
+    // CTA's only item otherwise waits on those fetches).  Its release of the
+    // accumulator is the first phase the MMA warp waits for, so no MMA writes
+    // TMEM before the dry pass has read it.  Its stores go to the rows and
+    // scale bytes that the same threads store again, later in program order,
+    // in the item's real pass; nothing reads them before the kernel ends.  The
+    // flag is read from shared memory so that the dry pass stays the same
+    // code as the real ones.
+    for (int w = (int)blockIdx.x - step; w < total; w += step) {
+      const bool dry = epi_dry[q] != 0;
+      __syncwarp();
+      if (dry && lane == 0) epi_dry[q] = 0;
+      const int wi = dry ? w + step : w;
+      if (wi >= total) continue;  // dry pass of a CTA without items
+      const int item = wi / S;
       const int4 tl = args.tiles[item / NB];
-      if (filtered_out(args, tl.x >= args.n_routed)) continue;
+      if (filtered_out(args, tl.x >= args.n_routed)) {
+        if (dry) {  // the MMA warp still counts the dry pass's release
+          tc_fence_before();
+          mbar_arrive(acc_empty);
+        }
+        continue;
+      }
       const int jb = item % NB;
       const int row0 = tl.y, nrows = tl.z;
       // epi_abort is written only by epilogue warps and read between two
       // barriers, so all four see the same value.
-      if (!mbar_wait(acc_full, aphase, DSV4_DEVERR_TIMEOUT_EPILOGUE)) {
+      if (!dry && !mbar_wait(acc_full, aphase, DSV4_DEVERR_TIMEOUT_EPILOGUE)) {
         *epi_abort = 1;
         *abort_flag = 1;
       }
@@ -546,12 +578,17 @@ __global__ void __launch_bounds__(192, 1)
       const bool stop = *epi_abort != 0;
       epi_bar();
       if (stop) break;
-      aphase ^= 1;
+      if (!dry) aphase ^= 1;
       tc_fence_after();
       const bool warp_rows = q * 32 < nrows;  // TMEM lanes of this quarter hold real rows
       if (S > 1) {
-        split_epilogue<GATED>(args, taddr, warp_rows, r, q, lane, item, w % S, tl, jb, acc_empty,
-                              split_last);
+        if (dry) {
+          tc_fence_before();
+          mbar_arrive(acc_empty);
+        } else {
+          split_epilogue<GATED>(args, taddr, warp_rows, r, q, lane, item, wi % S, tl, jb, acc_empty,
+                                split_last);
+        }
         continue;
       }
       uint32_t pk[128];                       // packed bf16 pairs out of TMEM
