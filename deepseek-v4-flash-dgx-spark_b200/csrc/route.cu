@@ -53,10 +53,15 @@ __global__ void __launch_bounds__(256) route_count_kernel(const int64_t* __restr
 }
 
 // Segment layout of one CTA from the per-segment counts s_cnt[0..NS) (shared
-// memory): padded segment starts and tile bases by a warp-0 scan, then the
-// tile list, the padding rows and the published counts.  A failed plan (an
-// invalid index seen earlier, or more rows / tiles than the workspace holds)
-// records a device error, sets ctrl[2] and emits no tiles.
+// memory): padded segment starts, tile bases and valid-row bases by a
+// block-wide scan (each thread sums a contiguous run of segments, warps scan
+// the thread sums with shuffles, warp 0 scans the warp totals), then the tile
+// list, the padding rows and the published counts.  A thread writes the tiles
+// of its own run (it holds the run's valid-row base in a register, so no
+// per-segment array beyond s_start and s_tbase is needed); a warp writes a
+// segment's padding rows.  A failed plan (an invalid index seen earlier, or more
+// rows / tiles than the workspace holds) records a device error, sets ctrl[2]
+// and emits no tiles.
 __device__ void plan_layout(int* s_cnt, int* s_start, int* s_tbase, int NS, int block_n,
                             int max_rows, int max_tiles, int bad, int* __restrict__ counts,
                             int* __restrict__ seg_start, int4* __restrict__ tiles,
@@ -64,39 +69,77 @@ __device__ void plan_layout(int* s_cnt, int* s_start, int* s_tbase, int NS, int 
                             float* __restrict__ slot_weight, int* __restrict__ ctrl,
                             int* __restrict__ zero_ptr, int n_zero) {
   __shared__ int s_fail;
+  __shared__ int s_wsum[3][32];  // per warp: padded rows, tiles, valid rows (then their exclusive scan)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
+  const int nwarps = (nthr + 31) >> 5;
+  __syncthreads();
+  const int per = (NS + nthr - 1) / nthr;
+  const int s_lo = min(tid * per, NS), s_hi = min(s_lo + per, NS);
+  int r_own = 0, t_own = 0, v_own = 0;
+  for (int s = s_lo; s < s_hi; ++s) {
+    const int c = s_cnt[s];
+    r_own += (c + kSegAlign - 1) / kSegAlign * kSegAlign;
+    t_own += (c + block_n - 1) / block_n;
+    v_own += c;
+  }
+  int r_inc = r_own, t_inc = t_own, v_inc = v_own;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int a = __shfl_up_sync(0xffffffffu, r_inc, o);
+    const int b = __shfl_up_sync(0xffffffffu, t_inc, o);
+    const int d = __shfl_up_sync(0xffffffffu, v_inc, o);
+    if (lane >= o) {
+      r_inc += a;
+      t_inc += b;
+      v_inc += d;
+    }
+  }
+  if (lane == 31) {
+    s_wsum[0][warp] = r_inc;
+    s_wsum[1][warp] = t_inc;
+    s_wsum[2][warp] = v_inc;
+  }
   __syncthreads();
   if (warp == 0) {
-    int row_run = 0, tile_run = 0;
-    for (int s0 = 0; s0 < NS; s0 += 32) {
-      const int s = s0 + lane;
-      const int c = s < NS ? s_cnt[s] : 0;
-      const int rows = (c + kSegAlign - 1) / kSegAlign * kSegAlign;
-      const int nt = (c + block_n - 1) / block_n;
-      int r_inc = rows, t_inc = nt;
+    const int r0 = lane < nwarps ? s_wsum[0][lane] : 0;
+    const int t0 = lane < nwarps ? s_wsum[1][lane] : 0;
+    const int v0 = lane < nwarps ? s_wsum[2][lane] : 0;
+    int r = r0, t = t0, v = v0;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int a = __shfl_up_sync(0xffffffffu, r_inc, o);
-        const int b = __shfl_up_sync(0xffffffffu, t_inc, o);
-        if (lane >= o) {
-          r_inc += a;
-          t_inc += b;
-        }
+    for (int o = 1; o < 32; o <<= 1) {
+      const int a = __shfl_up_sync(0xffffffffu, r, o);
+      const int b = __shfl_up_sync(0xffffffffu, t, o);
+      const int d = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) {
+        r += a;
+        t += b;
+        v += d;
       }
-      if (s < NS) {
-        s_start[s] = row_run + r_inc - rows;
-        s_tbase[s] = tile_run + t_inc - nt;
-      }
-      row_run += __shfl_sync(0xffffffffu, r_inc, 31);
-      tile_run += __shfl_sync(0xffffffffu, t_inc, 31);
     }
-    if (lane == 0) {
-      s_start[NS] = row_run;
-      s_tbase[NS] = tile_run;
-      s_fail = bad || row_run > max_rows || tile_run > max_tiles;
+    if (lane < nwarps) {
+      s_wsum[0][lane] = r - r0;
+      s_wsum[1][lane] = t - t0;
+      s_wsum[2][lane] = v - v0;
+    }
+    if (lane == 31) {
+      s_start[NS] = r;
+      s_tbase[NS] = t;
+      s_fail = bad || r > max_rows || t > max_tiles;
       if (s_fail) record_error(bad ? DSV4_DEVERR_BAD_INDEX : DSV4_DEVERR_PLAN_OVERFLOW);
       ctrl[2] = s_fail;
     }
+  }
+  __syncthreads();
+  // exclusive bases of this thread's first segment
+  int r_run = s_wsum[0][warp] + r_inc - r_own;
+  int t_run = s_wsum[1][warp] + t_inc - t_own;
+  const int v_base = s_wsum[2][warp] + v_inc - v_own;
+  for (int s = s_lo; s < s_hi; ++s) {
+    const int c = s_cnt[s];
+    s_start[s] = r_run;
+    s_tbase[s] = t_run;
+    r_run += (c + kSegAlign - 1) / kSegAlign * kSegAlign;
+    t_run += (c + block_n - 1) / block_n;
   }
   __syncthreads();
   if (s_fail) {
@@ -109,22 +152,21 @@ __device__ void plan_layout(int* s_cnt, int* s_start, int* s_tbase, int NS, int 
   }
   // split-K item counters of the GEMMs start at zero on every call
   for (int i = tid; i < n_zero; i += nthr) zero_ptr[i] = 0;
-  for (int s = warp; s < NS; s += nthr / 32) {
-    const int c = s_cnt[s], base = s_start[s], nt = s_tbase[s + 1] - s_tbase[s];
-    // compact row of the segment's first route: valid rows of earlier segments
-    int vb = 0;
-    for (int j = lane; j < s; j += 32) vb += s_cnt[j];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) vb += __shfl_xor_sync(0xffffffffu, vb, o);
-    // tile = {segment, first plan row, valid rows, compact index of the first row}
-    for (int m = lane; m < nt; m += 32)
-      tiles[s_tbase[s] + m] =
-          make_int4(s, base + m * block_n, min(block_n, c - m * block_n), vb + m * block_n);
-    for (int r = base + c + lane; r < s_start[s + 1]; r += 32) {
+  // tile = {segment, first plan row, valid rows, compact index of the first row};
+  // the compact index counts the valid rows of earlier segments
+  int vb = v_base;
+  for (int s = s_lo; s < s_hi; ++s) {
+    const int c = s_cnt[s], base = s_start[s], tb = s_tbase[s], nt = s_tbase[s + 1] - tb;
+    for (int m = 0; m < nt; ++m)
+      tiles[tb + m] = make_int4(s, base + m * block_n, min(block_n, c - m * block_n), vb + m * block_n);
+    vb += c;
+  }
+  // padding rows: one warp per segment, consecutive lanes on consecutive rows
+  for (int s = warp; s < NS; s += nwarps)
+    for (int r = s_start[s] + s_cnt[s] + lane; r < s_start[s + 1]; r += 32) {
       slot_token[r] = -1;
       slot_weight[r] = 0.f;
     }
-  }
   if (tid == 0) *n_tiles = s_tbase[NS];
 }
 
